@@ -1,0 +1,177 @@
+/*
+ * minikv -- C ABI of the B200 (sm_100a) paged-KV-cache hot path.
+ *
+ * Drop-in native layer for the reference engine's operator API in
+ * mini_engine/kernels (paths below are inside the reference project).  Every
+ * entry point takes raw device pointers, element counts and a cudaStream_t
+ * passed as void*; nothing here knows about torch.  All launches go on the
+ * given stream, never synchronise (except minikv_device_status) and allocate
+ * nothing, so they can be captured in a CUDA graph.
+ *
+ * Layouts (row-major, contiguous unless a stride argument says otherwise):
+ *   key/value cache : [num_blocks, block_size, kv_heads, head_dim]  -- one layer
+ *                     of the pool [layers, num_blocks, block_size, kv_heads, head_dim]
+ *                     (mini_engine/cache/kv_cache.py:50-52)
+ *   query / out     : [batch, q_heads, head_dim]        (decode)
+ *                     [tokens, q_heads, head_dim]       (prefill)
+ *   block_tables    : [rows, table_width] int64, -1 padded
+ * dtype codes: MINIKV_F32, MINIKV_F16, MINIKV_BF16 (all tensors of a call share it).
+ * head_dim must be one of 16, 32, 64, 80, 96, 128, 192, 256.
+ *
+ * Return value: MINIKV_OK or an error code; minikv_last_error() then holds a
+ * message (thread-local).  Pointers must be 16-byte aligned.
+ */
+#ifndef MINIKV_H
+#define MINIKV_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MINIKV_ABI_VERSION 1
+
+enum { MINIKV_F32 = 0, MINIKV_F16 = 1, MINIKV_BF16 = 2 };
+enum { MINIKV_OK = 0, MINIKV_EINVAL = 1, MINIKV_ECUDA = 2, MINIKV_EUNSUPPORTED = 3 };
+/* bits of the device status word (minikv_device_status) */
+enum { MINIKV_STATUS_WAIT_TIMEOUT = 1 };
+
+int minikv_abi_version(void);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* minikv_last_error(void);
+
+/* Synchronise `stream`, then read (and if clear != 0 reset) the device status
+ * word of the current device: kernels set bits there instead of trapping when
+ * a bounded wait gives up.  New; the reference has no device status. */
+int minikv_device_status(unsigned int* status, int clear, void* stream);
+
+/* ---------------------------------------------------------------- decode ---
+ * Split-KV decode attention over paged K/V (GQA: q head h reads kv head
+ * h / (q_heads / kv_heads)).  out[b, h] = softmax(q[b,h] . K^T / sqrt(D)) V over
+ * the first context_lens[b] tokens of request b's pages.
+ * Replaces paged_attention_cuda (mini_engine/kernels/csrc/paged_attention.cu:266-280)
+ * behind paged_attention (mini_engine/kernels/paged.py:8-22,
+ * mini_engine/kernels/csrc/bindings.cpp:152-184).
+ * Trusted-mode guards as in the reference kernel: a page id outside
+ * [0, num_blocks) masks its tokens, a length outside [1, table_width*block_size]
+ * or a fully masked row gives an all-zero output row.
+ * The number of KV splits depends only on (batch, table_width, block_size,
+ * heads, head_dim, dtype) and the device, never on context_lens, so a
+ * captured graph stays valid when lengths change.
+ * workspace: device scratch of at least minikv_paged_decode_workspace_bytes(). */
+int64_t minikv_paged_decode_workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                            int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                            int64_t table_width, int dtype);
+int minikv_paged_decode(const void* query, const void* key_cache, const void* value_cache,
+                        const int64_t* block_tables, const int64_t* context_lens, void* out,
+                        void* workspace, int64_t workspace_bytes,
+                        int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                        int64_t num_blocks, int64_t block_size, int64_t table_width,
+                        int dtype, void* stream);
+
+/* ------------------------------------------------------------- KV writes ---
+ * Bit-exact row copies with 16-byte vector loads/stores.  A source row is the
+ * [kv_heads, head_dim] block of one token; consecutive source tokens are
+ * `*_token_stride` elements apart (>= kv_heads*head_dim).
+ *
+ * Scatter rows[slot_mapping[t]] = key[t] (and value), rows = cache viewed as
+ * [num_blocks*block_size, kv_heads, head_dim].  Slots outside the capacity are
+ * skipped.  Replaces write_kv_cache_slots_cuda
+ * (mini_engine/kernels/csrc/data.cu:209-250; data.py:84-130). */
+int minikv_kv_scatter_slots(void* key_cache, void* value_cache, const int64_t* slot_mapping,
+                            const void* key, const void* value, int64_t tokens,
+                            int64_t num_blocks, int64_t block_size, int64_t kv_heads, int64_t head_dim,
+                            int64_t key_token_stride, int64_t value_token_stride,
+                            int dtype, void* stream);
+
+/* Decode append: request r writes its token at logical position
+ * token_offsets[r] through block_tables[r]; rows whose page index or physical
+ * page is out of range are skipped.  Replaces write_kv_cache_batch_cuda
+ * (mini_engine/kernels/csrc/data.cu:175-192; data.py:67-81). */
+int minikv_kv_append_batch(void* key_cache, void* value_cache, const int64_t* block_tables,
+                           const int64_t* token_offsets, const void* key, const void* value,
+                           int64_t batch, int64_t table_width, int64_t num_blocks, int64_t block_size,
+                           int64_t kv_heads, int64_t head_dim,
+                           int64_t key_token_stride, int64_t value_token_stride,
+                           int dtype, void* stream);
+
+/* Contiguous token range [token_offset, token_offset+tokens) through one list
+ * of block ids.  Replaces write_kv_cache_cuda
+ * (mini_engine/kernels/csrc/data.cu:165-173; data.py:39-64; kv_cache.py:123-145). */
+int minikv_kv_write_range(void* key_cache, void* value_cache, const int64_t* block_ids, int64_t num_ids,
+                          int64_t token_offset, const void* key, const void* value, int64_t tokens,
+                          int64_t num_blocks, int64_t block_size, int64_t kv_heads, int64_t head_dim,
+                          int64_t key_token_stride, int64_t value_token_stride,
+                          int dtype, void* stream);
+
+/* Copy-on-write: for every (src, dst) pair in `pairs` ([num_pairs, 2] int64,
+ * device memory) copy page src to page dst in every layer of both pools
+ * ([num_layers, num_blocks, block_elems] with block_elems =
+ * block_size*kv_heads*head_dim).  Pairs must have distinct dst pages and no
+ * dst may be another pair's src.  The reference has no copy-on-write; this is
+ * the kernel behind the new BlockManager fork (block_manager.py:99-116 keeps
+ * the refcounts it relies on). */
+int minikv_copy_blocks(void* key_pool, void* value_pool, const int64_t* pairs, int64_t num_pairs,
+                       int64_t num_layers, int64_t num_blocks, int64_t block_elems,
+                       int dtype, void* stream);
+
+/* --------------------------------------------------------------- prefill ---
+ * Ragged causal prefill over paged K/V: packed query token t of request r
+ * (cu_seqlens_q[r] <= t < cu_seqlens_q[r+1]) sits at position
+ * p = query_starts[r] + t - cu_seqlens_q[r] and attends keys [0, p] of r's
+ * pages (history and the current chunk, already scattered).
+ * Replaces paged_prefill_attention_cuda (mini_engine/kernels/csrc/prefill.cu:200-240;
+ * prefill.py:61-131).  bf16/fp16 with head_dim 64 or 128 and a GQA group that
+ * divides 128 run on tcgen05 tensor cores (TMEM accumulators, TMA-fed tiles);
+ * other shapes run a CUDA-core route.  max_query_len bounds every request's
+ * query count (it sizes the grid).  Tokens whose metadata is out of range get
+ * zero rows.  workspace: at least minikv_paged_prefill_workspace_bytes(). */
+int64_t minikv_paged_prefill_workspace_bytes(int64_t tokens, int64_t requests, int64_t q_heads,
+                                             int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
+                                             int64_t block_size, int64_t table_width,
+                                             int64_t max_query_len, int dtype);
+int minikv_paged_prefill(const void* q, const void* key_cache, const void* value_cache,
+                         const int64_t* cu_seqlens_q, const int64_t* query_starts,
+                         const int64_t* block_tables, const int64_t* context_lens, void* out,
+                         void* workspace, int64_t workspace_bytes,
+                         int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
+                         int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                         int64_t table_width, int64_t max_query_len, int dtype, void* stream);
+
+/* -------------------------------------------------------------- metadata ---
+ * Device-side construction of the ragged prefill batch metadata of
+ * PrefillBatch.from_sequences (mini_engine/engine/batch.py:67-137) from compact
+ * per-request inputs: query_starts[B], cu_seqlens_q[B+1], cu_blocks[B+1] and
+ * the concatenated block ids of every request.  Outputs (int64, device):
+ * input_ids[T] (copied from token_ids), positions[T], slot_mapping[T],
+ * out_cu_seqlens_q[B+1], out_query_starts[B], context_lens[B],
+ * block_tables[B, table_width] (-1 padded).  Host code validates first
+ * (shared-page writes, duplicates, ranges); the kernel itself only guards
+ * its own indices. */
+int minikv_build_prefill_metadata(const int64_t* query_starts, const int64_t* cu_seqlens_q,
+                                  const int64_t* cu_blocks, const int64_t* block_ids,
+                                  const int64_t* token_ids, int64_t requests, int64_t tokens,
+                                  int64_t table_width, int64_t block_size,
+                                  int64_t* input_ids, int64_t* positions, int64_t* slot_mapping,
+                                  int64_t* out_cu_seqlens_q, int64_t* out_query_starts,
+                                  int64_t* context_lens, int64_t* block_tables, void* stream);
+
+/* Fixed-shape decode metadata of a CUDA-graph bucket (the staging of
+ * mini_engine/engine/cuda_graph.py:149-181 with the padding rows of :66-86):
+ * rows r < *active take tokens[r], positions[r] and the block ids
+ * block_ids[cu_blocks[r] : cu_blocks[r+1]]; the other rows get token 0,
+ * position 0 and padding_pages[r] in column 0; all other columns are -1.
+ * `active` is read on the device, so the launch can sit inside a graph. */
+int minikv_build_decode_tables(const int64_t* active, const int64_t* tokens, const int64_t* positions,
+                               const int64_t* cu_blocks, const int64_t* block_ids,
+                               const int64_t* padding_pages, int64_t batch_size, int64_t max_blocks,
+                               int64_t* input_ids, int64_t* out_positions, int64_t* block_tables,
+                               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MINIKV_H */

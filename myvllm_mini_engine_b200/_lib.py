@@ -1,0 +1,97 @@
+"""ctypes binding of libminikv (the C ABI declared in include/minikv.h).
+
+The shared library is built in-tree (``python -m myvllm_mini_engine_b200.build``
+or ``__graft_entry__.build()``) and loaded from this package directory.  There
+is no CPU fallback: if the library is missing or fails to load, every op
+raises RuntimeError.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+import torch
+
+LIB_NAME = "libminikv.so"
+LIB_PATH = Path(__file__).resolve().parent / LIB_NAME
+
+F32, F16, BF16 = 0, 1, 2
+OK, EINVAL, ECUDA, EUNSUPPORTED = 0, 1, 2, 3
+DTYPE_CODES = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+
+_p, _i64, _int = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+
+# name -> (restype, argtypes); must match include/minikv.h
+SIGNATURES = {
+    "minikv_abi_version": (_int, []),
+    "minikv_last_error": (ctypes.c_char_p, []),
+    "minikv_device_status": (_int, [ctypes.POINTER(ctypes.c_uint), _int, _p]),
+    "minikv_paged_decode_workspace_bytes": (_i64, [_i64] * 7 + [_int]),
+    "minikv_paged_decode": (_int, [_p] * 6 + [_p, _i64] + [_i64] * 7 + [_int, _p]),
+    "minikv_kv_scatter_slots": (_int, [_p] * 5 + [_i64] * 7 + [_int, _p]),
+    "minikv_kv_append_batch": (_int, [_p] * 6 + [_i64] * 8 + [_int, _p]),
+    "minikv_kv_write_range": (_int, [_p, _p, _p, _i64, _i64, _p, _p] + [_i64] * 7 + [_int, _p]),
+    "minikv_copy_blocks": (_int, [_p, _p, _p] + [_i64] * 4 + [_int, _p]),
+    "minikv_paged_prefill_workspace_bytes": (_i64, [_i64] * 9 + [_int]),
+    "minikv_paged_prefill": (_int, [_p] * 8 + [_p, _i64] + [_i64] * 9 + [_int, _p]),
+    "minikv_build_prefill_metadata": (_int, [_p] * 5 + [_i64] * 4 + [_p] * 7 + [_p]),
+    "minikv_build_decode_tables": (_int, [_p] * 6 + [_i64, _i64] + [_p] * 3 + [_p]),
+}
+
+_LIB = None
+
+
+def load():
+    """Load libminikv once; raise RuntimeError (never fall back) on failure."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    path = Path(os.environ.get("MINIKV_LIBRARY", LIB_PATH))
+    if not path.is_file():
+        raise RuntimeError(f"{path} is missing: build it with `python -m myvllm_mini_engine_b200.build`; "
+                           "this package has no CPU fallback")
+    try:
+        lib = ctypes.CDLL(str(path))
+    except OSError as error:
+        raise RuntimeError(f"cannot load {path}: {error}") from error
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    if lib.minikv_abi_version() != 1:
+        raise RuntimeError("libminikv ABI version mismatch; rebuild the library")
+    _LIB = lib
+    return lib
+
+
+def dtype_code(dtype):
+    try:
+        return DTYPE_CODES[dtype]
+    except KeyError:
+        raise RuntimeError("FP32/FP16/BF16 required") from None
+
+
+def stream_of(device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def check(status: int, what: str) -> None:
+    if status != OK:
+        message = load().minikv_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what}: {message}")
+
+
+def ptr(tensor) -> int | None:
+    return tensor.data_ptr() if tensor is not None and tensor.numel() else None
+
+
+def device_status(device=None, *, clear=True) -> int:
+    """Synchronise the current stream and return (and clear) the device status bits."""
+    lib = load()
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    value = ctypes.c_uint(0)
+    with torch.cuda.device(device):
+        check(lib.minikv_device_status(ctypes.byref(value), int(clear), stream_of(device)), "device status")
+    return value.value

@@ -1,0 +1,314 @@
+// extern "C" entry points of libminikv (declared in include/minikv.h).
+//
+// Each entry point checks its arguments (returning MINIKV_EINVAL with a
+// message, never throwing across the ABI), picks the kernel instantiation and
+// launches on the caller's stream.  Messages reuse the wording of the
+// reference's TORCH_CHECKs (mini_engine/kernels/csrc/bindings.cpp:152-184,
+// data.cu:209-237, prefill.cu:200-233) where a check has a counterpart there.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <string>
+
+#include "../../include/minikv.h"
+#include "common.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& message) {
+    g_last_error = message;
+    return code;
+}
+
+int cuda_fail(cudaError_t err, const char* where) {
+    return fail(MINIKV_ECUDA, std::string(where) + ": " + cudaGetErrorString(err));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool valid_dtype(int dtype) { return dtype == MINIKV_F32 || dtype == MINIKV_F16 || dtype == MINIKV_BF16; }
+
+bool valid_head_dim(int64_t d) {
+    return d == 16 || d == 32 || d == 64 || d == 80 || d == 96 || d == 128 || d == 192 || d == 256;
+}
+
+int elem_bytes(int dtype) { return dtype == MINIKV_F32 ? 4 : 2; }
+
+int sm_count() {
+    static int cached[64] = {0};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 148;
+    if (cached[device] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device);
+        cached[device] = n > 0 ? n : 148;
+    }
+    return cached[device];
+}
+
+#define MINIKV_REQUIRE(cond, code, msg) \
+    do {                                \
+        if (!(cond)) return fail(code, msg); \
+    } while (0)
+
+}  // namespace
+
+#include "kv_write.cu"
+#include "decode.cu"
+#include "metadata.cu"
+#include "prefill.cu"
+
+using namespace minikv;
+
+extern "C" {
+
+int minikv_abi_version(void) { return MINIKV_ABI_VERSION; }
+
+const char* minikv_last_error(void) { return g_last_error.c_str(); }
+
+int minikv_device_status(unsigned int* status, int clear, void* stream) {
+    MINIKV_REQUIRE(status != nullptr, MINIKV_EINVAL, "status pointer is null");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err = cudaStreamSynchronize(s);
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_device_status");
+    err = cudaMemcpyFromSymbol(status, g_status, sizeof(unsigned int));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_device_status");
+    if (clear) {
+        const unsigned int zero = 0;
+        err = cudaMemcpyToSymbol(g_status, &zero, sizeof(unsigned int));
+        if (err != cudaSuccess) return cuda_fail(err, "minikv_device_status");
+    }
+    return MINIKV_OK;
+}
+
+// ------------------------------------------------------------------- decode
+static int check_decode_shapes(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                               int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype) {
+    MINIKV_REQUIRE(valid_dtype(dtype), MINIKV_EINVAL, "FP32/FP16/BF16 required");
+    MINIKV_REQUIRE(batch > 0 && q_heads > 0 && num_blocks > 0 && kv_heads > 0, MINIKV_EINVAL,
+                   "empty batch/heads/cache");
+    MINIKV_REQUIRE(block_size > 0, MINIKV_EINVAL, "block size mismatch");
+    MINIKV_REQUIRE(q_heads % kv_heads == 0, MINIKV_EINVAL, "head dimension or GQA mismatch");
+    MINIKV_REQUIRE(valid_head_dim(head_dim), MINIKV_EINVAL, "supported head_dim: 16,32,64,80,96,128,192,256");
+    MINIKV_REQUIRE(table_width > 0, MINIKV_EINVAL, "invalid block table");
+    MINIKV_REQUIRE(table_width * block_size <= 1048576, MINIKV_EINVAL, "maximum table capacity is 1M tokens");
+    MINIKV_REQUIRE(batch * q_heads <= 2147483647, MINIKV_EINVAL, "batch/head product too large");
+    MINIKV_REQUIRE(num_blocks * block_size <= 2147483647, MINIKV_EINVAL, "KV pool exceeds 2^31 token rows");
+    return MINIKV_OK;
+}
+
+int64_t minikv_paged_decode_workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                            int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                            int64_t table_width, int dtype) {
+    if (check_decode_shapes(batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype))
+        return -1;
+    DecodePlan plan;
+    if (!make_decode_plan(batch, q_heads, kv_heads, head_dim, block_size, table_width, dtype, sm_count(), &plan))
+        return -1;
+    return plan.ws_bytes;
+}
+
+int minikv_paged_decode(const void* query, const void* key_cache, const void* value_cache,
+                        const int64_t* block_tables, const int64_t* context_lens, void* out,
+                        void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
+                        int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                        int64_t table_width, int dtype, void* stream) {
+    int rc = check_decode_shapes(batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype);
+    if (rc) return rc;
+    MINIKV_REQUIRE(query && key_cache && value_cache && block_tables && context_lens && out, MINIKV_EINVAL,
+                   "null pointer argument");
+    MINIKV_REQUIRE(aligned16(query) && aligned16(key_cache) && aligned16(value_cache) && aligned16(out),
+                   MINIKV_EINVAL, "query, caches and output must be 16-byte aligned");
+    return run_decode(query, key_cache, value_cache, block_tables, context_lens, nullptr, out, workspace,
+                      workspace_bytes, batch, q_heads, kv_heads, head_dim, num_blocks, block_size,
+                      table_width, dtype, static_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------- KV writes
+static int check_rows(const void* kc, const void* vc, const void* k, const void* v, int64_t kv_heads,
+                      int64_t head_dim, int64_t k_stride, int64_t v_stride, int dtype) {
+    MINIKV_REQUIRE(valid_dtype(dtype), MINIKV_EINVAL, "KV cache requires FP32/FP16/BF16");
+    MINIKV_REQUIRE(kv_heads > 0 && head_dim > 0, MINIKV_EINVAL, "K/V head shape mismatch");
+    const int64_t row_bytes = kv_heads * head_dim * elem_bytes(dtype);
+    MINIKV_REQUIRE(row_bytes % 16 == 0, MINIKV_EINVAL, "KV row (kv_heads*head_dim) must be a multiple of 16 bytes");
+    MINIKV_REQUIRE(k_stride >= kv_heads * head_dim && v_stride >= kv_heads * head_dim, MINIKV_EINVAL,
+                   "K/V token stride smaller than a row");
+    MINIKV_REQUIRE((k_stride * elem_bytes(dtype)) % 16 == 0 && (v_stride * elem_bytes(dtype)) % 16 == 0,
+                   MINIKV_EINVAL, "K/V token stride must be a multiple of 16 bytes");
+    MINIKV_REQUIRE(kc && vc && k && v, MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(kc) && aligned16(vc) && aligned16(k) && aligned16(v), MINIKV_EINVAL,
+                   "KV tensors must be 16-byte aligned");
+    return MINIKV_OK;
+}
+
+int minikv_kv_scatter_slots(void* key_cache, void* value_cache, const int64_t* slot_mapping, const void* key,
+                            const void* value, int64_t tokens, int64_t num_blocks, int64_t block_size,
+                            int64_t kv_heads, int64_t head_dim, int64_t key_token_stride,
+                            int64_t value_token_stride, int dtype, void* stream) {
+    MINIKV_REQUIRE(tokens >= 0, MINIKV_EINVAL, "packed KV slots must be int64 [tokens]");
+    MINIKV_REQUIRE(num_blocks > 0 && block_size > 0, MINIKV_EINVAL, "packed KV cache must be nonempty");
+    if (tokens == 0) return MINIKV_OK;
+    int rc = check_rows(key_cache, value_cache, key, value, kv_heads, head_dim, key_token_stride,
+                        value_token_stride, dtype);
+    if (rc) return rc;
+    MINIKV_REQUIRE(slot_mapping != nullptr, MINIKV_EINVAL, "null slot_mapping");
+    const int64_t es = elem_bytes(dtype);
+    cudaError_t err = launch_write_rows(key_cache, value_cache, key, value, tokens, kv_heads * head_dim * es,
+                                        key_token_stride * es, value_token_stride * es,
+                                        SlotRows{slot_mapping, num_blocks * block_size},
+                                        static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_kv_scatter_slots launch");
+    return MINIKV_OK;
+}
+
+int minikv_kv_append_batch(void* key_cache, void* value_cache, const int64_t* block_tables,
+                           const int64_t* token_offsets, const void* key, const void* value, int64_t batch,
+                           int64_t table_width, int64_t num_blocks, int64_t block_size, int64_t kv_heads,
+                           int64_t head_dim, int64_t key_token_stride, int64_t value_token_stride, int dtype,
+                           void* stream) {
+    MINIKV_REQUIRE(batch >= 0 && table_width >= 0, MINIKV_EINVAL, "batch table shape mismatch");
+    MINIKV_REQUIRE(num_blocks > 0 && block_size > 0, MINIKV_EINVAL, "batch block size mismatch");
+    if (batch == 0) return MINIKV_OK;
+    MINIKV_REQUIRE(table_width > 0, MINIKV_EINVAL, "batch table shape mismatch");
+    int rc = check_rows(key_cache, value_cache, key, value, kv_heads, head_dim, key_token_stride,
+                        value_token_stride, dtype);
+    if (rc) return rc;
+    MINIKV_REQUIRE(block_tables && token_offsets, MINIKV_EINVAL, "null metadata pointer");
+    const int64_t es = elem_bytes(dtype);
+    cudaError_t err = launch_write_rows(key_cache, value_cache, key, value, batch, kv_heads * head_dim * es,
+                                        key_token_stride * es, value_token_stride * es,
+                                        AppendRows{block_tables, token_offsets, table_width, num_blocks, block_size},
+                                        static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_kv_append_batch launch");
+    return MINIKV_OK;
+}
+
+int minikv_kv_write_range(void* key_cache, void* value_cache, const int64_t* block_ids, int64_t num_ids,
+                          int64_t token_offset, const void* key, const void* value, int64_t tokens,
+                          int64_t num_blocks, int64_t block_size, int64_t kv_heads, int64_t head_dim,
+                          int64_t key_token_stride, int64_t value_token_stride, int dtype, void* stream) {
+    MINIKV_REQUIRE(num_blocks > 0 && block_size > 0, MINIKV_EINVAL, "block size mismatch");
+    MINIKV_REQUIRE(token_offset >= 0 && tokens >= 0 && token_offset + tokens <= num_ids * block_size,
+                   MINIKV_EINVAL, "KV write exceeds block table");
+    if (tokens == 0) return MINIKV_OK;
+    int rc = check_rows(key_cache, value_cache, key, value, kv_heads, head_dim, key_token_stride,
+                        value_token_stride, dtype);
+    if (rc) return rc;
+    MINIKV_REQUIRE(block_ids != nullptr, MINIKV_EINVAL, "null block ids");
+    const int64_t es = elem_bytes(dtype);
+    cudaError_t err = launch_write_rows(key_cache, value_cache, key, value, tokens, kv_heads * head_dim * es,
+                                        key_token_stride * es, value_token_stride * es,
+                                        RangeRows{block_ids, num_ids, token_offset, num_blocks, block_size},
+                                        static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_kv_write_range launch");
+    return MINIKV_OK;
+}
+
+int minikv_copy_blocks(void* key_pool, void* value_pool, const int64_t* pairs, int64_t num_pairs,
+                       int64_t num_layers, int64_t num_blocks, int64_t block_elems, int dtype, void* stream) {
+    MINIKV_REQUIRE(valid_dtype(dtype), MINIKV_EINVAL, "KV pool requires FP32/FP16/BF16");
+    MINIKV_REQUIRE(num_pairs >= 0 && num_layers > 0 && num_blocks > 0 && block_elems > 0, MINIKV_EINVAL,
+                   "copy_blocks shape mismatch");
+    if (num_pairs == 0) return MINIKV_OK;
+    const int64_t page_bytes = block_elems * elem_bytes(dtype);
+    MINIKV_REQUIRE(page_bytes % 16 == 0, MINIKV_EINVAL, "page must be a multiple of 16 bytes");
+    MINIKV_REQUIRE(key_pool && value_pool && pairs, MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(key_pool) && aligned16(value_pool), MINIKV_EINVAL, "pools must be 16-byte aligned");
+    cudaError_t err = launch_copy_blocks(key_pool, value_pool, pairs, num_pairs, num_layers, num_blocks, page_bytes,
+                                         static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_copy_blocks launch");
+    return MINIKV_OK;
+}
+
+// ------------------------------------------------------------------ prefill
+static int check_prefill(int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                         int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype) {
+    MINIKV_REQUIRE(valid_dtype(dtype), MINIKV_EINVAL, "paged prefill requires FP32/FP16/BF16");
+    MINIKV_REQUIRE(block_size > 0 && num_blocks > 0 && kv_heads > 0 && head_dim > 0, MINIKV_EINVAL,
+                   "paged prefill cache/block size mismatch");
+    MINIKV_REQUIRE(q_heads > 0 && q_heads % kv_heads == 0 && valid_head_dim(head_dim), MINIKV_EINVAL,
+                   "paged prefill GQA/head_dim mismatch");
+    MINIKV_REQUIRE(tokens >= 0 && requests >= 0 && table_width >= 0, MINIKV_EINVAL,
+                   "paged prefill metadata shape mismatch");
+    MINIKV_REQUIRE(tokens * q_heads <= 2147483647, MINIKV_EINVAL, "too many paged prefill rows");
+    MINIKV_REQUIRE(num_blocks * block_size <= 2147483647, MINIKV_EINVAL, "KV pool exceeds 2^31 token rows");
+    return MINIKV_OK;
+}
+
+int64_t minikv_paged_prefill_workspace_bytes(int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
+                                             int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                             int64_t table_width, int64_t max_query_len, int dtype) {
+    if (check_prefill(tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype))
+        return -1;
+    return prefill_workspace_bytes(tokens, requests, q_heads, kv_heads, head_dim, block_size, table_width,
+                                   max_query_len, dtype, sm_count());
+}
+
+int minikv_paged_prefill(const void* q, const void* key_cache, const void* value_cache,
+                         const int64_t* cu_seqlens_q, const int64_t* query_starts, const int64_t* block_tables,
+                         const int64_t* context_lens, void* out, void* workspace, int64_t workspace_bytes,
+                         int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                         int64_t num_blocks, int64_t block_size, int64_t table_width, int64_t max_query_len,
+                         int dtype, void* stream) {
+    int rc = check_prefill(tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width,
+                           dtype);
+    if (rc) return rc;
+    if (tokens == 0) return MINIKV_OK;
+    MINIKV_REQUIRE(requests > 0 && table_width > 0, MINIKV_EINVAL, "paged prefill metadata shape mismatch");
+    MINIKV_REQUIRE(q && key_cache && value_cache && cu_seqlens_q && query_starts && block_tables && context_lens &&
+                       out,
+                   MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(q) && aligned16(key_cache) && aligned16(value_cache) && aligned16(out), MINIKV_EINVAL,
+                   "paged prefill tensors must be 16-byte aligned");
+    const int64_t need = prefill_workspace_bytes(tokens, requests, q_heads, kv_heads, head_dim, block_size,
+                                                 table_width, max_query_len, dtype, sm_count());
+    MINIKV_REQUIRE(need >= 0, MINIKV_EUNSUPPORTED, "paged prefill shape does not fit shared memory");
+    MINIKV_REQUIRE(workspace_bytes >= need && (need == 0 || (workspace && aligned16(workspace))), MINIKV_EINVAL,
+                   "paged prefill workspace too small or misaligned");
+    return run_prefill(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens, out,
+                       workspace, tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width,
+                       max_query_len, dtype, static_cast<cudaStream_t>(stream));
+}
+
+// ----------------------------------------------------------------- metadata
+int minikv_build_prefill_metadata(const int64_t* query_starts, const int64_t* cu_seqlens_q, const int64_t* cu_blocks,
+                                  const int64_t* block_ids, const int64_t* token_ids, int64_t requests,
+                                  int64_t tokens, int64_t table_width, int64_t block_size, int64_t* input_ids,
+                                  int64_t* positions, int64_t* slot_mapping, int64_t* out_cu_seqlens_q,
+                                  int64_t* out_query_starts, int64_t* context_lens, int64_t* block_tables,
+                                  void* stream) {
+    MINIKV_REQUIRE(requests > 0 && tokens >= 0 && table_width > 0 && block_size > 0, MINIKV_EINVAL,
+                   "prefill metadata shape mismatch");
+    MINIKV_REQUIRE(query_starts && cu_seqlens_q && cu_blocks && block_ids && (token_ids || tokens == 0) &&
+                       (input_ids || tokens == 0) && (positions || tokens == 0) && (slot_mapping || tokens == 0) &&
+                       out_cu_seqlens_q && out_query_starts && context_lens && block_tables,
+                   MINIKV_EINVAL, "null pointer argument");
+    const int64_t grid = std::min<int64_t>(requests, (int64_t)sm_count() * 4);
+    prefill_metadata_kernel<<<(unsigned)grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        query_starts, cu_seqlens_q, cu_blocks, block_ids, token_ids, requests, table_width, block_size, input_ids,
+        positions, slot_mapping, out_cu_seqlens_q, out_query_starts, context_lens, block_tables);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_build_prefill_metadata launch");
+    return MINIKV_OK;
+}
+
+int minikv_build_decode_tables(const int64_t* active, const int64_t* tokens, const int64_t* positions,
+                               const int64_t* cu_blocks, const int64_t* block_ids, const int64_t* padding_pages,
+                               int64_t batch_size, int64_t max_blocks, int64_t* input_ids, int64_t* out_positions,
+                               int64_t* block_tables, void* stream) {
+    MINIKV_REQUIRE(batch_size > 0 && max_blocks > 0, MINIKV_EINVAL, "decode bucket shape must be positive");
+    MINIKV_REQUIRE(active && tokens && positions && cu_blocks && block_ids && padding_pages && input_ids &&
+                       out_positions && block_tables,
+                   MINIKV_EINVAL, "null pointer argument");
+    const int64_t grid = std::min<int64_t>(batch_size, (int64_t)sm_count() * 4);
+    decode_tables_kernel<<<(unsigned)grid, 128, 0, static_cast<cudaStream_t>(stream)>>>(
+        active, tokens, positions, cu_blocks, block_ids, padding_pages, batch_size, max_blocks, input_ids,
+        out_positions, block_tables);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_build_decode_tables launch");
+    return MINIKV_OK;
+}
+
+}  // extern "C"

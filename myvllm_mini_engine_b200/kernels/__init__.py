@@ -1,0 +1,8 @@
+"""Operator API of the paged-KV hot path (mirrors ``mini_engine/kernels``)."""
+
+from .data import copy_blocks, write_kv_cache, write_kv_cache_batch, write_kv_cache_slots
+from .paged import paged_attention
+from .prefill import paged_prefill_attention
+
+__all__ = ["copy_blocks", "paged_attention", "paged_prefill_attention", "write_kv_cache",
+           "write_kv_cache_batch", "write_kv_cache_slots"]

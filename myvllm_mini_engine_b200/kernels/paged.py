@@ -1,0 +1,100 @@
+"""Paged decode attention -- drop-in for ``mini_engine/kernels/paged.py``.
+
+Same signature as the reference (paged.py:8-22).  There is one implementation,
+the sm_100a split-KV kernel in libminikv; ``backend`` is accepted for
+compatibility and must name a CUDA backend ("cuda", "cuda_baseline" and
+"cuda_vector128" all run the same kernel).  Argument errors raise RuntimeError
+with the messages of the reference's native checks
+(``mini_engine/kernels/csrc/bindings.cpp:152-184``); ``validate=True`` adds the
+same host-synchronising metadata checks (bindings.cpp:175-182).  fp32 is
+supported in addition to fp16/bf16.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+CUDA_BACKENDS = ("cuda", "cuda_baseline", "cuda_vector128")
+HEAD_DIMS = (16, 32, 64, 80, 96, 128, 192, 256)
+
+
+def _require(condition, message):
+    if not condition:
+        raise RuntimeError(message)
+
+
+def check_backend(backend):
+    if backend not in CUDA_BACKENDS:
+        raise ValueError("decode backend must be cuda, cuda_baseline or cuda_vector128 "
+                         "(this package has no torch/CPU path)")
+
+
+def paged_attention(query, key_cache, value_cache, block_tables, context_lens, block_size,
+                    *, backend="cuda", validate=True, workspace=None):
+    """Decode attention ``out[b, h] = softmax(q . K^T / sqrt(D)) V`` over paged K/V.
+
+    ``query [B, Hq, D]``, ``key_cache``/``value_cache`` ``[num_blocks, block_size,
+    Hkv, D]``, ``block_tables [B, W]`` int64 (-1 padded), ``context_lens [B]`` int64.
+    Returns a new ``[B, Hq, D]`` tensor in the query dtype.  ``workspace`` (a
+    uint8 CUDA tensor of at least :func:`workspace_bytes` bytes) may be passed to
+    reuse scratch memory; otherwise it comes from torch's caching allocator.
+    """
+    check_backend(backend)
+    _require(query.is_cuda, "query must be CUDA")
+    for t in (key_cache, value_cache, block_tables, context_lens):
+        _require(t.device == query.device, "all inputs must be on the same CUDA device")
+        _require(t.is_contiguous(), "inputs must be contiguous")
+    _require(query.is_contiguous(), "query must be contiguous")
+    _require(query.dim() == 3 and key_cache.dim() == 4 and value_cache.shape == key_cache.shape,
+             "invalid query/cache shapes")
+    _require(query.dtype in _lib.DTYPE_CODES, "FP32/FP16/BF16 required")
+    _require(key_cache.dtype == query.dtype and value_cache.dtype == query.dtype, "cache dtype mismatch")
+    _require(block_tables.dtype == torch.int64 and context_lens.dtype == torch.int64, "metadata must be int64")
+    batch, heads, dim = query.shape
+    num_blocks, bs, kv_heads, _ = key_cache.shape
+    _require(batch > 0 and heads > 0 and num_blocks > 0 and kv_heads > 0, "empty batch/heads/cache")
+    _require(block_size > 0 and bs == block_size, "block size mismatch")
+    _require(dim == key_cache.shape[3] and heads % kv_heads == 0, "head dimension or GQA mismatch")
+    _require(dim in HEAD_DIMS, "supported head_dim: 16,32,64,80,96,128,192,256")
+    _require(block_tables.dim() == 2 and block_tables.shape[0] == batch and block_tables.shape[1] > 0,
+             "invalid block table")
+    _require(context_lens.dim() == 1 and context_lens.shape[0] == batch, "invalid context lengths")
+    width = block_tables.shape[1]
+    _require(width * block_size <= 1048576, "maximum table capacity is 1M tokens")
+    _require(batch * heads <= 2147483647, "batch/head product too large")
+    if validate:
+        _require(not bool(((context_lens <= 0) | (context_lens > width * block_size)).any()),
+                 "invalid context length")
+        positions = torch.arange(width, device=query.device, dtype=torch.int64) * block_size
+        active = positions.unsqueeze(0) < context_lens.unsqueeze(1)
+        _require(not bool((((block_tables < 0) | (block_tables >= num_blocks)) & active).any()),
+                 "physical block id out of range")
+    lib = _lib.load()
+    code = _lib.dtype_code(query.dtype)
+    need = lib.minikv_paged_decode_workspace_bytes(batch, heads, kv_heads, dim, num_blocks, block_size, width, code)
+    if need < 0:
+        _lib.check(_lib.EINVAL, "paged_attention")
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=query.device)
+    out = torch.empty_like(query)
+    with torch.cuda.device(query.device):
+        status = lib.minikv_paged_decode(
+            query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
+            context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
+            batch, heads, kv_heads, dim, num_blocks, block_size, width, code, _lib.stream_of(query.device))
+    _lib.check(status, "paged_attention")
+    return out
+
+
+def workspace_bytes(query, key_cache, block_tables):
+    """Scratch bytes one :func:`paged_attention` call with these shapes needs."""
+    lib = _lib.load()
+    batch, heads, dim = query.shape
+    num_blocks, block_size, kv_heads, _ = key_cache.shape
+    need = lib.minikv_paged_decode_workspace_bytes(batch, heads, kv_heads, dim, num_blocks, block_size,
+                                                   block_tables.shape[1], _lib.dtype_code(query.dtype))
+    if need < 0:
+        _lib.check(_lib.EINVAL, "workspace_bytes")
+    return need

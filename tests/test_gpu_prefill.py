@@ -1,0 +1,114 @@
+"""Ragged paged prefill on the GPU against the CPU oracle, including BASELINE config 4
+(copy-on-write of a shared prefix page + slot scatter + prefill)."""
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from myvllm_mini_engine_b200.cache import BlockManager
+from myvllm_mini_engine_b200.engine import PrefillBatch
+from myvllm_mini_engine_b200.kernels import copy_blocks, paged_prefill_attention, write_kv_cache_slots
+from oracle import kv_write, metadata, prefill
+
+pytestmark = pytest.mark.gpu
+TOL = {torch.float32: 1e-4, torch.float16: 2e-3, torch.bfloat16: 1e-2}
+PREFILL = np.load(Path(__file__).resolve().parent / "golden" / "golden_prefill.npz")
+NAMES = ("q", "key_cache", "value_cache", "cu_seqlens_q", "query_starts", "block_tables", "context_lens")
+
+
+def assert_close(actual, expected_fp32, dtype):
+    torch.testing.assert_close(actual.float().cpu(), expected_fp32, atol=TOL[dtype], rtol=TOL[dtype])
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("dim", [16, 128])
+def test_small_packed_prefill_on_nondefault_stream(cuda_device, dtype, dim):
+    c = cases.ragged_small(dtype, dim)
+    expected = prefill.per_token_fp32(*[c[k] for k in NAMES], 4)
+    args = [c[k].cuda() for k in NAMES]
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        result = paged_prefill_attention(*args, 4)
+    torch.cuda.current_stream().wait_stream(stream)
+    assert_close(result, expected, dtype)
+    if dtype == torch.float32 and dim == 16:
+        golden = torch.from_numpy(PREFILL["small/out"]).view(torch.float32).reshape(result.shape)
+        assert_close(result, golden, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("dim,heads,kv_heads", [(128, 16, 8), (64, 8, 8), (128, 32, 4), (96, 16, 8), (256, 16, 8)])
+def test_ragged_prefill_matches_oracle(cuda_device, dtype, dim, heads, kv_heads):
+    c = cases.ragged_prefill_case(dtype, head_dim=dim, heads=heads, kv_heads=kv_heads)
+    expected = prefill.paged_prefill_fp32(*[c[k] for k in NAMES], c["block_size"])
+    result = paged_prefill_attention(*[c[k].cuda() for k in NAMES], c["block_size"])
+    assert_close(result, expected, dtype)
+
+
+@pytest.mark.parametrize("name", ["fp16", "bf16"])
+def test_ragged_prefill_matches_reference_golden(cuda_device, name):
+    dtype = {"fp16": torch.float16, "bf16": torch.bfloat16}[name]
+    c = cases.ragged_prefill_case(dtype)
+    result = paged_prefill_attention(*[c[k].cuda() for k in NAMES], c["block_size"])
+    golden = torch.from_numpy(PREFILL[f"ragged_{name}/out"]).view(dtype).reshape(result.shape)
+    assert_close(result, golden.float(), dtype)
+
+
+def test_context_beyond_dense_prefill_limit(cuda_device):
+    block, context = 32, 8193
+    gen = cases.rng(77)
+    pages = (context + block - 1) // block
+    key = cases.randn(gen, (pages, block, 1, 16), torch.float16)
+    value = cases.randn(gen, (pages, block, 1, 16), torch.float16)
+    q = cases.randn(gen, (1, 2, 16), torch.float16)
+    tables = torch.from_numpy(gen.permutation(pages).astype(np.int64)).view(1, -1)
+    meta = [torch.tensor([0, 1]), torch.tensor([context - 1]), tables, torch.tensor([context])]
+    expected = prefill.per_token_fp32(q, key, value, meta[0], meta[1], meta[2], meta[3], block)
+    actual = paged_prefill_attention(q.cuda(), key.cuda(), value.cuda(), meta[0].cuda(), meta[1].cuda(),
+                                     meta[2].cuda(), meta[3].cuda(), block)
+    assert_close(actual, expected, torch.float16)
+
+
+def test_empty_packed_queries(cuda_device):
+    c = cases.ragged_small(torch.bfloat16, 16)
+    empty = torch.empty(0, dtype=torch.int64, device="cuda")
+    result = paged_prefill_attention(c["q"][:0].cuda(), c["key_cache"].cuda(), c["value_cache"].cuda(),
+                                     torch.tensor([0], device="cuda"), empty,
+                                     torch.empty(0, 0, dtype=torch.int64, device="cuda"), empty, 4)
+    assert result.shape == (0, 4, 16)
+
+
+def test_config4_copy_on_write_scatter_and_prefill(cuda_device):
+    c = cases.config4()
+    bs = c["block_size"]
+    # host allocator decides the copy-on-write exactly as the case describes
+    manager = BlockManager(c["num_blocks"], bs)
+    # oracle path (CPU): CoW copy, metadata, scatter, prefill
+    kc, vc = c["key_cache"].clone(), c["value_cache"].clone()
+    kv_write.copy_blocks(kc.unsqueeze(0), vc.unsqueeze(0), [c["cow_pair"]])
+    meta = metadata.prefill_metadata(c["tokens"], c["cow_tables"], c["starts"], block_size=bs,
+                                     num_blocks=c["num_blocks"])
+    t = {k: torch.tensor(v, dtype=torch.int64) for k, v in meta.items()}
+    kv_write.write_kv_cache_slots(kc, vc, t["slot_mapping"], c["key"], c["value"])
+    expected = prefill.paged_prefill_fp32(c["q"], kc, vc, t["cu_seqlens_q"], t["query_starts"],
+                                          t["block_tables"], t["context_lens"], bs)
+    # GPU path: device CoW, device metadata, scatter, tcgen05 prefill
+    gk, gv = c["key_cache"].cuda(), c["value_cache"].cuda()
+    copy_blocks(gk.unsqueeze(0), gv.unsqueeze(0), [c["cow_pair"]])
+    batch = PrefillBatch.from_sequences(c["tokens"], c["cow_tables"], c["starts"], block_size=bs,
+                                        num_blocks=c["num_blocks"], device="cuda")
+    for name, values in meta.items():
+        assert getattr(batch, name).tolist() == values, name
+    write_kv_cache_slots(gk, gv, batch.slot_mapping, c["key"].cuda(), c["value"].cuda(), validate=False)
+    assert torch.equal(gk.cpu(), kc) and torch.equal(gv.cpu(), vc)
+    out = paged_prefill_attention(c["q"].cuda(), gk, gv, batch.cu_seqlens_q, batch.query_starts,
+                                  batch.block_tables, batch.context_lens, bs, validate=False)
+    assert_close(out, expected, torch.bfloat16)
+    rows = torch.from_numpy(PREFILL["config4/rows"])
+    golden = torch.from_numpy(PREFILL["config4/out_rows"]).view(torch.bfloat16).reshape(-1, 16, 128)
+    assert_close(out[rows.cuda()], golden.float(), torch.bfloat16)
+    del manager
