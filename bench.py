@@ -46,8 +46,8 @@ HQ, HKV, D, BS = 16, 8, 128, 16
 def parse_args(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=200)
-    parser.add_argument("--warmup", type=int, default=10)
+    parser.add_argument("--steps", type=int, default=20000)
+    parser.add_argument("--warmup", type=int, default=20)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--batch", type=int, default=32, help="requests per GPU")
     parser.add_argument("--context", type=int, default=2048, help="attended tokens per request")
@@ -225,8 +225,13 @@ def run_reference(args, world, rank):
         return None
     torch.set_num_threads(os.cpu_count() or 1)
     ref = CpuReference(args.context)
-    ref.timed(0.0, args.warmup)
-    per_step, done = ref.timed(0.0, args.steps)
+    ref.timed(0.0, min(args.warmup, 3))
+    # each step is a bounded CPU sample; stop after ~60 s so the run ends in minutes
+    done, start = 0, time.perf_counter()
+    while done < args.steps and (done < 3 or time.perf_counter() - start < 60.0):
+        ref.step()
+        done += 1
+    per_step = (time.perf_counter() - start) / done
     base = ref.describe(per_step, done)
     value = base["value"]
     return {"metric": METRIC, "value": value, "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,

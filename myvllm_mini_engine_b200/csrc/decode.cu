@@ -427,8 +427,15 @@ __global__ void __launch_bounds__(256) paged_decode_combine_kernel(const DecodeP
     if (c0 == c1) return;  // a single CTA wrote the final row
     const int n = c1 - c0 + 1;
     const int64_t first = (int64_t)b + c0;
+    // CTAs whose tile range is empty (grid larger than the batch's tile count)
+    // wrote no record: their weight is zero.
+    auto owns_tiles = [&](int k) {
+        const int64_t cta = c0 + k;
+        return (cta * total) / G != ((cta + 1) * total) / G;
+    };
     float mx = -INFINITY;
-    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, p.lse[(first + k) * p.q_heads + qh]);
+    for (int k = lane; k < n; k += 32)
+        if (owns_tiles(k)) mx = fmaxf(mx, p.lse[(first + k) * p.q_heads + qh]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     constexpr int kMaxDimsPerLane = 8;  // D <= 256
@@ -438,7 +445,7 @@ __global__ void __launch_bounds__(256) paged_decode_combine_kernel(const DecodeP
     float wsum = 0.f;
     for (int base = 0; base < n; base += 32) {
         float w = 0.f;
-        if (base + lane < n && mx != -INFINITY) {
+        if (base + lane < n && mx != -INFINITY && owns_tiles(base + lane)) {
             const float lse = p.lse[(first + base + lane) * p.q_heads + qh];
             w = (lse == -INFINITY) ? 0.f : exp2f(lse - mx);
         }

@@ -23,7 +23,8 @@ def test_slot_scatter_bit_exact_on_nondefault_stream_with_strided_sources(cuda_d
     expected_k, expected_v = c["key_cache"].clone(), c["value_cache"].clone()
     kv_write.write_kv_cache_slots(expected_k, expected_v, c["slot_mapping"], c["key"], c["value"])
     g = cuda(c)
-    key, value = g["key"], g["value"]        # [:, :2] / [:, 2:] views of one packed tensor
+    packed = torch.cat([c["key"], c["value"]], dim=1).cuda()
+    key, value = packed[:, :2], packed[:, 2:]  # split-projection views: token-strided, rows contiguous
     assert not key.is_contiguous()
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())

@@ -36,10 +36,10 @@ def test_prefill_metadata_random_batch_matches_reference(cuda_device):
     expected = metadata.prefill_metadata(m["tokens"], m["tables"], m["starts"], block_size=m["block_size"],
                                          num_blocks=m["num_blocks"])
     assert {n: getattr(batch, n).tolist() for n in NAMES} == expected
-    batch.validate(block_size=m["block_size"], num_blocks=m["num_blocks"], device="cuda",
+    batch.validate(block_size=m["block_size"], num_blocks=m["num_blocks"], device=cuda_device,
                    max_position_embeddings=4096, vocab_size=151936)
     with pytest.raises(ValueError, match="vocabulary"):
-        batch.validate(block_size=m["block_size"], num_blocks=m["num_blocks"], device="cuda",
+        batch.validate(block_size=m["block_size"], num_blocks=m["num_blocks"], device=cuda_device,
                        max_position_embeddings=4096, vocab_size=10)
 
 
