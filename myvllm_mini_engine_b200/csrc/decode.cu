@@ -469,8 +469,15 @@ __global__ void __launch_bounds__(256) paged_decode_combine_kernel(const DecodeP
     }
 }
 
+}  // namespace minikv
+
+#include "decode_mma.cu"
+
+namespace minikv {
+
 // ------------------------------------------------------------------ host side
 struct DecodePlan {
+    bool mma;
     int tile_tokens, stages, row_bytes, heads_per_cta, chunks_per_head, chunk_groups, head_groups;
     int grid, smem_bytes;
     int64_t records, ws_prefix, ws_lse, ws_partial, ws_bytes;
@@ -486,12 +493,17 @@ static int lanes_per_token(int D, int esize) {
 static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
 // Everything here depends on shapes and the device only (graph-static).
+// fp16/bf16 use the tensor-core consumer (decode_mma.cu): warps own up to 16
+// query heads, shared-memory rows are padded by 16 bytes and tiles are
+// multiples of 16 tokens.  fp32 uses the CUDA-core consumer above.
 static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t block_size,
                              int64_t table_width, int dtype, int sm_count, DecodePlan* plan) {
     const int es = esize_of(dtype);
-    const int sc = kTokensPerGroup * (32 / lanes_per_token((int)D, es));
+    const bool mma = dtype != 0;
+    const int sc = mma ? 16 : kTokensPerGroup * (32 / lanes_per_token((int)D, es));
+    const int heads_per_item = mma ? 16 : kItemHeads;
     const int64_t group = Hq / Hkv;
-    const int cph = (int)((group + kItemHeads - 1) / kItemHeads);
+    const int cph = (int)((group + heads_per_item - 1) / heads_per_item);
     int hpc, ncg, z;
     if (cph >= kConsumerWarps) {
         hpc = 1;
@@ -503,13 +515,13 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
         ncg = 1;
         z = (int)((Hkv + hpc - 1) / hpc);
     }
-    const int row = hpc * (int)D * es;
+    const int row = hpc * (int)D * es + (mma ? 16 : 0);  // shared-memory row stride
     int tt = (32768 / row) / sc * sc;
     tt = std::max(sc, std::min(64, tt));
     const int stage = 2 * tt * row;
     const int fixed = (int)((B + 1) * 4) + 128;
     const int max_smem = 232448 - 1024;  // opt-in limit per block, minus static smem
-    int stages = std::min(4, (196608) / stage);
+    int stages = std::min(4, (196608 + 4096) / stage);
     while (stages > 1 && stages * (stage + 24) + fixed > max_smem) --stages;
     if (stages < 1 || stages * (stage + 24) + fixed > max_smem) return false;
     const int smem = stages * (stage + 24) + fixed;
@@ -517,6 +529,7 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
     const int64_t cap = table_width * block_size;
     const int64_t upper_tiles = B * ((cap + tt - 1) / tt);
     const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((int64_t)sm_count * per_sm, upper_tiles));
+    plan->mma = mma;
     plan->tile_tokens = tt;
     plan->stages = stages;
     plan->row_bytes = row;
@@ -534,12 +547,25 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
     return true;
 }
 
+template <typename Kernel>
+static cudaError_t set_smem(Kernel kernel, int bytes) {
+    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
 template <typename T, int D>
 static cudaError_t launch_decode_typed(const DecodeParams& p, const DecodePlan& plan, cudaStream_t stream) {
-    auto kernel = paged_decode_split_kernel<T, D>;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.smem_bytes);
-    if (err != cudaSuccess) return err;
-    kernel<<<dim3(plan.grid, plan.head_groups), kDecodeThreads, plan.smem_bytes, stream>>>(p);
+    cudaError_t err;
+    if constexpr (sizeof(T) == 2) {
+        auto kernel = paged_decode_mma_kernel<T, D>;
+        err = set_smem(kernel, plan.smem_bytes);
+        if (err != cudaSuccess) return err;
+        kernel<<<dim3(plan.grid, plan.head_groups), kDecodeThreads, plan.smem_bytes, stream>>>(p);
+    } else {
+        auto kernel = paged_decode_split_kernel<T, D>;
+        err = set_smem(kernel, plan.smem_bytes);
+        if (err != cudaSuccess) return err;
+        kernel<<<dim3(plan.grid, plan.head_groups), kDecodeThreads, plan.smem_bytes, stream>>>(p);
+    }
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
     const int rows = p.batch * p.q_heads;
