@@ -2,9 +2,9 @@
 //
 // * element traits: 16-byte vectors of fp32 / fp16 / bf16 <-> fp32 registers;
 // * mbarrier + 1-D bulk-copy (TMA engine) wrappers in inline PTX;
-// * bounded waits: every spin on an mbarrier gives up after a fixed number of
-//   suspended try_wait rounds (about two seconds in total), records an error
-//   bit in the device status word and lets the kernel run to its end.
+// * bounded waits: every spin on an mbarrier polls with try_wait and gives up
+//   after two seconds of %globaltimer time, records an error bit in the device
+//   status word and lets the kernel run to its end.
 #pragma once
 
 #include <cuda.h>
@@ -105,25 +105,38 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                  ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
 }
 
+// One polling probe of the phase with the given parity (no suspend-time hint:
+// the call returns after a short, hardware-defined interval at the latest).
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t done;
-    // Suspend-time hint of 1 ms: the call returns as soon as the phase flips.
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(done) : "r"(smem_addr(bar)), "r"(parity), "r"(1000000u) : "memory");
+        : "=r"(done) : "r"(smem_addr(bar)), "r"(parity) : "memory");
     return done != 0;
 }
 
-constexpr int kWaitRounds = 2000;  // x <= 1 ms suspend hint each
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
 // Bounded wait for the phase with the given parity.  Returns false (and sets
-// the status bit) if the phase did not complete in time; callers then carry on
-// so that the kernel reaches its end instead of hanging the GPU.
+// the status bit) if the phase did not complete within kWaitLimitNs; callers
+// then carry on so that the kernel reaches its end instead of hanging the GPU.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (int round = 0; round < kWaitRounds; ++round)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t start = global_ns();
+    for (;;) {
+#pragma unroll 1
+        for (int i = 0; i < 32; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - start > kWaitLimitNs) break;
+    }
     raise_status(kStatusWaitTimeout);
     return false;
 }

@@ -3,27 +3,33 @@
 // Work decomposition ("balanced split-KV").  The tokens of every request are
 // cut into tiles of TT tokens; the tiles of the whole batch form one list of
 // `total` tiles and CTA c of a persistent grid of G CTAs (one per SM) takes
-// tiles [c*total/G, (c+1)*total/G).  A CTA therefore streams an equal share
-// of the batch's KV bytes whatever the (ragged) lengths are; its range covers
-// one or more request *segments*.  A segment that is a whole request writes
-// the final output; otherwise it writes an fp32 partial (output normalised by
-// its own softmax sum) and its log2-sum-exp, and a second kernel merges the
-// partials of each request (exactly the reference's merge,
-// mini_engine/kernels/csrc/paged_attention.cu:195-215).  The grid, the
-// workspace and the record layout depend only on (batch, table width, block
-// size, heads, head dim, dtype) and the SM count, never on context_lens, so a
-// captured CUDA graph stays valid when lengths change (the reference derives
-// its partition count from the table width for the same reason,
-// paged_attention.cu:271).
+// tiles [c*total/G, (c+1)*total/G).  A CTA therefore streams an equal share of
+// the batch's KV bytes whatever the (ragged) lengths are; its range covers one
+// or more request *segments*.  A segment that is a whole request writes the
+// final output.  Otherwise it writes an fp32 partial (its output normalised by
+// its own softmax sum) and its log2-sum-exp, takes a ticket on the request's
+// counter, and the CTA holding the last ticket merges the partials
+// (exp-weighted by log-sum-exp, as the reference's second pass does,
+// mini_engine/kernels/csrc/paged_attention.cu:195-215) -- inside this kernel,
+// so there is no second launch.  The grid, the workspace and the record layout
+// depend only on (batch, table width, block size, heads, head dim, dtype) and
+// the SM count, never on context_lens, so a captured CUDA graph stays valid
+// when lengths change (the reference derives its partition count from the
+// table width for the same reason, paged_attention.cu:271).
 //
-// CTA layout: 8 consumer warps + 1 producer warp.  The producer stages each
-// tile's K and V rows -- all kv heads of the CTA's head group, i.e. whole
-// contiguous page rows -- into shared memory with 1-D bulk copies (TMA engine)
-// on a ring of `stages` buffers guarded by full/empty mbarriers.  Each
-// consumer warp owns one kv head and two of its query heads (GQA: every KV
-// byte is read from HBM once per step, whatever the group size), keeps a
-// per-lane-group online softmax in registers and merges the lane groups when
-// the segment ends.
+// CTA layout: 8 consumer warps + 1 producer warp.  The producer first reads
+// the physical rows of the next 32 tiles into shared memory with independent
+// loads (one page-table lookup per page, all in flight together), then stages
+// every tile's K and V rows -- all kv heads of the CTA's head group -- into
+// shared memory with 1-D bulk copies (TMA engine), on a ring of `stages`
+// buffers guarded by full/empty mbarriers.  Token rows in shared memory are
+// padded by 16 bytes.  Each consumer warp owns one kv head and some of its
+// query heads (GQA: every KV byte is read from HBM once per step, whatever the
+// group size):
+//  * fp16/bf16: tensor-core consumer (decode_mma.cu), up to 8 query heads per
+//    warp as the N columns of mma.sync m16n8k16 (tokens are the M rows);
+//  * fp32: CUDA-core consumer below, two query heads per warp, lane groups
+//    with their own online softmax merged at segment end.
 //
 // Trusted-mode guards of the reference kernel are kept: a page id outside
 // [0, num_blocks) masks its tokens (score -inf, paged_attention.cu:72-82); a
@@ -35,8 +41,10 @@ namespace minikv {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
-constexpr int kItemHeads = 2;      // query heads per consumer warp
-constexpr int kTokensPerGroup = 4; // tokens per lane group per sub-chunk
+constexpr int kCoreHeads = 2;       // query heads per CUDA-core consumer warp
+constexpr int kMmaHeads = 8;        // query heads per tensor-core consumer warp (MMA N)
+constexpr int kTokensPerGroup = 4;  // CUDA-core: tokens per lane group per sub-chunk
+constexpr int kWindowTiles = 32;    // tiles whose rows the producer prefetches at once
 
 struct DecodeParams {
     const void* q;
@@ -46,46 +54,47 @@ struct DecodeParams {
     const int64_t* lens;
     const int64_t* table_rows;  // table row of request b (nullptr: row b)
     void* out;
-    float* partial;   // [records, q_heads, D]
-    float* lse;       // [records, q_heads]   (log2 domain)
-    int* prefix_out;  // [batch + 1] tile prefix, written by CTA (0, 0)
+    float* partial;             // [records, q_heads, D]
+    float* lse;                 // [records, q_heads]   (log2 domain)
+    unsigned int* tickets;      // [batch, head groups], zero before the launch; left zero after it
     int batch, q_heads, kv_heads, num_blocks, block_size, table_width;
     int group;            // q_heads / kv_heads
-    int chunks_per_head;  // ceil(group / kItemHeads)
+    int heads_per_item;   // query heads per consumer warp
+    int chunks_per_head;  // ceil(group / heads_per_item)
     int heads_per_cta;    // kv heads per CTA head group (1 when chunks_per_head >= 8)
     int chunk_groups;     // head groups per kv head (> 1 only when chunks_per_head > 8)
-    int tile_tokens;      // TT, multiple of the sub-chunk size, <= 64
+    int tile_tokens;      // TT, multiple of the consumer's sub-chunk, <= 64
     int stages;
-    int row_bytes;        // shared-memory row stride = heads_per_cta * D * elem
+    int row_stride;       // shared-memory stride of one token row (padded)
     float scale_log2;     // log2(e) / sqrt(D)
 };
 
-template <typename T, int D>
-struct DecodeShape {
-    static constexpr int E = Elem<T>::kPerVec;           // elements per 16 B
-    static constexpr int VR = D / E;                      // vectors per head row
-    static constexpr int LPT = (VR % 8 == 0) ? 8 : (VR % 4 == 0) ? 4 : 2;  // lanes per token
-    static constexpr int VPL = VR / LPT;                  // vectors per lane
-    static constexpr int TPI = 32 / LPT;                  // lane groups (tokens in flight)
-    static constexpr int SC = kTokensPerGroup * TPI;      // tokens per sub-chunk
-    static_assert(VR % LPT == 0 && VR >= 2, "unsupported head_dim for this dtype");
-};
-
-// CTA c of G owns tiles [c*total/G, (c+1)*total/G); cta_of(t) inverts it.
+// CTA c of G owns tiles [c*total/G, (c+1)*total/G); cta_of_tile(t) inverts it.
 __device__ __forceinline__ int cta_of_tile(int t, int G, int total) {
     return (int)((((int64_t)t + 1) * G + total - 1) / total) - 1;
 }
+__device__ __forceinline__ bool cta_owns_tiles(int cta, int G, int total) {
+    return ((int64_t)cta * total) / G != ((int64_t)(cta + 1) * total) / G;
+}
 
-// Exclusive prefix of per-request tile counts into prefix[0..B] (shared).
+// Consumer-only barrier (the producer warp never joins it).
+__device__ __forceinline__ void consumers_sync() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kConsumerWarps * 32) : "memory");
+}
+
+// lens_s[b] = usable length (0 when out of range); prefix[0..B] = exclusive
+// prefix of per-request tile counts.  All threads of the CTA take part.
 __device__ void tile_prefix(const int64_t* __restrict__ lens, int B, int64_t cap, int TT, int* prefix,
-                            int* warp_sums) {
+                            int* lens_s, int* warp_sums) {
     const int tid = threadIdx.x, nthreads = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int per = (B + nthreads - 1) / nthreads;
     const int lo = min(B, tid * per), hi = min(B, lo + per);
     int local = 0;
     for (int i = lo; i < hi; ++i) {
         const int64_t len = lens[i];
-        local += (len > 0 && len <= cap) ? (int)((len + TT - 1) / TT) : 0;
+        const int usable = (len > 0 && len <= cap) ? (int)len : 0;
+        lens_s[i] = usable;
+        local += (usable + TT - 1) / TT;
     }
     int incl = local;
 #pragma unroll
@@ -108,32 +117,251 @@ __device__ void tile_prefix(const int64_t* __restrict__ lens, int B, int64_t cap
     __syncthreads();
     int run = incl - local + (warp > 0 ? warp_sums[warp - 1] : 0);
     for (int i = lo; i < hi; ++i) {
-        const int64_t len = lens[i];
         prefix[i] = run;
-        run += (len > 0 && len <= cap) ? (int)((len + TT - 1) / TT) : 0;
+        run += (lens_s[i] + TT - 1) / TT;
     }
     if (tid == nthreads - 1) prefix[B] = run;
     __syncthreads();
 }
 
+// Largest b in [0, B) with prefix[b] <= t (the request owning tile t).
+__device__ __forceinline__ int request_of_tile(const int* prefix, int B, int t) {
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (prefix[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// One warp merges the partial records of request b, query head qh: records
+// b + c for the CTAs c in [c0, c1] that own tiles.
 template <typename T, int D>
-__global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_split_kernel(const DecodeParams p) {
-    using S = DecodeShape<T, D>;
+__device__ void merge_head(const DecodeParams& p, int b, int qh, int c0, int c1, int G, int total, int lane) {
+    const int n = c1 - c0 + 1;
+    const int64_t first = (int64_t)b + c0;
+    float mx = -INFINITY;
+    for (int k = lane; k < n; k += 32)
+        if (cta_owns_tiles(c0 + k, G, total)) mx = fmaxf(mx, __ldcg(p.lse + (first + k) * p.q_heads + qh));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    constexpr int kDims = (D + 31) / 32;
+    float acc[kDims];
+#pragma unroll
+    for (int i = 0; i < kDims; ++i) acc[i] = 0.f;
+    float wsum = 0.f;
+    for (int base = 0; base < n; base += 32) {
+        float w = 0.f;
+        if (base + lane < n && mx != -INFINITY && cta_owns_tiles(c0 + base + lane, G, total)) {
+            const float lse = __ldcg(p.lse + (first + base + lane) * p.q_heads + qh);
+            w = (lse == -INFINITY) ? 0.f : exp2f(lse - mx);
+        }
+        const int count = min(32, n - base);
+        for (int k = 0; k < count; ++k) {
+            const float wk = __shfl_sync(0xffffffffu, w, k);
+            wsum += wk;
+            if (wk == 0.f) continue;
+            const float* part = p.partial + ((first + base + k) * p.q_heads + qh) * D;
+#pragma unroll
+            for (int i = 0; i < kDims; ++i) {
+                const int d = lane + 32 * i;
+                if (d < D) acc[i] = fmaf(wk, __ldcg(part + d), acc[i]);
+            }
+        }
+    }
+    T* out = static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh) * D;
+#pragma unroll
+    for (int i = 0; i < kDims; ++i) {
+        const int d = lane + 32 * i;
+        if (d < D) out[d] = Elem<T>::from_float(wsum > 0.f ? acc[i] / wsum : 0.f);
+    }
+}
+
+template <typename T, int D>
+struct CoreShape {
+    static constexpr int E = Elem<T>::kPerVec;           // elements per 16 B
+    static constexpr int VR = D / E;                      // vectors per head row
+    static constexpr int LPT = (VR % 8 == 0) ? 8 : (VR % 4 == 0) ? 4 : 2;  // lanes per token
+    static constexpr int VPL = VR / LPT;                  // vectors per lane
+    static constexpr int TPI = 32 / LPT;                  // lane groups (tokens in flight)
+    static constexpr int SC = kTokensPerGroup * TPI;      // tokens per sub-chunk
+    static_assert(VR % LPT == 0 && VR >= 2, "unsupported head_dim for this dtype");
+};
+
+// ------------------------------------------------------- CUDA-core consumer
+// Lane group g (LPT lanes) handles tokens g, g+TPI, ... of each sub-chunk with
+// its own online softmax; groups merge when the segment ends.
+template <typename T, int D>
+struct CoreConsumer {
+    using S = CoreShape<T, D>;
+    static constexpr int kSubTokens = S::SC;
+    float qf[kCoreHeads][S::VPL][S::E];
+    float acc[kCoreHeads][S::VPL][S::E];
+    float m[kCoreHeads], l[kCoreHeads];
+    int g, lj;
+
+    __device__ void setup(int lane) {
+        g = lane / S::LPT;
+        lj = lane % S::LPT;
+    }
+
+    __device__ void begin(const T* qrows, int item_heads) {
+#pragma unroll
+        for (int h = 0; h < kCoreHeads; ++h) {
+            const uint4* qrow = reinterpret_cast<const uint4*>(qrows + min(h, item_heads - 1) * D);
+#pragma unroll
+            for (int v = 0; v < S::VPL; ++v) {
+                Elem<T>::load(qrow[lj + v * S::LPT], qf[h][v]);
+#pragma unroll
+                for (int e = 0; e < S::E; ++e) acc[h][v][e] = 0.f;
+            }
+            m[h] = -INFINITY;
+            l[h] = 0.f;
+        }
+    }
+
+    __device__ void tile(const unsigned char* ks, const unsigned char* vs, int stride, int TT, int n,
+                         uint64_t mask, float scale_log2) {
+        for (int sub = 0; sub < TT; sub += S::SC) {
+            float s[kTokensPerGroup][kCoreHeads];
+            bool ok[kTokensPerGroup];
+#pragma unroll
+            for (int i = 0; i < kTokensPerGroup; ++i) {
+                const int j = sub + i * S::TPI + g;
+                ok[i] = j < n && ((mask >> j) & 1ull);
+                float dot[kCoreHeads];
+#pragma unroll
+                for (int h = 0; h < kCoreHeads; ++h) dot[h] = 0.f;
+                if (ok[i]) {
+                    const uint4* row = reinterpret_cast<const uint4*>(ks + j * stride);
+#pragma unroll
+                    for (int v = 0; v < S::VPL; ++v) {
+                        float f[S::E];
+                        Elem<T>::load(row[lj + v * S::LPT], f);
+#pragma unroll
+                        for (int h = 0; h < kCoreHeads; ++h)
+#pragma unroll
+                            for (int e = 0; e < S::E; ++e) dot[h] = fmaf(qf[h][v][e], f[e], dot[h]);
+                    }
+                }
+#pragma unroll
+                for (int off = 1; off < S::LPT; off <<= 1)
+#pragma unroll
+                    for (int h = 0; h < kCoreHeads; ++h) dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], off);
+#pragma unroll
+                for (int h = 0; h < kCoreHeads; ++h) s[i][h] = ok[i] ? dot[h] * scale_log2 : -INFINITY;
+            }
+            float pr[kTokensPerGroup][kCoreHeads];
+#pragma unroll
+            for (int h = 0; h < kCoreHeads; ++h) {
+                float mt = s[0][h];
+#pragma unroll
+                for (int i = 1; i < kTokensPerGroup; ++i) mt = fmaxf(mt, s[i][h]);
+                const float mn = fmaxf(m[h], mt);
+                float alpha = 1.f, sum = 0.f;
+                if (mn != -INFINITY) {
+                    alpha = exp2f(m[h] - mn);
+#pragma unroll
+                    for (int i = 0; i < kTokensPerGroup; ++i) {
+                        pr[i][h] = exp2f(s[i][h] - mn);
+                        sum += pr[i][h];
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < kTokensPerGroup; ++i) pr[i][h] = 0.f;
+                }
+                l[h] = l[h] * alpha + sum;
+                m[h] = mn;
+#pragma unroll
+                for (int v = 0; v < S::VPL; ++v)
+#pragma unroll
+                    for (int e = 0; e < S::E; ++e) acc[h][v][e] *= alpha;
+            }
+#pragma unroll
+            for (int i = 0; i < kTokensPerGroup; ++i) {
+                if (!ok[i]) continue;
+                const int j = sub + i * S::TPI + g;
+                const uint4* row = reinterpret_cast<const uint4*>(vs + j * stride);
+#pragma unroll
+                for (int v = 0; v < S::VPL; ++v) {
+                    float f[S::E];
+                    Elem<T>::load(row[lj + v * S::LPT], f);
+#pragma unroll
+                    for (int h = 0; h < kCoreHeads; ++h)
+#pragma unroll
+                        for (int e = 0; e < S::E; ++e) acc[h][v][e] = fmaf(pr[i][h], f[e], acc[h][v][e]);
+                }
+            }
+        }
+    }
+
+    // Merge lane groups, normalise, write the final row or the partial record.
+    __device__ void finish(const DecodeParams& p, int b, int qh0, int item_heads, bool final_row, int64_t record) {
+#pragma unroll
+        for (int h = 0; h < kCoreHeads; ++h) {
+            float mx = m[h];
+#pragma unroll
+            for (int off = S::LPT; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float f = (m[h] == -INFINITY) ? 0.f : exp2f(m[h] - mx);
+            float L = l[h] * f;
+#pragma unroll
+            for (int off = S::LPT; off < 32; off <<= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+#pragma unroll
+            for (int v = 0; v < S::VPL; ++v)
+#pragma unroll
+                for (int e = 0; e < S::E; ++e) {
+                    float a = acc[h][v][e] * f;
+#pragma unroll
+                    for (int off = S::LPT; off < 32; off <<= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
+                    acc[h][v][e] = (L > 0.f) ? a / L : 0.f;
+                }
+            if (g != 0 || h >= item_heads) continue;
+            const int qh = qh0 + h;
+            if (final_row) {
+                uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh) * D);
+#pragma unroll
+                for (int v = 0; v < S::VPL; ++v) orow[lj + v * S::LPT] = Elem<T>::store(acc[h][v]);
+            } else {
+                float4* prow = reinterpret_cast<float4*>(p.partial + (record * p.q_heads + qh) * D);
+#pragma unroll
+                for (int v = 0; v < S::VPL; ++v)
+#pragma unroll
+                    for (int e = 0; e < S::E; e += 4)
+                        prow[((lj + v * S::LPT) * S::E + e) / 4] =
+                            make_float4(acc[h][v][e], acc[h][v][e + 1], acc[h][v][e + 2], acc[h][v][e + 3]);
+                if (lj == 0) p.lse[record * p.q_heads + qh] = (L > 0.f) ? mx + log2f(L) : -INFINITY;
+            }
+        }
+    }
+};
+
+}  // namespace minikv
+
+#include "decode_mma.cu"
+
+namespace minikv {
+
+// -------------------------------------------------------------- the kernel
+template <typename T, int D, typename Consumer>
+__global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const DecodeParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int warp_sums[kDecodeThreads / 32];
+    __shared__ int last_ticket;
 
-    const int TT = p.tile_tokens, NS = p.stages, row_bytes = p.row_bytes;
-    const int stage_bytes = 2 * TT * row_bytes;
+    const int TT = p.tile_tokens, NS = p.stages, stride = p.row_stride;
+    const int B = p.batch;
+    const int stage_bytes = 2 * TT * stride;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * stage_bytes);
     uint64_t* empty = full + NS;
     uint64_t* masks = empty + NS;
-    int* prefix = reinterpret_cast<int*>(masks + NS);
+    int* window = reinterpret_cast<int*>(masks + NS);    // [kWindowTiles][TT] physical rows (-1: masked)
+    int* prefix = window + kWindowTiles * TT;             // [B + 1]
+    int* lens_s = prefix + B + 1;                         // [B]
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int B = p.batch;
     const int64_t cap = (int64_t)p.table_width * p.block_size;
 
-    tile_prefix(p.lens, B, cap, TT, prefix, warp_sums);
+    tile_prefix(p.lens, B, cap, TT, prefix, lens_s, warp_sums);
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
@@ -141,12 +369,18 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_split_kernel(c
         }
         mbar_init_fence();
     }
-    if (blockIdx.x == 0 && blockIdx.y == 0)
-        for (int i = tid; i <= B; i += blockDim.x) p.prefix_out[i] = prefix[i];
     __syncthreads();
 
     const int total = prefix[B];
     const int G = gridDim.x, c = blockIdx.x;
+    // Requests with no usable tokens get zero rows (reference: count 0 -> 0).
+    if (blockIdx.y == 0 && warp < kConsumerWarps) {
+        for (int b = c; b < B; b += G) {
+            if (lens_s[b] != 0) continue;
+            T* row = static_cast<T*>(p.out) + (int64_t)b * p.q_heads * D;
+            for (int i = tid; i < p.q_heads * D; i += kConsumerWarps * 32) row[i] = Elem<T>::from_float(0.f);
+        }
+    }
     const int tile_lo = (int)((int64_t)c * total / G), tile_hi = (int)((int64_t)(c + 1) * total / G);
     if (tile_lo >= tile_hi) return;
 
@@ -168,319 +402,143 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_split_kernel(c
         active = warp < nh * cph;
     }
     constexpr int esize = (int)sizeof(T);
-    const int copy_row = nh * D * esize;                    // bytes per token and K|V
-    const int cache_row = p.kv_heads * D * esize;           // global row stride
-    const bool whole_rows = (nh == p.kv_heads);             // CTA rows are contiguous in HBM
-    int b = 0;
-    {   // request containing tile_lo: largest b with prefix[b] <= tile_lo
-        int lo = 0, hi = B - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (prefix[mid] <= tile_lo) lo = mid; else hi = mid - 1;
-        }
-        b = lo;
-    }
+    const int copy_row = nh * D * esize;              // bytes per token and K|V
+    const int cache_row = p.kv_heads * D * esize;     // global row stride
 
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------------ producer
         const uint64_t policy = policy_evict_first();
         const unsigned char* kbase = static_cast<const unsigned char*>(p.kc) + (size_t)h0 * D * esize;
         const unsigned char* vbase = static_cast<const unsigned char*>(p.vc) + (size_t)h0 * D * esize;
+        const uint64_t tile_bits = (TT == 64) ? ~0ull : ((1ull << TT) - 1);
         int gt = 0;
-        for (int t = tile_lo; t < tile_hi;) {
-            while (b + 1 < B && prefix[b + 1] <= t) ++b;
-            const int seg_hi = min(tile_hi, prefix[b + 1]);
-            const int64_t len = p.lens[b];
-            const int64_t* table = p.tables + (p.table_rows ? p.table_rows[b] : (int64_t)b) * p.table_width;
-            for (int k = t - prefix[b]; k < seg_hi - prefix[b]; ++k, ++gt) {
+        for (int w0 = tile_lo; w0 < tile_hi; w0 += kWindowTiles) {
+            // Rows of tiles w0 .. w0+31: lane i resolves tile w0+i, one table
+            // load per page, all lanes' loads in flight together.
+            const int t = w0 + lane;
+            if (t < tile_hi) {
+                const int b = request_of_tile(prefix, B, t);
+                const int k = t - prefix[b];
+                const int64_t t0 = (int64_t)k * TT;
+                const int n = (int)min((int64_t)TT, (int64_t)lens_s[b] - t0);
+                const int64_t* table = p.tables + (p.table_rows ? p.table_rows[b] : (int64_t)b) * p.table_width;
+                int* rows = window + lane * TT;
+                int j = 0;
+                while (j < n) {
+                    const int64_t pos = t0 + j;
+                    const int64_t page = table[pos / p.block_size];
+                    const int in_page = (int)(pos % p.block_size);
+                    const int run = min(n - j, p.block_size - in_page);
+                    const bool ok = page >= 0 && page < p.num_blocks;
+                    const int base = ok ? (int)(page * p.block_size) + in_page : -1;
+                    for (int r = 0; r < run; ++r) rows[j + r] = ok ? base + r : -1;
+                    j += run;
+                }
+                for (; j < TT; ++j) rows[j] = -1;
+            }
+            __syncwarp();
+            const int count = min(kWindowTiles, tile_hi - w0);
+            for (int i = 0; i < count; ++i, ++gt) {
                 const int slot = gt % NS;
                 if (gt >= NS) mbar_wait(&empty[slot], ((gt / NS) - 1) & 1);
-                const int64_t t0 = (int64_t)k * TT;
-                const int n = (int)min((int64_t)TT, len - t0);
-                int64_t rows[2];
+                int row[2];
                 bool ok[2];
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const int j = lane + 32 * h;
-                    ok[h] = false;
-                    rows[h] = 0;
-                    if (j < n) {
-                        const int64_t pos = t0 + j;
-                        const int64_t page = table[pos / p.block_size];
-                        ok[h] = page >= 0 && page < p.num_blocks;
-                        rows[h] = page * p.block_size + pos % p.block_size;
-                    }
+                    row[h] = j < TT ? window[i * TT + j] : -1;
+                    ok[h] = row[h] >= 0;
                 }
                 const uint64_t mask = (uint64_t)__ballot_sync(0xffffffffu, ok[0]) |
                                       ((uint64_t)__ballot_sync(0xffffffffu, ok[1]) << 32);
+                unsigned char* kdst = smem + slot * stage_bytes;
+                unsigned char* vdst = kdst + TT * stride;
+                // Masked V rows must hold finite values (the tensor-core PV
+                // multiplies them by P = 0): zero them with generic stores,
+                // ordered before the consumers' reads by the arrive below.
+                uint64_t holes = ~mask & tile_bits;
+                while (holes) {
+                    const int j = __ffsll((long long)holes) - 1;
+                    holes &= holes - 1;
+                    uint4* vrow = reinterpret_cast<uint4*>(vdst + j * stride);
+                    for (int v = lane; v < copy_row / 16; v += 32) vrow[v] = make_uint4(0, 0, 0, 0);
+                }
+                __syncwarp();
                 if (lane == 0) {
                     masks[slot] = mask;
                     mbar_arrive_expect_tx(&full[slot], (uint32_t)(__popcll(mask) * copy_row * 2));
                 }
                 __syncwarp();
-                unsigned char* kdst = smem + slot * stage_bytes;
-                unsigned char* vdst = kdst + TT * row_bytes;
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                    const int j = lane + 32 * h;
                     if (!ok[h]) continue;
-                    if (whole_rows) {
-                        // one copy per run of valid tokens inside one page
-                        const bool prev_ok = j > 0 && ((mask >> (j - 1)) & 1ull);
-                        const bool page_start = ((t0 + j) % p.block_size) == 0;
-                        if (prev_ok && !page_start) continue;
-                        const int to_page_end = (int)(p.block_size - (t0 + j) % p.block_size);
-                        int end = min(n, j + to_page_end);
-                        const uint64_t above = (j >= 63) ? 0ull : (~0ull << (j + 1));
-                        const uint64_t gaps = ~mask & above;
-                        if (gaps) end = min(end, __ffsll((long long)gaps) - 1);
-                        const uint32_t bytes = (uint32_t)((end - j) * copy_row);
-                        bulk_load(kdst + j * row_bytes, kbase + rows[h] * cache_row, bytes, &full[slot], policy);
-                        bulk_load(vdst + j * row_bytes, vbase + rows[h] * cache_row, bytes, &full[slot], policy);
-                    } else {
-                        bulk_load(kdst + j * row_bytes, kbase + rows[h] * cache_row, copy_row, &full[slot], policy);
-                        bulk_load(vdst + j * row_bytes, vbase + rows[h] * cache_row, copy_row, &full[slot], policy);
-                    }
+                    const int j = lane + 32 * h;
+                    const int64_t r = row[h];
+                    bulk_load(kdst + j * stride, kbase + r * cache_row, copy_row, &full[slot], policy);
+                    bulk_load(vdst + j * stride, vbase + r * cache_row, copy_row, &full[slot], policy);
                 }
             }
-            t = seg_hi;
+            __syncwarp();
         }
         return;
     }
 
     // ---------------------------------------------------------------- consumers
-    const int g = lane / S::LPT, lj = lane % S::LPT;
-    const int item_heads = min(kItemHeads, p.group - chunk * kItemHeads);
+    Consumer cons;
+    cons.setup(lane);
+    const int item_heads = min(p.heads_per_item, p.group - chunk * p.heads_per_item);
     const int local_head = kvh - h0;
-    float qf[kItemHeads][S::VPL][S::E];
-    float acc[kItemHeads][S::VPL][S::E];
-    float m[kItemHeads], l[kItemHeads];
+    const int qh0 = kvh * p.group + chunk * p.heads_per_item;
     int gt = 0;
+    int b = request_of_tile(prefix, B, tile_lo);
     for (int t = tile_lo; t < tile_hi;) {
         while (b + 1 < B && prefix[b + 1] <= t) ++b;
         const int seg_hi = min(tile_hi, prefix[b + 1]);
-        const int64_t len = p.lens[b];
-        if (active) {
-#pragma unroll
-            for (int h = 0; h < kItemHeads; ++h) {
-                const int qh = kvh * p.group + chunk * kItemHeads + min(h, item_heads - 1);
-                const uint4* qrow = reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) +
-                                                                   ((int64_t)b * p.q_heads + qh) * D);
-#pragma unroll
-                for (int v = 0; v < S::VPL; ++v) {
-                    Elem<T>::load(qrow[lj + v * S::LPT], qf[h][v]);
-#pragma unroll
-                    for (int e = 0; e < S::E; ++e) acc[h][v][e] = 0.f;
-                }
-                m[h] = -INFINITY;
-                l[h] = 0.f;
-            }
-        }
+        const int len = lens_s[b];
+        if (active) cons.begin(static_cast<const T*>(p.q) + ((int64_t)b * p.q_heads + qh0) * D, item_heads);
         for (int k = t - prefix[b]; k < seg_hi - prefix[b]; ++k, ++gt) {
             const int slot = gt % NS;
             mbar_wait(&full[slot], (gt / NS) & 1);
             if (active) {
-                const uint64_t mask = masks[slot];
-                const int n = (int)min((int64_t)TT, len - (int64_t)k * TT);
                 const unsigned char* ks = smem + slot * stage_bytes + local_head * D * esize;
-                const unsigned char* vs = ks + TT * row_bytes;
-                for (int sub = 0; sub < TT; sub += S::SC) {
-                    float s[kTokensPerGroup][kItemHeads];
-                    bool ok[kTokensPerGroup];
-#pragma unroll
-                    for (int i = 0; i < kTokensPerGroup; ++i) {
-                        const int j = sub + i * S::TPI + g;
-                        ok[i] = j < n && ((mask >> j) & 1ull);
-                        float dot[kItemHeads];
-#pragma unroll
-                        for (int h = 0; h < kItemHeads; ++h) dot[h] = 0.f;
-                        if (ok[i]) {
-                            const uint4* row = reinterpret_cast<const uint4*>(ks + j * row_bytes);
-#pragma unroll
-                            for (int v = 0; v < S::VPL; ++v) {
-                                float f[S::E];
-                                Elem<T>::load(row[lj + v * S::LPT], f);
-#pragma unroll
-                                for (int h = 0; h < kItemHeads; ++h)
-#pragma unroll
-                                    for (int e = 0; e < S::E; ++e) dot[h] = fmaf(qf[h][v][e], f[e], dot[h]);
-                            }
-                        }
-#pragma unroll
-                        for (int off = 1; off < S::LPT; off <<= 1)
-#pragma unroll
-                            for (int h = 0; h < kItemHeads; ++h)
-                                dot[h] += __shfl_xor_sync(0xffffffffu, dot[h], off);
-#pragma unroll
-                        for (int h = 0; h < kItemHeads; ++h) s[i][h] = ok[i] ? dot[h] * p.scale_log2 : -INFINITY;
-                    }
-                    float pr[kTokensPerGroup][kItemHeads];
-#pragma unroll
-                    for (int h = 0; h < kItemHeads; ++h) {
-                        float mt = s[0][h];
-#pragma unroll
-                        for (int i = 1; i < kTokensPerGroup; ++i) mt = fmaxf(mt, s[i][h]);
-                        const float mn = fmaxf(m[h], mt);
-                        float alpha = 1.f, sum = 0.f;
-                        if (mn != -INFINITY) {
-                            alpha = exp2f(m[h] - mn);
-#pragma unroll
-                            for (int i = 0; i < kTokensPerGroup; ++i) {
-                                pr[i][h] = exp2f(s[i][h] - mn);
-                                sum += pr[i][h];
-                            }
-                        } else {
-#pragma unroll
-                            for (int i = 0; i < kTokensPerGroup; ++i) pr[i][h] = 0.f;
-                        }
-                        l[h] = l[h] * alpha + sum;
-                        m[h] = mn;
-#pragma unroll
-                        for (int v = 0; v < S::VPL; ++v)
-#pragma unroll
-                            for (int e = 0; e < S::E; ++e) acc[h][v][e] *= alpha;
-                    }
-#pragma unroll
-                    for (int i = 0; i < kTokensPerGroup; ++i) {
-                        if (!ok[i]) continue;
-                        const int j = sub + i * S::TPI + g;
-                        const uint4* row = reinterpret_cast<const uint4*>(vs + j * row_bytes);
-#pragma unroll
-                        for (int v = 0; v < S::VPL; ++v) {
-                            float f[S::E];
-                            Elem<T>::load(row[lj + v * S::LPT], f);
-#pragma unroll
-                            for (int h = 0; h < kItemHeads; ++h)
-#pragma unroll
-                                for (int e = 0; e < S::E; ++e) acc[h][v][e] = fmaf(pr[i][h], f[e], acc[h][v][e]);
-                        }
-                    }
-                }
+                cons.tile(ks, ks + TT * stride, stride, TT, min(TT, len - k * TT), masks[slot], p.scale_log2);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
         }
-        if (active) {
-            // Merge the lane groups (each saw every TPI-th token), then write.
-            const bool final_row = cta_of_tile(prefix[b], G, total) == cta_of_tile(prefix[b + 1] - 1, G, total);
-            const int record = b + c;
-#pragma unroll
-            for (int h = 0; h < kItemHeads; ++h) {
-                float mx = m[h];
-#pragma unroll
-                for (int off = S::LPT; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-                const float f = (m[h] == -INFINITY) ? 0.f : exp2f(m[h] - mx);
-                float L = l[h] * f;
-#pragma unroll
-                for (int off = S::LPT; off < 32; off <<= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-#pragma unroll
-                for (int v = 0; v < S::VPL; ++v)
-#pragma unroll
-                    for (int e = 0; e < S::E; ++e) {
-                        float a = acc[h][v][e] * f;
-#pragma unroll
-                        for (int off = S::LPT; off < 32; off <<= 1) a += __shfl_xor_sync(0xffffffffu, a, off);
-                        acc[h][v][e] = (L > 0.f) ? a / L : 0.f;
-                    }
-                if (g == 0 && h < item_heads) {
-                    const int qh = kvh * p.group + chunk * kItemHeads + h;
-                    if (final_row) {
-                        uint4* orow = reinterpret_cast<uint4*>(static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh) * D);
-#pragma unroll
-                        for (int v = 0; v < S::VPL; ++v) orow[lj + v * S::LPT] = Elem<T>::store(acc[h][v]);
-                    } else {
-                        float4* prow = reinterpret_cast<float4*>(p.partial + ((int64_t)record * p.q_heads + qh) * D);
-#pragma unroll
-                        for (int v = 0; v < S::VPL; ++v)
-#pragma unroll
-                            for (int e = 0; e < S::E; e += 4)
-                                prow[((lj + v * S::LPT) * S::E + e) / 4] =
-                                    make_float4(acc[h][v][e], acc[h][v][e + 1], acc[h][v][e + 2], acc[h][v][e + 3]);
-                        if (lj == 0)
-                            p.lse[(int64_t)record * p.q_heads + qh] = (L > 0.f) ? mx + log2f(L) : -INFINITY;
-                    }
-                }
+        const int c0 = cta_of_tile(prefix[b], G, total), c1 = cta_of_tile(prefix[b + 1] - 1, G, total);
+        const bool final_row = c0 == c1;
+        if (active) cons.finish(p, b, qh0, item_heads, final_row, (int64_t)b + c);
+        if (!final_row) {
+            // Ticket: the CTA that completes request b last merges its records.
+            int owners = 0;
+            for (int cc = c0; cc <= c1; ++cc) owners += cta_owns_tiles(cc, G, total) ? 1 : 0;
+            __threadfence();
+            consumers_sync();
+            if (tid == 0) {
+                const unsigned int ticket =
+                    atomicInc(p.tickets + (int64_t)b * gridDim.y + blockIdx.y, (unsigned int)(owners - 1));
+                last_ticket = (ticket == (unsigned int)(owners - 1)) ? 1 : 0;
             }
+            consumers_sync();
+            if (last_ticket) {
+                __threadfence();
+                if (active)
+                    for (int h = 0; h < item_heads; ++h) merge_head<T, D>(p, b, qh0 + h, c0, c1, G, total, lane);
+            }
+            consumers_sync();  // last_ticket is reused by the next segment
         }
         t = seg_hi;
     }
 }
 
-// Merge the partial records of every request that spans several CTAs; write
-// zero rows for requests with no tiles (invalid length).  One warp per
-// (request, query head).
-template <typename T>
-__global__ void __launch_bounds__(256) paged_decode_combine_kernel(const DecodeParams p, int D, int G) {
-    const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (row >= p.batch * p.q_heads) return;
-    const int b = row / p.q_heads, qh = row % p.q_heads;
-    const int* prefix = p.prefix_out;
-    const int total = prefix[p.batch];
-    const int t0 = prefix[b], t1 = prefix[b + 1];
-    T* out = static_cast<T*>(p.out) + (int64_t)row * D;
-    if (t1 == t0) {
-        for (int d = lane; d < D; d += 32) out[d] = Elem<T>::from_float(0.f);
-        return;
-    }
-    const int c0 = cta_of_tile(t0, G, total), c1 = cta_of_tile(t1 - 1, G, total);
-    if (c0 == c1) return;  // a single CTA wrote the final row
-    const int n = c1 - c0 + 1;
-    const int64_t first = (int64_t)b + c0;
-    // CTAs whose tile range is empty (grid larger than the batch's tile count)
-    // wrote no record: their weight is zero.
-    auto owns_tiles = [&](int k) {
-        const int64_t cta = c0 + k;
-        return (cta * total) / G != ((cta + 1) * total) / G;
-    };
-    float mx = -INFINITY;
-    for (int k = lane; k < n; k += 32)
-        if (owns_tiles(k)) mx = fmaxf(mx, p.lse[(first + k) * p.q_heads + qh]);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    constexpr int kMaxDimsPerLane = 8;  // D <= 256
-    float acc[kMaxDimsPerLane];
-#pragma unroll
-    for (int i = 0; i < kMaxDimsPerLane; ++i) acc[i] = 0.f;
-    float wsum = 0.f;
-    for (int base = 0; base < n; base += 32) {
-        float w = 0.f;
-        if (base + lane < n && mx != -INFINITY && owns_tiles(base + lane)) {
-            const float lse = p.lse[(first + base + lane) * p.q_heads + qh];
-            w = (lse == -INFINITY) ? 0.f : exp2f(lse - mx);
-        }
-        const int count = min(32, n - base);
-        for (int k = 0; k < count; ++k) {
-            const float wk = __shfl_sync(0xffffffffu, w, k);
-            wsum += wk;
-            if (wk == 0.f) continue;
-            const float* part = p.partial + ((first + base + k) * p.q_heads + qh) * D;
-#pragma unroll
-            for (int i = 0; i < kMaxDimsPerLane; ++i) {
-                const int d = lane + 32 * i;
-                if (d < D) acc[i] = fmaf(wk, part[d], acc[i]);
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < kMaxDimsPerLane; ++i) {
-        const int d = lane + 32 * i;
-        if (d < D) out[d] = Elem<T>::from_float(wsum > 0.f ? acc[i] / wsum : 0.f);
-    }
-}
-
-}  // namespace minikv
-
-#include "decode_mma.cu"
-
-namespace minikv {
-
 // ------------------------------------------------------------------ host side
 struct DecodePlan {
     bool mma;
-    int tile_tokens, stages, row_bytes, heads_per_cta, chunks_per_head, chunk_groups, head_groups;
+    int tile_tokens, stages, row_stride, heads_per_item, heads_per_cta, chunks_per_head, chunk_groups,
+        head_groups;
     int grid, smem_bytes;
-    int64_t records, ws_prefix, ws_lse, ws_partial, ws_bytes;
+    int64_t records, ws_tickets, ws_lse, ws_partial, ws_bytes;
 };
 
 static int esize_of(int dtype) { return dtype == 0 ? 4 : 2; }
@@ -493,15 +551,12 @@ static int lanes_per_token(int D, int esize) {
 static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
 // Everything here depends on shapes and the device only (graph-static).
-// fp16/bf16 use the tensor-core consumer (decode_mma.cu): warps own up to 16
-// query heads, shared-memory rows are padded by 16 bytes and tiles are
-// multiples of 16 tokens.  fp32 uses the CUDA-core consumer above.
 static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t block_size,
                              int64_t table_width, int dtype, int sm_count, DecodePlan* plan) {
     const int es = esize_of(dtype);
     const bool mma = dtype != 0;
     const int sc = mma ? 16 : kTokensPerGroup * (32 / lanes_per_token((int)D, es));
-    const int heads_per_item = mma ? 16 : kItemHeads;
+    const int heads_per_item = mma ? kMmaHeads : kCoreHeads;
     const int64_t group = Hq / Hkv;
     const int cph = (int)((group + heads_per_item - 1) / heads_per_item);
     int hpc, ncg, z;
@@ -515,13 +570,14 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
         ncg = 1;
         z = (int)((Hkv + hpc - 1) / hpc);
     }
-    const int row = hpc * (int)D * es + (mma ? 16 : 0);  // shared-memory row stride
-    int tt = (32768 / row) / sc * sc;
+    // Padding by 16 bytes makes (stride / 16) odd: ldmatrix rows hit distinct banks.
+    const int stride = hpc * (int)D * es + 16;
+    int tt = (32768 / stride) / sc * sc;
     tt = std::max(sc, std::min(64, tt));
-    const int stage = 2 * tt * row;
-    const int fixed = (int)((B + 1) * 4) + 128;
-    const int max_smem = 232448 - 1024;  // opt-in limit per block, minus static smem
-    int stages = std::min(4, (196608 + 4096) / stage);
+    const int stage = 2 * tt * stride;
+    const int fixed = kWindowTiles * tt * 4 + (int)(2 * B + 1) * 4 + 128;
+    const int max_smem = 232448 - 1024;  // opt-in limit per block, minus static shared memory
+    int stages = std::min(4, (196608 + 8192) / stage);
     while (stages > 1 && stages * (stage + 24) + fixed > max_smem) --stages;
     if (stages < 1 || stages * (stage + 24) + fixed > max_smem) return false;
     const int smem = stages * (stage + 24) + fixed;
@@ -532,7 +588,8 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
     plan->mma = mma;
     plan->tile_tokens = tt;
     plan->stages = stages;
-    plan->row_bytes = row;
+    plan->row_stride = stride;
+    plan->heads_per_item = heads_per_item;
     plan->heads_per_cta = hpc;
     plan->chunks_per_head = cph;
     plan->chunk_groups = ncg;
@@ -540,36 +597,20 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
     plan->grid = (int)grid;
     plan->smem_bytes = smem;
     plan->records = B + grid - 1;
-    plan->ws_prefix = 0;
-    plan->ws_lse = align256((B + 1) * 4);
+    plan->ws_tickets = 0;
+    plan->ws_lse = align256(B * z * 4);
     plan->ws_partial = plan->ws_lse + align256(plan->records * Hq * 4);
     plan->ws_bytes = plan->ws_partial + align256(plan->records * Hq * D * 4);
     return true;
 }
 
-template <typename Kernel>
-static cudaError_t set_smem(Kernel kernel, int bytes) {
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-}
-
 template <typename T, int D>
 static cudaError_t launch_decode_typed(const DecodeParams& p, const DecodePlan& plan, cudaStream_t stream) {
-    cudaError_t err;
-    if constexpr (sizeof(T) == 2) {
-        auto kernel = paged_decode_mma_kernel<T, D>;
-        err = set_smem(kernel, plan.smem_bytes);
-        if (err != cudaSuccess) return err;
-        kernel<<<dim3(plan.grid, plan.head_groups), kDecodeThreads, plan.smem_bytes, stream>>>(p);
-    } else {
-        auto kernel = paged_decode_split_kernel<T, D>;
-        err = set_smem(kernel, plan.smem_bytes);
-        if (err != cudaSuccess) return err;
-        kernel<<<dim3(plan.grid, plan.head_groups), kDecodeThreads, plan.smem_bytes, stream>>>(p);
-    }
-    err = cudaGetLastError();
+    using Consumer = typename std::conditional<sizeof(T) == 2, MmaConsumer<T, D>, CoreConsumer<T, D>>::type;
+    auto kernel = paged_decode_kernel<T, D, Consumer>;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.smem_bytes);
     if (err != cudaSuccess) return err;
-    const int rows = p.batch * p.q_heads;
-    paged_decode_combine_kernel<T><<<(rows + 7) / 8, 256, 0, stream>>>(p, D, plan.grid);
+    kernel<<<dim3(plan.grid, plan.head_groups), kDecodeThreads, plan.smem_bytes, stream>>>(p);
     return cudaGetLastError();
 }
 
@@ -595,6 +636,42 @@ static cudaError_t launch_decode(int dtype, int D, const DecodeParams& p, const 
     return launch_decode_dim<__nv_bfloat16>(D, p, plan, stream);
 }
 
+// Fill DecodeParams from a plan; `tickets`, `lse` and `partial` point into the
+// scratch memory `ws` laid out by the plan.
+static DecodeParams decode_params(const void* query, const void* key_cache, const void* value_cache,
+                                  const int64_t* block_tables, const int64_t* context_lens,
+                                  const int64_t* table_rows, void* out, unsigned char* ws, int64_t batch,
+                                  int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
+                                  int64_t block_size, int64_t table_width, const DecodePlan& plan) {
+    DecodeParams p{};
+    p.q = query;
+    p.kc = key_cache;
+    p.vc = value_cache;
+    p.tables = block_tables;
+    p.lens = context_lens;
+    p.table_rows = table_rows;
+    p.out = out;
+    p.tickets = reinterpret_cast<unsigned int*>(ws + plan.ws_tickets);
+    p.lse = reinterpret_cast<float*>(ws + plan.ws_lse);
+    p.partial = reinterpret_cast<float*>(ws + plan.ws_partial);
+    p.batch = (int)batch;
+    p.q_heads = (int)q_heads;
+    p.kv_heads = (int)kv_heads;
+    p.num_blocks = (int)std::min<int64_t>(num_blocks, 2147483647);
+    p.block_size = (int)block_size;
+    p.table_width = (int)table_width;
+    p.group = (int)(q_heads / kv_heads);
+    p.heads_per_item = plan.heads_per_item;
+    p.chunks_per_head = plan.chunks_per_head;
+    p.heads_per_cta = plan.heads_per_cta;
+    p.chunk_groups = plan.chunk_groups;
+    p.tile_tokens = plan.tile_tokens;
+    p.stages = plan.stages;
+    p.row_stride = plan.row_stride;
+    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+    return p;
+}
+
 static int run_decode(const void* query, const void* key_cache, const void* value_cache,
                       const int64_t* block_tables, const int64_t* context_lens, const int64_t* table_rows,
                       void* out, void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
@@ -605,33 +682,14 @@ static int run_decode(const void* query, const void* key_cache, const void* valu
         return fail(MINIKV_EUNSUPPORTED, "decode shape does not fit shared memory (batch too large?)");
     MINIKV_REQUIRE(workspace != nullptr && workspace_bytes >= plan.ws_bytes && aligned16(workspace),
                    MINIKV_EINVAL, "decode workspace too small or misaligned");
-    DecodeParams p{};
-    p.q = query;
-    p.kc = key_cache;
-    p.vc = value_cache;
-    p.tables = block_tables;
-    p.lens = context_lens;
-    p.table_rows = table_rows;
-    p.out = out;
     unsigned char* ws = static_cast<unsigned char*>(workspace);
-    p.prefix_out = reinterpret_cast<int*>(ws + plan.ws_prefix);
-    p.lse = reinterpret_cast<float*>(ws + plan.ws_lse);
-    p.partial = reinterpret_cast<float*>(ws + plan.ws_partial);
-    p.batch = (int)batch;
-    p.q_heads = (int)q_heads;
-    p.kv_heads = (int)kv_heads;
-    p.num_blocks = (int)std::min<int64_t>(num_blocks, 2147483647);
-    p.block_size = (int)block_size;
-    p.table_width = (int)table_width;
-    p.group = (int)(q_heads / kv_heads);
-    p.chunks_per_head = plan.chunks_per_head;
-    p.heads_per_cta = plan.heads_per_cta;
-    p.chunk_groups = plan.chunk_groups;
-    p.tile_tokens = plan.tile_tokens;
-    p.stages = plan.stages;
-    p.row_bytes = plan.row_bytes;
-    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
-    cudaError_t err = launch_decode(dtype, (int)head_dim, p, plan, stream);
+    // Tickets start at zero on every call (the kernel also leaves them zero).
+    cudaError_t err = cudaMemsetAsync(ws + plan.ws_tickets, 0, (size_t)batch * plan.head_groups * 4, stream);
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_decode ticket reset");
+    const DecodeParams p = decode_params(query, key_cache, value_cache, block_tables, context_lens, table_rows,
+                                         out, ws, batch, q_heads, kv_heads, head_dim, num_blocks, block_size,
+                                         table_width, plan);
+    err = launch_decode(dtype, (int)head_dim, p, plan, stream);
     if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_decode launch");
     return MINIKV_OK;
 }

@@ -1,24 +1,22 @@
-// Tensor-core consumer for the split-KV decode (fp16 / bf16).
+// Tensor-core consumer of the split-KV decode kernel (fp16 / bf16).
 //
-// Same work decomposition, producer protocol, records and merge as
-// paged_decode_split_kernel (decode.cu); only the per-tile math differs.  A
-// consumer warp owns one kv head and up to 16 of its query heads and runs the
-// tile on the tensor cores with mma.sync m16n8k16 (fp32 accumulate):
-//   S[16 heads x 8 tokens]  = Q[16 x 16 dims] . K^T      (K rows via ldmatrix)
-//   O[16 heads x D]        += P[16 x 16 tokens] . V      (V rows via ldmatrix.trans)
-// The GQA heads of one kv head form the M rows, so every K/V byte staged in
-// shared memory is read once per kv head.  Softmax runs on the S fragments in
-// registers (row max / sum across the 4-lane quad); P is rounded to the input
-// type for the PV product, as in FlashAttention.  Shared-memory token rows are
-// padded by 16 bytes (row stride / 16 is odd) so ldmatrix is bank-conflict
-// free; the producer therefore copies each token row with its own bulk copy
-// and zero-fills the V rows of masked tokens (the MMA multiplies them by P=0,
-// which must not meet a NaN bit pattern left in shared memory).
+// A consumer warp owns one kv head and up to 8 of its query heads.  Each
+// 16-token slice of a staged tile runs on the tensor cores with mma.sync
+// m16n8k16 (fp32 accumulate) in the transposed form, tokens as the M rows and
+// the GQA query heads as the N columns:
+//   S^T[16 tokens x 8 heads]  = K[16 x 16 dims] . Q^T          (A = K via ldmatrix)
+//   O^T[16 dims x 8 heads]   += V^T[16 dims x 16 tokens] . P^T (A = V via ldmatrix.trans)
+// so a slice costs D/16 + D/16 MMAs whatever the group size (<= 8), every K/V
+// byte staged in shared memory is read once per kv head, and the Q operand
+// (16 registers for D=128) and the O accumulators (32) stay small.  Softmax
+// runs on the S^T fragments: the max and sum of a head are reductions across
+// the 8 lanes that share its column.  P is rounded to the input type, packed
+// and moved into the B-operand layout with four shuffles.  Token rows in
+// shared memory are padded (stride / 16 odd), so ldmatrix is bank-conflict
+// free; masked tokens' V rows are zero (see the producer).
 #include "common.cuh"
 
 namespace minikv {
-
-constexpr int kMmaHeads = 16;  // query heads per consumer warp (M rows of the MMA)
 
 template <typename T> struct MmaType;
 template <> struct MmaType<__half> {
@@ -42,299 +40,154 @@ template <> struct MmaType<__nv_bfloat16> {
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t* r) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
-                 : "=r"(r[0]), "=r"(r[1]) : "r"(addr));
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr) : "memory");
 }
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t* r) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr) : "memory");
+}
+
+// Low or high 16-bit half of x (selected by `high`) into the low half of the
+// result, and the same half of y into the high half.
+__device__ __forceinline__ uint32_t pick_halves(uint32_t x, uint32_t y, bool high) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(y), "r"(high ? 0x7632u : 0x5410u));
+    return r;
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_mma_kernel(const DecodeParams p) {
+struct MmaConsumer {
     static_assert(D % 16 == 0, "head_dim must be a multiple of 16");
-    constexpr int KSTEPS = D / 16;  // k-steps of the QK product
-    constexpr int NTILES = D / 8;   // n-tiles of the PV product
-    extern __shared__ __align__(128) unsigned char smem[];
-    __shared__ int warp_sums[kDecodeThreads / 32];
-
-    const int TT = p.tile_tokens, NS = p.stages, stride = p.row_bytes;
-    const int stage_bytes = 2 * TT * stride;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * stage_bytes);
-    uint64_t* empty = full + NS;
-    uint64_t* masks = empty + NS;
-    int* prefix = reinterpret_cast<int*>(masks + NS);
-
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int B = p.batch;
-    const int64_t cap = (int64_t)p.table_width * p.block_size;
-
-    tile_prefix(p.lens, B, cap, TT, prefix, warp_sums);
-    if (tid == 0) {
-        for (int s = 0; s < NS; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kConsumerWarps);
-        }
-        mbar_init_fence();
-    }
-    if (blockIdx.x == 0 && blockIdx.y == 0)
-        for (int i = tid; i <= B; i += blockDim.x) p.prefix_out[i] = prefix[i];
-    __syncthreads();
-
-    const int total = prefix[B];
-    const int G = gridDim.x, c = blockIdx.x;
-    const int tile_lo = (int)((int64_t)c * total / G), tile_hi = (int)((int64_t)(c + 1) * total / G);
-    if (tile_lo >= tile_hi) return;
-
-    const int cph = p.chunks_per_head;  // chunks of kMmaHeads query heads per kv head
-    int h0, nh, kvh, chunk;
-    bool active;
-    if (cph >= kConsumerWarps) {
-        h0 = blockIdx.y / p.chunk_groups;
-        nh = 1;
-        kvh = h0;
-        chunk = (blockIdx.y % p.chunk_groups) * kConsumerWarps + warp;
-        active = chunk < cph;
-    } else {
-        h0 = blockIdx.y * p.heads_per_cta;
-        nh = min(p.heads_per_cta, p.kv_heads - h0);
-        kvh = h0 + warp / cph;
-        chunk = warp % cph;
-        active = warp < nh * cph;
-    }
-    constexpr int esize = 2;
-    const int copy_row = nh * D * esize;
-    const int cache_row = p.kv_heads * D * esize;
-    int b = 0;
-    {
-        int lo = 0, hi = B - 1;
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (prefix[mid] <= tile_lo) lo = mid; else hi = mid - 1;
-        }
-        b = lo;
-    }
-
-    if (warp == kConsumerWarps) {
-        // ------------------------------------------------------------ producer
-        const uint64_t policy = policy_evict_first();
-        const unsigned char* kbase = static_cast<const unsigned char*>(p.kc) + (size_t)h0 * D * esize;
-        const unsigned char* vbase = static_cast<const unsigned char*>(p.vc) + (size_t)h0 * D * esize;
-        int gt = 0;
-        for (int t = tile_lo; t < tile_hi;) {
-            while (b + 1 < B && prefix[b + 1] <= t) ++b;
-            const int seg_hi = min(tile_hi, prefix[b + 1]);
-            const int64_t len = p.lens[b];
-            const int64_t* table = p.tables + (p.table_rows ? p.table_rows[b] : (int64_t)b) * p.table_width;
-            for (int k = t - prefix[b]; k < seg_hi - prefix[b]; ++k, ++gt) {
-                const int slot = gt % NS;
-                if (gt >= NS) mbar_wait(&empty[slot], ((gt / NS) - 1) & 1);
-                const int64_t t0 = (int64_t)k * TT;
-                const int n = (int)min((int64_t)TT, len - t0);
-                int64_t rows[2];
-                bool ok[2];
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int j = lane + 32 * h;
-                    ok[h] = false;
-                    rows[h] = 0;
-                    if (j < n) {
-                        const int64_t pos = t0 + j;
-                        const int64_t page = table[pos / p.block_size];
-                        ok[h] = page >= 0 && page < p.num_blocks;
-                        rows[h] = page * p.block_size + pos % p.block_size;
-                    }
-                }
-                const uint64_t mask = (uint64_t)__ballot_sync(0xffffffffu, ok[0]) |
-                                      ((uint64_t)__ballot_sync(0xffffffffu, ok[1]) << 32);
-                unsigned char* kdst = smem + slot * stage_bytes;
-                unsigned char* vdst = kdst + TT * stride;
-                // Masked V rows must hold finite values: zero them (generic stores,
-                // ordered before the consumers' reads by the arrive below).
-                const uint64_t tile_bits = (TT == 64) ? ~0ull : ((1ull << TT) - 1);
-                uint64_t holes = ~mask & tile_bits;
-                while (holes) {
-                    const int j = __ffsll((long long)holes) - 1;
-                    holes &= holes - 1;
-                    uint4* row = reinterpret_cast<uint4*>(vdst + j * stride);
-                    for (int v = lane; v < copy_row / 16; v += 32) row[v] = make_uint4(0, 0, 0, 0);
-                }
-                __syncwarp();
-                if (lane == 0) {
-                    masks[slot] = mask;
-                    mbar_arrive_expect_tx(&full[slot], (uint32_t)(__popcll(mask) * copy_row * 2));
-                }
-                __syncwarp();
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int j = lane + 32 * h;
-                    if (!ok[h]) continue;
-                    bulk_load(kdst + j * stride, kbase + rows[h] * cache_row, copy_row, &full[slot], policy);
-                    bulk_load(vdst + j * stride, vbase + rows[h] * cache_row, copy_row, &full[slot], policy);
-                }
-            }
-            t = seg_hi;
-        }
-        return;
-    }
-
-    // ---------------------------------------------------------------- consumers
+    static constexpr int KSTEPS = D / 16;  // k-steps of S^T = K Q^T
+    static constexpr int MTILES = D / 16;  // m-tiles (16 dims) of O^T
+    static constexpr int esize = 2;
     using Mma = MmaType<T>;
-    const int g = lane >> 2, q4 = lane & 3;
-    const int item_heads = min(kMmaHeads, p.group - chunk * kMmaHeads);
-    const int local_head = kvh - h0;
-    uint32_t qa[KSTEPS][4];   // Q as the A operand, rows = query heads
-    float o[NTILES][4];       // O accumulators: rows g and g+8, dims 8*nd + 2*q4 (+1)
-    float m[2], l[2];         // running max (log2 domain) / partial sum of rows g, g+8
-    int gt = 0;
-    const uint32_t smem_base = smem_addr(smem);
-    // ldmatrix lane addressing (see the fragment layout of m16n8k16)
-    const int ld_row = lane & 7, ld_mat = lane >> 3;
-    for (int t = tile_lo; t < tile_hi;) {
-        while (b + 1 < B && prefix[b + 1] <= t) ++b;
-        const int seg_hi = min(tile_hi, prefix[b + 1]);
-        const int64_t len = p.lens[b];
-        if (active) {
-            const T* qbase = static_cast<const T*>(p.q) + ((int64_t)b * p.q_heads + kvh * p.group + chunk * kMmaHeads) * D;
-            const bool row_lo = g < item_heads, row_hi = g + 8 < item_heads;
+
+    uint32_t qb[KSTEPS][2];  // Q^T as the B operand: head g, dims 16kk + 2*q4 (+1) and +8
+    float o[MTILES][4];      // O^T: dims 16mt + g (e=0,1) / + g + 8 (e=2,3), heads 2*q4 + (e & 1)
+    float m[2], l[2];        // running max (log2 domain) / lane-partial sum of heads 2*q4, 2*q4+1
+    int g, q4, ld_row, ld_mat;
+
+    __device__ void setup(int lane) {
+        g = lane >> 2;
+        q4 = lane & 3;
+        ld_row = lane & 7;   // ldmatrix: row of the 8x8 matrix this lane addresses
+        ld_mat = lane >> 3;  // ... and which of the four matrices
+    }
+
+    __device__ void begin(const T* qrows, int item_heads) {
+        const bool valid = g < item_heads;
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+            const int d0 = 16 * kk + 2 * q4;
+            qb[kk][0] = valid ? *reinterpret_cast<const uint32_t*>(qrows + g * D + d0) : 0u;
+            qb[kk][1] = valid ? *reinterpret_cast<const uint32_t*>(qrows + g * D + d0 + 8) : 0u;
+        }
+#pragma unroll
+        for (int mt = 0; mt < MTILES; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
+        m[0] = m[1] = -INFINITY;
+        l[0] = l[1] = 0.f;
+    }
+
+    __device__ void tile(const unsigned char* kptr, const unsigned char* vptr, int stride, int TT, int n,
+                         uint64_t mask, float scale_log2) {
+        const uint32_t ks = smem_addr(kptr), vs = smem_addr(vptr);
+        // ldmatrix row addresses: K (A, non-transposed) and V (A of O^T, transposed)
+        const int k_tok = ld_row + 8 * (ld_mat & 1), k_dim = 8 * (ld_mat >> 1);
+        const int v_tok = ld_row + 8 * (ld_mat >> 1), v_dim = 8 * (ld_mat & 1);
+        for (int sub = 0; sub < TT; sub += 16) {
+            // ---- S^T = K Q^T, two independent k chains
+            float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t krow = ks + (sub + k_tok) * stride + k_dim * esize;
 #pragma unroll
             for (int kk = 0; kk < KSTEPS; ++kk) {
-                const int d0 = 16 * kk + 2 * q4;
-                qa[kk][0] = row_lo ? *reinterpret_cast<const uint32_t*>(qbase + g * D + d0) : 0u;
-                qa[kk][1] = row_hi ? *reinterpret_cast<const uint32_t*>(qbase + (g + 8) * D + d0) : 0u;
-                qa[kk][2] = row_lo ? *reinterpret_cast<const uint32_t*>(qbase + g * D + d0 + 8) : 0u;
-                qa[kk][3] = row_hi ? *reinterpret_cast<const uint32_t*>(qbase + (g + 8) * D + d0 + 8) : 0u;
+                uint32_t a[4];
+                ldsm_x4(krow + 16 * kk * esize, a);
+                Mma::mma((kk & 1) ? s2 : s, a, qb[kk][0], qb[kk][1]);
             }
+            // ---- mask and scale: s[0,1] is token sub+g, s[2,3] token sub+g+8; columns heads 2q4, 2q4+1
+            const int j0 = sub + g, j1 = j0 + 8;
+            const bool ok0 = j0 < n && ((mask >> j0) & 1ull), ok1 = j1 < n && ((mask >> j1) & 1ull);
+            s[0] = ok0 ? (s[0] + s2[0]) * scale_log2 : -INFINITY;
+            s[1] = ok0 ? (s[1] + s2[1]) * scale_log2 : -INFINITY;
+            s[2] = ok1 ? (s[2] + s2[2]) * scale_log2 : -INFINITY;
+            s[3] = ok1 ? (s[3] + s2[3]) * scale_log2 : -INFINITY;
+            // ---- online softmax per head column (reduce over the 8 lanes with this q4)
+            float alpha[2];
 #pragma unroll
-            for (int nd = 0; nd < NTILES; ++nd)
+            for (int h = 0; h < 2; ++h) {
+                float mx = fmaxf(s[h], s[h + 2]);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float mn = fmaxf(m[h], mx);
+                alpha[h] = (mn == -INFINITY) ? 1.f : exp2f(m[h] - mn);
+                m[h] = mn;
+            }
+            float pv[4];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) o[nd][e] = 0.f;
-            m[0] = m[1] = -INFINITY;
-            l[0] = l[1] = 0.f;
-        }
-        for (int k = t - prefix[b]; k < seg_hi - prefix[b]; ++k, ++gt) {
-            const int slot = gt % NS;
-            mbar_wait(&full[slot], (gt / NS) & 1);
-            if (active) {
-                const uint64_t mask = masks[slot];
-                const int n = (int)min((int64_t)TT, len - (int64_t)k * TT);
-                const uint32_t ks = smem_base + slot * stage_bytes + local_head * D * esize;
-                const uint32_t vs = ks + TT * stride;
-                for (int sub = 0; sub < TT; sub += 16) {
-                    // ---- S = Q K^T for 16 tokens (two n-tiles of 8)
-                    float s[2][4];
+            for (int e = 0; e < 4; ++e) pv[e] = (m[e & 1] == -INFINITY) ? 0.f : exp2f(s[e] - m[e & 1]);
+            l[0] = l[0] * alpha[0] + pv[0] + pv[2];
+            l[1] = l[1] * alpha[1] + pv[1] + pv[3];
+            if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
 #pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) s[nt][e] = 0.f;
-                        const uint32_t krow = ks + (sub + nt * 8 + ld_row) * stride;
-#pragma unroll
-                        for (int kk = 0; kk + 1 < KSTEPS; kk += 2) {
-                            uint32_t r[4];
-                            ldsm_x4(krow + (16 * kk + 8 * ld_mat) * esize, r);
-                            Mma::mma(s[nt], qa[kk], r[0], r[1]);
-                            Mma::mma(s[nt], qa[kk + 1], r[2], r[3]);
-                        }
-                        if (KSTEPS & 1) {
-                            uint32_t r[2];
-                            ldsm_x2(krow + (16 * (KSTEPS - 1) + 8 * (ld_mat & 1)) * esize, r);
-                            Mma::mma(s[nt], qa[KSTEPS - 1], r[0], r[1]);
-                        }
-                    }
-                    // ---- mask, scale, online softmax on rows g (e = 0,1) and g+8 (e = 2,3)
-                    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int j = sub + nt * 8 + 2 * q4 + (e & 1);
-                            const bool ok = j < n && ((mask >> j) & 1ull);
-                            s[nt][e] = ok ? s[nt][e] * p.scale_log2 : -INFINITY;
-                            mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
-                        }
-                    float alpha[2];
-#pragma unroll
-                    for (int r = 0; r < 2; ++r) {
-                        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-                        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-                        const float mn = fmaxf(m[r], mx[r]);
-                        alpha[r] = (mn == -INFINITY) ? 1.f : exp2f(m[r] - mn);
-                        m[r] = mn;
-                    }
-                    uint32_t pa[4];
-                    float psum[2] = {0.f, 0.f};
-#pragma unroll
-                    for (int nt = 0; nt < 2; ++nt) {
-                        float pv[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float mr = m[e >> 1];
-                            pv[e] = (mr == -INFINITY) ? 0.f : exp2f(s[nt][e] - mr);
-                            psum[e >> 1] += pv[e];
-                        }
-                        pa[2 * nt] = Elem<T>::pack(pv[0], pv[1]);
-                        pa[2 * nt + 1] = Elem<T>::pack(pv[2], pv[3]);
-                    }
-                    l[0] = l[0] * alpha[0] + psum[0];
-                    l[1] = l[1] * alpha[1] + psum[1];
-                    if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
-#pragma unroll
-                        for (int nd = 0; nd < NTILES; ++nd) {
-                            o[nd][0] *= alpha[0];
-                            o[nd][1] *= alpha[0];
-                            o[nd][2] *= alpha[1];
-                            o[nd][3] *= alpha[1];
-                        }
-                    }
-                    // ---- O += P V: A = P (tokens 0-7 | 8-15 from the two S n-tiles)
-                    const uint32_t afrag[4] = {pa[0], pa[1], pa[2], pa[3]};
-                    const uint32_t vrow = vs + (sub + ld_row + 8 * (ld_mat & 1)) * stride;
-#pragma unroll
-                    for (int nd = 0; nd < NTILES; nd += 2) {
-                        uint32_t r[4];
-                        ldsm_x4_trans(vrow + (8 * (nd + (ld_mat >> 1))) * esize, r);
-                        Mma::mma(o[nd], afrag, r[0], r[1]);
-                        Mma::mma(o[nd + 1], afrag, r[2], r[3]);
-                    }
+                for (int mt = 0; mt < MTILES; ++mt) {
+                    o[mt][0] *= alpha[0];
+                    o[mt][1] *= alpha[1];
+                    o[mt][2] *= alpha[0];
+                    o[mt][3] *= alpha[1];
                 }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[slot]);
-        }
-        if (active) {
-            const bool final_row = cta_of_tile(prefix[b], G, total) == cta_of_tile(prefix[b + 1] - 1, G, total);
-            const int record = b + c;
+            // ---- P^T into the B layout: lane (g, q4) needs tokens 2q4, 2q4+1 (b0) and
+            // 2q4+8, 2q4+9 (b1) of head g; lane (t, h/2) holds tokens t, t+8 of heads h&~1, h|1.
+            const uint32_t lo = Elem<T>::pack(pv[0], pv[1]);  // token sub+g,   heads 2q4, 2q4+1
+            const uint32_t hi = Elem<T>::pack(pv[2], pv[3]);  // token sub+g+8, heads 2q4, 2q4+1
+            const int src0 = (2 * q4) * 4 + (g >> 1), src1 = src0 + 4;
+            const bool odd = g & 1;
+            const uint32_t b0 = pick_halves(__shfl_sync(0xffffffffu, lo, src0), __shfl_sync(0xffffffffu, lo, src1), odd);
+            const uint32_t b1 = pick_halves(__shfl_sync(0xffffffffu, hi, src0), __shfl_sync(0xffffffffu, hi, src1), odd);
+            // ---- O^T += V^T P^T
+            const uint32_t vrow = vs + (sub + v_tok) * stride + v_dim * esize;
 #pragma unroll
-            for (int r = 0; r < 2; ++r) {
-                float L = l[r];
-                L += __shfl_xor_sync(0xffffffffu, L, 1);
-                L += __shfl_xor_sync(0xffffffffu, L, 2);
-                const int row = g + 8 * r;
-                if (row >= item_heads) continue;
-                const int qh = kvh * p.group + chunk * kMmaHeads + row;
-                const float inv = (L > 0.f) ? 1.f / L : 0.f;
-                if (final_row) {
-                    T* orow = static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh) * D;
-#pragma unroll
-                    for (int nd = 0; nd < NTILES; ++nd)
-                        *reinterpret_cast<uint32_t*>(orow + 8 * nd + 2 * q4) =
-                            Elem<T>::pack(o[nd][2 * r] * inv, o[nd][2 * r + 1] * inv);
-                } else {
-                    float* prow = p.partial + ((int64_t)record * p.q_heads + qh) * D;
-#pragma unroll
-                    for (int nd = 0; nd < NTILES; ++nd)
-                        *reinterpret_cast<float2*>(prow + 8 * nd + 2 * q4) =
-                            make_float2(o[nd][2 * r] * inv, o[nd][2 * r + 1] * inv);
-                    if (q4 == 0)
-                        p.lse[(int64_t)record * p.q_heads + qh] = (L > 0.f) ? m[r] + log2f(L) : -INFINITY;
-                }
+            for (int mt = 0; mt < MTILES; ++mt) {
+                uint32_t a[4];
+                ldsm_x4_trans(vrow + 16 * mt * esize, a);
+                Mma::mma(o[mt], a, b0, b1);
             }
         }
-        t = seg_hi;
     }
-}
+
+    __device__ void finish(const DecodeParams& p, int b, int qh0, int item_heads, bool final_row, int64_t record) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float L = l[h];
+            L += __shfl_xor_sync(0xffffffffu, L, 4);
+            L += __shfl_xor_sync(0xffffffffu, L, 8);
+            L += __shfl_xor_sync(0xffffffffu, L, 16);
+            const int head = 2 * q4 + h;
+            if (head >= item_heads) continue;
+            const int qh = qh0 + head;
+            const float inv = (L > 0.f) ? 1.f / L : 0.f;
+            if (final_row) {
+                T* orow = static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh) * D;
+#pragma unroll
+                for (int mt = 0; mt < MTILES; ++mt) {
+                    orow[16 * mt + g] = Elem<T>::from_float(o[mt][h] * inv);
+                    orow[16 * mt + g + 8] = Elem<T>::from_float(o[mt][h + 2] * inv);
+                }
+            } else {
+                float* prow = p.partial + (record * p.q_heads + qh) * D;
+#pragma unroll
+                for (int mt = 0; mt < MTILES; ++mt) {
+                    prow[16 * mt + g] = o[mt][h] * inv;
+                    prow[16 * mt + g + 8] = o[mt][h + 2] * inv;
+                }
+                if (g == 0) p.lse[record * p.q_heads + qh] = (L > 0.f) ? m[h] + log2f(L) : -INFINITY;
+            }
+        }
+    }
+};
 
 }  // namespace minikv
