@@ -262,14 +262,19 @@ def run_ours(args, world, rank, local):
         return paged_attention(x["query"], x["key_cache"], x["value_cache"], x["block_tables"],
                                x["context_lens"], BS, validate=False)
 
-    for _ in range(3):
-        step()
+    # warm up on the capture stream, so the per-stream decode workspace exists
+    # before capture and its one-time zero fill is not part of the graph
+    capture_stream = torch.cuda.Stream(device)
+    capture_stream.wait_stream(stream)
+    with torch.cuda.stream(capture_stream):
+        for _ in range(3):
+            step()
     torch.cuda.synchronize(device)
     # one step captured as a graph, with external timing events around the decode op
     ev_a = torch.cuda.Event(enable_timing=True, external=True)
     ev_b = torch.cuda.Event(enable_timing=True, external=True)
     graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+    with torch.cuda.graph(graph, stream=capture_stream):
         write_kv_cache_batch(x["key_cache"], x["value_cache"], x["block_tables"], x["token_offsets"], x["key"],
                              x["value"], BS, validate=False)
         ev_a.record()

@@ -60,7 +60,10 @@ int minikv_device_status(unsigned int* status, int clear, void* stream);
  * The number of KV splits depends only on (batch, table_width, block_size,
  * heads, head_dim, dtype) and the device, never on context_lens, so a
  * captured graph stays valid when lengths change.
- * workspace: device scratch of at least minikv_paged_decode_workspace_bytes(). */
+ * workspace: device scratch of at least minikv_paged_decode_workspace_bytes()
+ * bytes, zero-filled before its first use (e.g. one cudaMemset) and then
+ * reused as is: every call leaves the ticket counters it keeps there at zero.
+ * Calls that share a workspace must not overlap on the GPU. */
 int64_t minikv_paged_decode_workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads,
                                             int64_t head_dim, int64_t num_blocks, int64_t block_size,
                                             int64_t table_width, int dtype);

@@ -135,9 +135,12 @@ __device__ __forceinline__ int request_of_tile(const int* prefix, int B, int t) 
 }
 
 // One warp merges the partial records of request b, query head qh: records
-// b + c for the CTAs c in [c0, c1] that own tiles.
+// b + c for the CTAs c in [c0, c1] that own tiles.  Loads of up to eight
+// records are issued together before they are combined.
 template <typename T, int D>
 __device__ void merge_head(const DecodeParams& p, int b, int qh, int c0, int c1, int G, int total, int lane) {
+    constexpr int kBatch = 8;
+    constexpr int kDims = (D + 31) / 32;
     const int n = c1 - c0 + 1;
     const int64_t first = (int64_t)b + c0;
     float mx = -INFINITY;
@@ -145,7 +148,6 @@ __device__ void merge_head(const DecodeParams& p, int b, int qh, int c0, int c1,
         if (cta_owns_tiles(c0 + k, G, total)) mx = fmaxf(mx, __ldcg(p.lse + (first + k) * p.q_heads + qh));
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    constexpr int kDims = (D + 31) / 32;
     float acc[kDims];
 #pragma unroll
     for (int i = 0; i < kDims; ++i) acc[i] = 0.f;
@@ -157,15 +159,26 @@ __device__ void merge_head(const DecodeParams& p, int b, int qh, int c0, int c1,
             w = (lse == -INFINITY) ? 0.f : exp2f(lse - mx);
         }
         const int count = min(32, n - base);
-        for (int k = 0; k < count; ++k) {
-            const float wk = __shfl_sync(0xffffffffu, w, k);
-            wsum += wk;
-            if (wk == 0.f) continue;
-            const float* part = p.partial + ((first + base + k) * p.q_heads + qh) * D;
+        for (int k0 = 0; k0 < count; k0 += kBatch) {
+            float vals[kBatch][kDims];
+            float wk[kBatch];
 #pragma unroll
-            for (int i = 0; i < kDims; ++i) {
-                const int d = lane + 32 * i;
-                if (d < D) acc[i] = fmaf(wk, __ldcg(part + d), acc[i]);
+            for (int u = 0; u < kBatch; ++u) {
+                wk[u] = __shfl_sync(0xffffffffu, w, (k0 + u) & 31);
+                const bool use = k0 + u < count && wk[u] != 0.f;
+                const float* part = p.partial + ((first + base + k0 + u) * p.q_heads + qh) * D;
+#pragma unroll
+                for (int i = 0; i < kDims; ++i) {
+                    const int d = lane + 32 * i;
+                    vals[u][i] = (use && d < D) ? __ldcg(part + d) : 0.f;
+                }
+                if (k0 + u >= count) wk[u] = 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                wsum += wk[u];
+#pragma unroll
+                for (int i = 0; i < kDims; ++i) acc[i] = fmaf(wk[u], vals[u][i], acc[i]);
             }
         }
     }
@@ -683,15 +696,17 @@ static int run_decode(const void* query, const void* key_cache, const void* valu
     MINIKV_REQUIRE(workspace != nullptr && workspace_bytes >= plan.ws_bytes && aligned16(workspace),
                    MINIKV_EINVAL, "decode workspace too small or misaligned");
     unsigned char* ws = static_cast<unsigned char*>(workspace);
-    // Tickets start at zero on every call (the kernel also leaves them zero).
-    cudaError_t err = cudaMemsetAsync(ws + plan.ws_tickets, 0, (size_t)batch * plan.head_groups * 4, stream);
-    if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_decode ticket reset");
+    // The ticket region (the first bytes of the workspace) must be zero when
+    // the kernel starts; every launch leaves it zero again (atomicInc wraps).
     const DecodeParams p = decode_params(query, key_cache, value_cache, block_tables, context_lens, table_rows,
                                          out, ws, batch, q_heads, kv_heads, head_dim, num_blocks, block_size,
                                          table_width, plan);
-    err = launch_decode(dtype, (int)head_dim, p, plan, stream);
+    const cudaError_t err = launch_decode(dtype, (int)head_dim, p, plan, stream);
     if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_decode launch");
     return MINIKV_OK;
 }
+
+// Bytes at the start of a decode workspace that must be zero before its first use.
+static int64_t decode_ticket_bytes(const DecodePlan& plan) { return plan.ws_lse; }
 
 }  // namespace minikv

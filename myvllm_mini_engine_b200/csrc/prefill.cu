@@ -59,6 +59,8 @@ static int run_prefill(const void* q, const void* key_cache, const void* value_c
                                                                      token_len, token_row);
         cudaError_t err = cudaGetLastError();
         if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_prefill token map");
+        err = cudaMemsetAsync(decode_ws, 0, (size_t)decode_ticket_bytes(plan), stream);
+        if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_prefill ticket reset");
         const unsigned char* qn = static_cast<const unsigned char*>(q) + t0 * row_elems * es;
         unsigned char* on = static_cast<unsigned char*>(out) + t0 * row_elems * es;
         int rc = run_decode(qn, key_cache, value_cache, block_tables, token_len, token_row, on, decode_ws,

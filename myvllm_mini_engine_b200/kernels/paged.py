@@ -38,8 +38,11 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
     ``query [B, Hq, D]``, ``key_cache``/``value_cache`` ``[num_blocks, block_size,
     Hkv, D]``, ``block_tables [B, W]`` int64 (-1 padded), ``context_lens [B]`` int64.
     Returns a new ``[B, Hq, D]`` tensor in the query dtype.  ``workspace`` (a
-    uint8 CUDA tensor of at least :func:`workspace_bytes` bytes) may be passed to
-    reuse scratch memory; otherwise it comes from torch's caching allocator.
+    zero-filled uint8 CUDA tensor of at least :func:`workspace_bytes` bytes,
+    reused as is by calls that do not overlap) may be passed; by default each
+    stream gets a buffer kept by this module (see :func:`_workspace`).  Before
+    capturing a CUDA graph, make one call on the capture stream so the buffer
+    exists and its zero fill stays out of the graph.
     """
     check_backend(backend)
     _require(query.is_cuda, "query must be CUDA")
@@ -73,19 +76,49 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
                  "physical block id out of range")
     lib = _lib.load()
     code = _lib.dtype_code(query.dtype)
-    need = lib.minikv_paged_decode_workspace_bytes(batch, heads, kv_heads, dim, num_blocks, block_size, width, code)
-    if need < 0:
-        _lib.check(_lib.EINVAL, "paged_attention")
-    if workspace is None or workspace.numel() < need:
-        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=query.device)
-    out = torch.empty_like(query)
+    key = (batch, heads, kv_heads, dim, num_blocks, block_size, width, code)
+    need = _WS_BYTES.get(key)
+    if need is None:
+        need = lib.minikv_paged_decode_workspace_bytes(*key)
+        if need < 0:
+            _lib.check(_lib.EINVAL, "paged_attention")
+        _WS_BYTES[key] = need
     with torch.cuda.device(query.device):
+        stream = torch.cuda.current_stream(query.device)
+        if workspace is None:
+            workspace = _workspace(query.device, stream, need)
+        elif workspace.numel() < need:
+            raise RuntimeError("decode workspace too small")
+        out = torch.empty_like(query)
         status = lib.minikv_paged_decode(
             query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
             context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
-            batch, heads, kv_heads, dim, num_blocks, block_size, width, code, _lib.stream_of(query.device))
+            batch, heads, kv_heads, dim, num_blocks, block_size, width, code, stream.cuda_stream)
     _lib.check(status, "paged_attention")
     return out
+
+
+_WS_BYTES: dict = {}
+_WORKSPACES: dict = {}
+_RETIRED: list = []
+
+
+def _workspace(device, stream, need):
+    """Zero-filled scratch reused by every decode call on ``stream``.
+
+    The kernel keeps per-request ticket counters in it and leaves them at zero,
+    so it is zeroed once, when allocated.  Calls on one stream never overlap;
+    each stream gets its own buffer.  Buffers are never freed while the process
+    runs, because a captured CUDA graph may still refer to one.
+    """
+    key = (device.index, stream.cuda_stream)
+    buf = _WORKSPACES.get(key)
+    if buf is None or buf.numel() < need:
+        if buf is not None:
+            _RETIRED.append(buf)
+        buf = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = buf
+    return buf
 
 
 def workspace_bytes(query, key_cache, block_tables):
