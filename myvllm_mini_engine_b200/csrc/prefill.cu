@@ -1,6 +1,9 @@
 // Ragged causal paged prefill.
 //
-// CUDA-core route (every dtype / head_dim): each packed query token is turned
+// Tensor-core route (prefill_tc.cu): bf16/fp16, head_dim 64 or 128, GQA group
+// dividing 128, block_size a multiple of 8.
+//
+// CUDA-core route (every other dtype / shape): each packed query token is turned
 // into a one-token "decode request" -- its own query row, the page-table row
 // of its request and the context length start + i + 1 it may attend
 // (prefill.cu:112-123 of the reference computes the same per-token values) --
@@ -8,6 +11,7 @@
 // processed in chunks of kPrefillChunk so the per-launch workspace stays
 // bounded.
 #include "common.cuh"
+#include "prefill_tc.cu"
 
 namespace minikv {
 
@@ -30,6 +34,7 @@ static int64_t prefill_workspace_bytes(int64_t tokens, int64_t requests, int64_t
     (void)requests;
     (void)max_query_len;
     if (tokens <= 0) return 0;
+    if (prefill_tc_supported(q_heads, kv_heads, head_dim, block_size, dtype, 1, tokens)) return 0;
     return prefill_core_workspace(tokens, q_heads, kv_heads, head_dim, block_size, table_width, dtype, sms,
                                   nullptr);
 }
@@ -40,6 +45,10 @@ static int run_prefill(const void* q, const void* key_cache, const void* value_c
                        int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
                        int64_t table_width, int64_t max_query_len, int dtype, cudaStream_t stream) {
     (void)max_query_len;
+    if (prefill_tc_supported(q_heads, kv_heads, head_dim, block_size, dtype, num_blocks, tokens))
+        return run_prefill_tc(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens, out,
+                              tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width,
+                              dtype, stream);
     const int sms = sm_count();
     const int64_t chunk = std::min(tokens, kPrefillChunk);
     unsigned char* ws = static_cast<unsigned char*>(workspace);

@@ -1,0 +1,539 @@
+// Ragged causal paged prefill on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// One CTA computes one 128-row tile of one request for one kv head: the rows
+// are tm = 128 / group consecutive query tokens x the group's query heads
+// (GQA packing, so every K/V tile is loaded once for all query heads that
+// read it).  The CTA walks the request's key tiles of 128 keys, up to the
+// tile's last query position (causal):
+//   S   = Q K^T   tcgen05.mma kind::f16, M=128, N=128, K=D -> TMEM (fp32)
+//   P   = exp2(S * log2(e)/sqrt(D) - rowmax)                 (softmax warps)
+//   O_t = P V     tcgen05.mma, M=128, N=D, K=128           -> TMEM (fp32)
+//   O   = O * alpha + O_t  (registers of the softmax warps; online softmax)
+// Warp roles: warp 0 issues the TMA loads (Q once; the K and V boxes of each
+// key tile straight from the physical pages of the block table, SWIZZLE_128B,
+// two-stage ring), warp 1 owns the TMEM allocation and one of its lanes issues
+// every MMA, warps 2-5 own one TMEM lane (= one row) each for the softmax, the
+// P tile (written to shared memory in the swizzled K-major layout the MMA
+// reads) and the epilogue.  No TMA multicast.
+//
+// Semantics follow the reference kernel (mini_engine/kernels/csrc/prefill.cu:
+// 104-185): row t of request r attends keys [0, start_r + t]; keys on a page
+// id outside [0, num_blocks) are masked; rows whose position falls outside
+// the context or the table get zeros.  Keys past the context and keys of
+// masked pages have their V rows zeroed in shared memory before the PV product.
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace minikv {
+
+constexpr int kPfThreads = 192;  // warp 0 TMA, warp 1 MMA/TMEM, warps 2-5 softmax
+constexpr int kPfRows = 128;     // M rows per CTA (tokens x GQA heads)
+constexpr int kPfKeys = 128;     // keys per tile
+
+struct PrefillTcParams {
+    const int64_t* cu_q;
+    const int64_t* starts;
+    const int64_t* tables;
+    const int64_t* ctx;
+    void* out;
+    int requests, q_heads, group, num_blocks, block_size, table_width;
+    int tm;        // query tokens per tile = 128 / group
+    int box_rows;  // rows per K/V TMA box (divides block_size and 128, >= 8)
+    float scale_log2;
+};
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        ::"r"(smem_addr(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_addr(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                 ::"r"(smem_addr(bar)) : "memory");
+}
+
+// 32 TMEM lanes x 32 columns of 32-bit values: thread i of the warp gets row
+// (lane base + i), columns [col, col + 32).
+__device__ __forceinline__ void tmem_load_32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor, SWIZZLE_128B (sm100 layout code 2), version 1.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = (uint64_t)((addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor of kind::f16 with fp32 accumulate.
+__host__ __device__ constexpr uint32_t umma_idesc(int M, int N, bool bf16, bool b_mn_major) {
+    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((b_mn_major ? 1u : 0u) << 16) |
+           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void softmax_sync() {
+    asm volatile("bar.sync 2, 128;" ::: "memory");
+}
+
+template <typename T, int D>
+struct PfLayout {
+    static constexpr int KB = D / 64;                     // 128-byte K-blocks per row
+    static constexpr int Q_BYTES = kPfRows * D * 2;
+    static constexpr int KV_BYTES = kPfKeys * D * 2;
+    static constexpr int P_BYTES = kPfRows * kPfKeys * 2;
+    static constexpr int BLOCK_BYTES = 128 * 128;         // one K-block of a 128-row operand
+    static constexpr int OFF_K = Q_BYTES;
+    static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
+    static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
+    static constexpr int OFF_BAR = OFF_P + P_BYTES;
+    static constexpr int SMEM = OFF_BAR + 256 + 1024;     // + barriers/flags + alignment slack
+    static constexpr uint32_t TMEM_COLS = (kPfKeys + D) <= 256 ? 256 : 512;
+};
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
+    const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+    const __grid_constant__ CUtensorMap tm_v, const PrefillTcParams p) {
+    using L = PfLayout<T, D>;
+    constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* sQ = smem;
+    unsigned char* sK = smem + L::OFF_K;
+    unsigned char* sV = smem + L::OFF_V;
+    unsigned char* sP = smem + L::OFF_P;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+    uint64_t* q_full = bar + 0;
+    uint64_t* kv_full = bar + 1;   // [2]
+    uint64_t* kv_empty = bar + 3;  // [2]
+    uint64_t* s_full = bar + 5;
+    uint64_t* s_free = bar + 6;
+    uint64_t* p_full = bar + 7;
+    uint64_t* o_full = bar + 8;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 9);
+    int* info = reinterpret_cast<int*>(bar + 10);               // request, tile, valid
+    uint32_t* key_ok = reinterpret_cast<uint32_t*>(bar + 12);   // [2][4] validity bits of a key tile
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int B = p.requests, G = p.group, TM = p.tm;
+    const int h = blockIdx.y;  // kv head
+
+    // ---- which (request, query tile) this CTA computes
+    if (warp == 0) {
+        const int target = blockIdx.x;
+        int run = 0, found = -1, tile = 0;
+        for (int base = 0; base < B && found < 0; base += 32) {
+            const int r = base + lane;
+            int t = 0;
+            if (r < B) t = (int)((p.cu_q[r + 1] - p.cu_q[r] + TM - 1) / TM);
+            if (t < 0) t = 0;
+            int incl = t;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += v;
+            }
+            const bool hit = r < B && t > 0 && run + incl - t <= target && target < run + incl;
+            const unsigned who = __ballot_sync(0xffffffffu, hit);
+            if (who) {
+                const int src = __ffs(who) - 1;
+                found = base + src;
+                tile = target - (run + __shfl_sync(0xffffffffu, incl - t, src));
+            }
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (lane == 0) {
+            info[0] = found;
+            info[1] = tile;
+        }
+    }
+    __syncthreads();
+    const int r = info[0];
+    if (r < 0) return;  // grid is an upper bound on the number of query tiles
+    const int m = info[1];
+
+    const int64_t q0 = p.cu_q[r];
+    const int qlen = (int)(p.cu_q[r + 1] - q0);
+    const int64_t start = p.starts[r];
+    const int64_t cap = (int64_t)p.table_width * p.block_size;
+    const int64_t limit = min(p.ctx[r], cap);  // keys [0, limit) exist
+    const int t_lo = m * TM;
+    const int64_t p_last = min(start + min(t_lo + TM, qlen) - 1, limit - 1);
+    const int n_tiles = (p_last < 0 || start < 0) ? 0 : (int)(p_last / kPfKeys + 1);
+    const int64_t* table = p.tables + (int64_t)r * p.table_width;
+
+    if (tid == 0) {
+        mbar_init(q_full, 1);
+        mbar_init(&kv_full[0], 1);
+        mbar_init(&kv_full[1], 1);
+        mbar_init(&kv_empty[0], 1);
+        mbar_init(&kv_empty[1], 1);
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 4);
+        mbar_init(p_full, 4);
+        mbar_init(o_full, 1);
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                     ::"r"(smem_addr(tmem_slot)), "r"(L::TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (n_tiles > 0) {
+            if (lane == 0) {
+                mbar_arrive_expect_tx(q_full, (uint32_t)L::Q_BYTES);
+#pragma unroll
+                for (int kb = 0; kb < L::KB; ++kb)
+                    tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, h * G, (int)(q0 + t_lo), q_full);
+            }
+            const int R = p.box_rows, groups = kPfKeys / R;
+            for (int j = 0; j < n_tiles; ++j) {
+                const int slot = j & 1;
+                if (j >= 2) mbar_wait(&kv_empty[slot], ((j >> 1) - 1) & 1);
+                // lane gi handles boxes gi, gi + 32, ... (R rows each)
+                uint32_t bytes = 0;
+                for (int gi = lane; gi < groups; gi += 32) {
+                    const int64_t k0 = (int64_t)j * kPfKeys + gi * R;
+                    if (k0 >= limit) continue;
+                    const int64_t page = table[k0 / p.block_size];
+                    if (page < 0 || page >= p.num_blocks) continue;
+                    bytes += (uint32_t)(2 * L::KB * R * 128);
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
+                if (lane == 0) mbar_arrive_expect_tx(&kv_full[slot], bytes);
+                __syncwarp();
+                unsigned char* kdst = sK + slot * L::KV_BYTES;
+                unsigned char* vdst = sV + slot * L::KV_BYTES;
+                for (int gi = lane; gi < groups; gi += 32) {
+                    const int64_t k0 = (int64_t)j * kPfKeys + gi * R;
+                    if (k0 >= limit) continue;
+                    const int64_t page = table[k0 / p.block_size];
+                    if (page < 0 || page >= p.num_blocks) continue;
+                    const int z = (int)(page * p.block_size + k0 % p.block_size);
+#pragma unroll
+                    for (int kb = 0; kb < L::KB; ++kb) {
+                        tma_load_3d(kdst + kb * L::BLOCK_BYTES + gi * R * 128, &tm_k, kb * 64, h, z, &kv_full[slot]);
+                        tma_load_3d(vdst + kb * L::BLOCK_BYTES + gi * R * 128, &tm_v, kb * 64, h, z, &kv_full[slot]);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0 && n_tiles > 0) {
+            constexpr uint32_t idesc_s = umma_idesc(128, kPfKeys, kBf16, false);
+            constexpr uint32_t idesc_o = umma_idesc(128, D, kBf16, true);
+            const uint32_t t_s = tmem, t_o = tmem + kPfKeys;
+            const uint32_t q_addr = smem_addr(sQ), p_addr = smem_addr(sP);
+            mbar_wait(q_full, 0);
+            for (int j = 0; j < n_tiles; ++j) {
+                const int slot = j & 1;
+                mbar_wait(&kv_full[slot], (j >> 1) & 1);
+                if (j > 0) mbar_wait(s_free, (j - 1) & 1);
+                tc_fence_after();
+                const uint32_t k_addr = smem_addr(sK + slot * L::KV_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < D / 16; ++kk) {
+                    const uint32_t off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
+                    umma_f16(t_s, smem_desc(q_addr + off, 16, 1024), smem_desc(k_addr + off, 16, 1024), idesc_s, kk > 0);
+                }
+                umma_commit(s_full);
+                mbar_wait(p_full, j & 1);
+                tc_fence_after();
+                const uint32_t v_addr = smem_addr(sV + slot * L::KV_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < kPfKeys / 16; ++kk) {
+                    const uint32_t a_off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
+                    umma_f16(t_o, smem_desc(p_addr + a_off, 16, 1024),
+                             smem_desc(v_addr + kk * 16 * 128, L::BLOCK_BYTES, 1024), idesc_o, kk > 0);
+                }
+                umma_commit(o_full);
+                umma_commit(&kv_empty[slot]);
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ softmax warps
+        const int quarter = warp & 3;            // TMEM lane quarter of this warp
+        const int row = quarter * 32 + lane;     // tile row = TMEM lane
+        const int st = (warp - 2) * 32 + lane;   // 0..127 for cooperative work
+        const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+        const uint32_t t_s = tmem + lane_base, t_o = tmem + lane_base + kPfKeys;
+        const int t = t_lo + row / G, g = row % G;
+        const int64_t pos = start + t;
+        const bool row_valid = t < qlen && pos < limit;
+        float o_acc[D];
+#pragma unroll
+        for (int d = 0; d < D; ++d) o_acc[d] = 0.f;
+        float mrow = -INFINITY, lrow = 0.f, alpha_prev = 1.f;
+        for (int j = 0; j < n_tiles; ++j) {
+            const int slot = j & 1;
+            uint32_t* ok_words = key_ok + 4 * (j & 1);
+            {   // key validity of this tile: thread st checks key j*128 + st
+                const int64_t key = (int64_t)j * kPfKeys + st;
+                bool ok = key < limit;
+                if (ok) {
+                    const int64_t page = table[key / p.block_size];
+                    ok = page >= 0 && page < p.num_blocks;
+                }
+                const unsigned bits = __ballot_sync(0xffffffffu, ok);
+                if (lane == 0) ok_words[warp - 2] = bits;
+                // V rows of masked keys must be finite zeros before P V runs
+                mbar_wait(&kv_full[slot], (j >> 1) & 1);
+                if (!ok) {
+                    unsigned char* vrow = sV + slot * L::KV_BYTES + st * 128;
+#pragma unroll
+                    for (int kb = 0; kb < L::KB; ++kb) {
+                        uint4* v4 = reinterpret_cast<uint4*>(vrow + kb * L::BLOCK_BYTES);
+#pragma unroll
+                        for (int c = 0; c < 8; ++c) v4[c] = make_uint4(0, 0, 0, 0);
+                    }
+                    fence_async_smem();
+                }
+            }
+            softmax_sync();
+            mbar_wait(s_full, j & 1);
+            tc_fence_after();
+            // pass 1: row max of the masked, scaled scores
+            const int64_t key0 = (int64_t)j * kPfKeys;
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kPfKeys / 32; ++c) {
+                float v[32];
+                tmem_load_32(t_s + c * 32, v);
+                const uint32_t word = ok_words[c];
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    const bool ok = row_valid && ((word >> e) & 1u) && key0 + c * 32 + e <= pos;
+                    mx = fmaxf(mx, ok ? v[e] * p.scale_log2 : -INFINITY);
+                }
+            }
+            const float m_new = fmaxf(mrow, mx);
+            const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(mrow - m_new);
+            // O += previous tile (its PV product is done once o_full flips)
+            if (j > 0) {
+                mbar_wait(o_full, (j - 1) & 1);
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    float v[32];
+                    tmem_load_32(t_o + c * 32, v);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o_acc[c * 32 + e] = fmaf(o_acc[c * 32 + e], alpha_prev, v[e]);
+                }
+            }
+            // pass 2: P = exp2(s - m_new) -> shared memory (K-major, 128B swizzle), row sums
+            float sum = 0.f;
+            unsigned char* prow = sP + row * 128;
+#pragma unroll
+            for (int c = 0; c < kPfKeys / 32; ++c) {
+                float v[32];
+                tmem_load_32(t_s + c * 32, v);
+                const uint32_t word = ok_words[c];
+                uint32_t packed[16];
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                    float pe[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const bool ok = row_valid && ((word >> (e + u)) & 1u) && key0 + c * 32 + e + u <= pos;
+                        pe[u] = (ok && m_new != -INFINITY) ? exp2f(v[e + u] * p.scale_log2 - m_new) : 0.f;
+                        sum += pe[u];
+                    }
+                    packed[e / 2] = Elem<T>::pack(pe[0], pe[1]);
+                }
+                // keys c*32 .. c*32+31: K-block c/2, 16-byte chunks (c%2)*4 .. +3
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int chunk = (c & 1) * 4 + q;
+                    uint4* dst = reinterpret_cast<uint4*>(prow + (c >> 1) * L::BLOCK_BYTES + ((chunk ^ (row & 7)) * 16));
+                    *dst = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+                }
+            }
+            lrow = lrow * alpha + sum;
+            mrow = m_new;
+            alpha_prev = alpha;
+            fence_async_smem();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(s_free);
+                mbar_arrive(p_full);
+            }
+        }
+        if (n_tiles > 0) {
+            mbar_wait(o_full, (n_tiles - 1) & 1);
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < D / 32; ++c) {
+                float v[32];
+                tmem_load_32(t_o + c * 32, v);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) o_acc[c * 32 + e] = fmaf(o_acc[c * 32 + e], alpha_prev, v[e]);
+            }
+        }
+        if (t < qlen) {
+            const float inv = (row_valid && lrow > 0.f) ? 1.f / lrow : 0.f;
+            T* orow = static_cast<T*>(p.out) + ((q0 + t) * p.q_heads + h * G + g) * D;
+#pragma unroll
+            for (int d = 0; d < D; d += 8) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = o_acc[d + e] * inv;
+                *reinterpret_cast<uint4*>(orow + d) = Elem<T>::store(f);
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(L::TMEM_COLS) : "memory");
+    }
+}
+
+// ------------------------------------------------------------------ host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_tiled_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+    return fn;
+}
+
+// 3-D map over [dim2][dim1][dim0] (dim0 innermost, elements of 2 bytes), 128B swizzle.
+static bool encode_map_3d(CUtensorMap* map, const void* base, bool bf16, uint64_t d0, uint64_t d1, uint64_t d2,
+                          uint32_t b0, uint32_t b1, uint32_t b2) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {d0 * 2, d0 * d1 * 2};
+    const cuuint32_t box[3] = {b0, b1, b2};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    return fn(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+              const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int gcd_int(int a, int b) {
+    while (b) {
+        const int t = a % b;
+        a = b;
+        b = t;
+    }
+    return a;
+}
+
+// Shapes the tensor-core route handles.
+static bool prefill_tc_supported(int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t block_size,
+                                 int dtype, int64_t num_blocks, int64_t tokens) {
+    if (dtype == MINIKV_F32 || (head_dim != 64 && head_dim != 128)) return false;
+    const int64_t group = q_heads / kv_heads;
+    if (group < 1 || 128 % group != 0 || kv_heads > 65535) return false;
+    if (gcd_int((int)std::min<int64_t>(block_size, 1 << 20), 128) < 8) return false;
+    return num_blocks * block_size < (1ll << 31) && tokens < (1ll << 31) && encode_tiled_fn() != nullptr;
+}
+
+template <typename T, int D>
+static cudaError_t launch_prefill_tc_typed(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
+                                           const PrefillTcParams& p, int grid_x, int kv_heads, cudaStream_t stream) {
+    using L = PfLayout<T, D>;
+    auto kernel = paged_prefill_tc_kernel<T, D>;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    if (err != cudaSuccess) return err;
+    kernel<<<dim3(grid_x, kv_heads), kPfThreads, L::SMEM, stream>>>(mq, mk, mv, p);
+    return cudaGetLastError();
+}
+
+static int run_prefill_tc(const void* q, const void* key_cache, const void* value_cache, const int64_t* cu_seqlens_q,
+                          const int64_t* query_starts, const int64_t* block_tables, const int64_t* context_lens,
+                          void* out, int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
+                          int64_t head_dim, int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype,
+                          cudaStream_t stream) {
+    const bool bf16 = dtype == MINIKV_BF16;
+    const int group = (int)(q_heads / kv_heads);
+    const int tm = 128 / group;
+    const int box_rows = gcd_int((int)std::min<int64_t>(block_size, 1 << 20), 128);
+    CUtensorMap mq, mk, mv;
+    if (!encode_map_3d(&mq, q, bf16, head_dim, q_heads, tokens, 64, group, tm) ||
+        !encode_map_3d(&mk, key_cache, bf16, head_dim, kv_heads, num_blocks * block_size, 64, 1, box_rows) ||
+        !encode_map_3d(&mv, value_cache, bf16, head_dim, kv_heads, num_blocks * block_size, 64, 1, box_rows))
+        return fail(MINIKV_ECUDA, "cuTensorMapEncodeTiled failed for the paged prefill operands");
+    PrefillTcParams p{};
+    p.cu_q = cu_seqlens_q;
+    p.starts = query_starts;
+    p.tables = block_tables;
+    p.ctx = context_lens;
+    p.out = out;
+    p.requests = (int)requests;
+    p.q_heads = (int)q_heads;
+    p.group = group;
+    p.num_blocks = (int)num_blocks;
+    p.block_size = (int)block_size;
+    p.table_width = (int)table_width;
+    p.tm = tm;
+    p.box_rows = box_rows;
+    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+    const int64_t grid_x = (tokens + tm - 1) / tm + requests;  // >= number of query tiles
+    if (grid_x > 2147483647) return fail(MINIKV_EINVAL, "too many paged prefill tiles");
+    cudaError_t err;
+    if (bf16)
+        err = head_dim == 64 ? launch_prefill_tc_typed<__nv_bfloat16, 64>(mq, mk, mv, p, (int)grid_x, (int)kv_heads, stream)
+                             : launch_prefill_tc_typed<__nv_bfloat16, 128>(mq, mk, mv, p, (int)grid_x, (int)kv_heads, stream);
+    else
+        err = head_dim == 64 ? launch_prefill_tc_typed<__half, 64>(mq, mk, mv, p, (int)grid_x, (int)kv_heads, stream)
+                             : launch_prefill_tc_typed<__half, 128>(mq, mk, mv, p, (int)grid_x, (int)kv_heads, stream);
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_prefill tcgen05 launch");
+    return MINIKV_OK;
+}
+
+}  // namespace minikv

@@ -8,7 +8,6 @@ import pytest
 import torch
 
 import cases
-from myvllm_mini_engine_b200.cache import BlockManager
 from myvllm_mini_engine_b200.engine import PrefillBatch
 from myvllm_mini_engine_b200.kernels import copy_blocks, paged_prefill_attention, write_kv_cache_slots
 from oracle import kv_write, metadata, prefill
@@ -85,8 +84,6 @@ def test_empty_packed_queries(cuda_device):
 def test_config4_copy_on_write_scatter_and_prefill(cuda_device):
     c = cases.config4()
     bs = c["block_size"]
-    # host allocator decides the copy-on-write exactly as the case describes
-    manager = BlockManager(c["num_blocks"], bs)
     # oracle path (CPU): CoW copy, metadata, scatter, prefill
     kc, vc = c["key_cache"].clone(), c["value_cache"].clone()
     kv_write.copy_blocks(kc.unsqueeze(0), vc.unsqueeze(0), [c["cow_pair"]])
@@ -111,4 +108,25 @@ def test_config4_copy_on_write_scatter_and_prefill(cuda_device):
     rows = torch.from_numpy(PREFILL["config4/rows"])
     golden = torch.from_numpy(PREFILL["config4/out_rows"]).view(torch.bfloat16).reshape(-1, 16, 128)
     assert_close(out[rows.cuda()], golden.float(), torch.bfloat16)
-    del manager
+
+
+def _kernel_names(fn):
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {evt.name for evt in prof.events() if evt.device_type == torch.autograd.DeviceType.CUDA}
+
+
+@pytest.mark.parametrize("dtype,dim,heads,kv_heads,expect_tc", [
+    (torch.bfloat16, 128, 16, 8, True), (torch.float16, 64, 8, 8, True), (torch.bfloat16, 128, 32, 4, True),
+    (torch.bfloat16, 96, 16, 8, False), (torch.float32, 128, 16, 8, False),
+])
+def test_tensor_core_route_selection(cuda_device, dtype, dim, heads, kv_heads, expect_tc):
+    c = cases.ragged_prefill_case(dtype, head_dim=dim, heads=heads, kv_heads=kv_heads)
+    args = [c[k].cuda() for k in NAMES]
+    paged_prefill_attention(*args, c["block_size"])  # load + warm up
+    names = _kernel_names(lambda: paged_prefill_attention(*args, c["block_size"]))
+    used_tc = any("paged_prefill_tc_kernel" in n for n in names)
+    assert used_tc == expect_tc, names
+    if not expect_tc:
+        assert any("paged_decode_kernel" in n for n in names), names
