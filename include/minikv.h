@@ -74,6 +74,23 @@ int minikv_paged_decode(const void* query, const void* key_cache, const void* va
                         int64_t num_blocks, int64_t block_size, int64_t table_width,
                         int dtype, void* stream);
 
+/* Same decode attention, for callers that cannot allocate device memory when
+ * they call (a CUDA graph being captured under a framework that owns every
+ * allocation, a serving loop that bans cudaMalloc after start-up, a cgo/JNI
+ * host without a device allocator).  No counterpart in the reference: its
+ * kernel always allocates its partials with at::empty.  The scratch lives in a
+ * built-in 16 MiB device array that every GPU loading the library keeps until
+ * exit; shapes needing more scratch than that fail with MINIKV_EINVAL.  The
+ * first call on each device looks the array up (cudaGetSymbolAddress) and
+ * should come before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU race and must be serialised by the caller.  Nothing
+ * is allocated or freed. */
+int minikv_paged_decode_noalloc(const void* query, const void* key_cache, const void* value_cache,
+                                const int64_t* block_tables, const int64_t* context_lens, void* out,
+                                int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                int64_t num_blocks, int64_t block_size, int64_t table_width,
+                                int dtype, void* stream);
+
 /* ------------------------------------------------------------- KV writes ---
  * Bit-exact row copies with 16-byte vector loads/stores.  A source row is the
  * [kv_heads, head_dim] block of one token; consecutive source tokens are

@@ -312,3 +312,7 @@ int minikv_build_decode_tables(const int64_t* active, const int64_t* tokens, con
 }
 
 }  // extern "C"
+
+// The no-allocation decode entry point (its scratch array and its set-up live in
+// that file; it uses check_decode_shapes above).
+#include "decode_noalloc.cu"
