@@ -124,6 +124,7 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+constexpr uint64_t kWaitCheckNs = 200000ull;       // 200 us: from here on, check for another timeout
 
 // Bounded wait for the phase with the given parity.  Returns false (and sets
 // the status bit) if the phase did not complete within kWaitLimitNs; callers
@@ -135,7 +136,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 #pragma unroll 1
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
-        if (global_ns() - start > kWaitLimitNs) break;
+        const uint64_t waited = global_ns() - start;
+        if (waited > kWaitLimitNs) break;
+        // A wait this long is already abnormal: give up at once if another one
+        // has timed out, so a broken pipeline costs one limit, not one per wait.
+        if (waited > kWaitCheckNs && (*reinterpret_cast<volatile unsigned int*>(&g_status) & kStatusWaitTimeout))
+            return false;
     }
     raise_status(kStatusWaitTimeout);
     return false;

@@ -5,15 +5,21 @@
 // (GQA packing, so every K/V tile is loaded once for all query heads that
 // read it).  The CTA walks the request's key tiles of 128 keys, up to the
 // tile's last query position (causal):
-//   S   = Q K^T   tcgen05.mma kind::f16, M=128, N=128, K=D -> TMEM (fp32)
-//   P   = exp2(S * log2(e)/sqrt(D) - rowmax)                 (softmax warps)
-//   O_t = P V     tcgen05.mma, M=128, N=D, K=128           -> TMEM (fp32)
-//   O   = O * alpha + O_t  (registers of the softmax warps; online softmax)
+//   S_j = Q K_j^T   tcgen05.mma kind::f16, M=128, N=128, K=D -> TMEM (fp32),
+//                   double-buffered (two 128-column S buffers)
+//   P_j = exp2(S_j * log2(e)/sqrt(D) - m)                      (softmax warps)
+//   O  += P_j V_j   tcgen05.mma, M=128, N=D, K=128 -> TMEM (fp32), accumulated
+//                   across key tiles
+// The running max m is raised lazily: while no score exceeds it by more than
+// 8 (log2 units) P is formed against the old m, so O is rescaled in TMEM
+// (tcgen05.ld / st by the row's thread) only when m moves by more than that.
 // Warp roles: warp 0 issues the TMA loads (Q once; the K and V boxes of each
 // key tile straight from the physical pages of the block table, SWIZZLE_128B,
-// two-stage ring), warp 1 owns the TMEM allocation and one of its lanes issues
-// every MMA, warps 2-5 own one TMEM lane (= one row) each for the softmax, the
-// P tile (written to shared memory in the swizzled K-major layout the MMA
+// two-stage ring) and publishes each tile's key-validity bits; warp 1 owns
+// the TMEM allocation and one of its lanes issues every MMA, S_{j+1} before
+// P_j V_j so the scores of the next tile are computed while the softmax warps
+// work; warps 2-5 own one TMEM lane (= one row) each for the softmax, the P
+// tile (written to shared memory in the swizzled K-major layout the MMA
 // reads) and the epilogue.  No TMA multicast.
 //
 // Semantics follow the reference kernel (mini_engine/kernels/csrc/prefill.cu:
@@ -70,7 +76,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
 
 // 32 TMEM lanes x 32 columns of 32-bit values: thread i of the warp gets row
 // (lane base + i), columns [col, col + 32).
+// tcgen05.ld / st / wait are warp-wide (.sync.aligned): every helper below
+// starts by reconverging the warp, and callers reach them with all 32 lanes.
 __device__ __forceinline__ void tmem_load_32(uint32_t taddr, float* v) {
+    __syncwarp();
     uint32_t r[32];
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
@@ -82,8 +91,55 @@ __device__ __forceinline__ void tmem_load_32(uint32_t taddr, float* v) {
           "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    // the loaded registers are valid only after the wait: tie every use to it
+#pragma unroll
+    for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i]));
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Four 32-column loads of one row (128 consecutive columns), one wait.
+__device__ __forceinline__ void tmem_load_128(uint32_t taddr, float* v) {
+    __syncwarp();
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        uint32_t* r = reinterpret_cast<uint32_t*>(v + 32 * c);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+            "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+            "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+              "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+              "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+              "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+            : "r"(taddr + 32 * c));
+    }
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    uint32_t* r = reinterpret_cast<uint32_t*>(v);
+#pragma unroll
+    for (int i = 0; i < 128; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+__device__ __forceinline__ void tmem_store_32(uint32_t taddr, const float* v) {
+    __syncwarp();
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        ::"r"(taddr), "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]),
+          "f"(v[8]), "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]),
+          "f"(v[16]), "f"(v[17]), "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]),
+          "f"(v[24]), "f"(v[25]), "f"(v[26]), "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_store_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 2^x on the special-function unit (ex2.approx, flush to zero); 2^-inf = 0.
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 // Shared-memory matrix descriptor, SWIZZLE_128B (sm100 layout code 2), version 1.
@@ -118,7 +174,7 @@ struct PfLayout {
     static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
     static constexpr int OFF_BAR = OFF_P + P_BYTES;
     static constexpr int SMEM = OFF_BAR + 256 + 1024;     // + barriers/flags + alignment slack
-    static constexpr uint32_t TMEM_COLS = (kPfKeys + D) <= 256 ? 256 : 512;
+    static constexpr uint32_t TMEM_COLS = 512;  // S0, S1 (128 columns each) and O (D columns)
 };
 
 template <typename T, int D>
@@ -135,15 +191,15 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     unsigned char* sP = smem + L::OFF_P;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     uint64_t* q_full = bar + 0;
-    uint64_t* kv_full = bar + 1;   // [2]
-    uint64_t* kv_empty = bar + 3;  // [2]
-    uint64_t* s_full = bar + 5;
-    uint64_t* s_free = bar + 6;
-    uint64_t* p_full = bar + 7;
-    uint64_t* o_full = bar + 8;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 9);
-    int* info = reinterpret_cast<int*>(bar + 10);               // request, tile, valid
-    uint32_t* key_ok = reinterpret_cast<uint32_t*>(bar + 12);   // [2][4] validity bits of a key tile
+    uint64_t* kv_full = bar + 1;   // [2] K and V of a key tile landed (+ its key_ok words)
+    uint64_t* kv_empty = bar + 3;  // [2] both MMAs of the tile are done with its K/V slot
+    uint64_t* s_full = bar + 5;    // [2] S of a tile is in its TMEM buffer
+    uint64_t* s_free = bar + 7;    // [2] the softmax warps have read that S buffer
+    uint64_t* p_full = bar + 9;    // P of the tile is in shared memory and O is rescaled
+    uint64_t* o_done = bar + 10;   // the P V product of the tile has been accumulated into O
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 11);
+    int* info = reinterpret_cast<int*>(bar + 12);               // request, tile
+    uint32_t* key_ok = reinterpret_cast<uint32_t*>(bar + 14);   // [2][4] validity bits of a key tile
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int B = p.requests, G = p.group, TM = p.tm;
@@ -195,14 +251,14 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
 
     if (tid == 0) {
         mbar_init(q_full, 1);
-        mbar_init(&kv_full[0], 1);
-        mbar_init(&kv_full[1], 1);
-        mbar_init(&kv_empty[0], 1);
-        mbar_init(&kv_empty[1], 1);
-        mbar_init(s_full, 1);
-        mbar_init(s_free, 4);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+            mbar_init(&s_full[s], 1);
+            mbar_init(&s_free[s], 4);
+        }
         mbar_init(p_full, 4);
-        mbar_init(o_full, 1);
+        mbar_init(o_done, 1);
         mbar_init_fence();
     }
     if (warp == 1) {
@@ -213,7 +269,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_slot;
+    const uint32_t tmem = *tmem_slot;  // columns: S0 [0,128) | S1 [128,256) | O [256, 256+D)
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -228,10 +284,23 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
             for (int j = 0; j < n_tiles; ++j) {
                 const int slot = j & 1;
                 if (j >= 2) mbar_wait(&kv_empty[slot], ((j >> 1) - 1) & 1);
+                const int64_t key0 = (int64_t)j * kPfKeys;
+                // validity of the tile's keys (in the context and on a valid page), for the softmax warps
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int64_t key = key0 + q * 32 + lane;
+                    bool ok = key < limit;
+                    if (ok) {
+                        const int64_t page = table[key / p.block_size];
+                        ok = page >= 0 && page < p.num_blocks;
+                    }
+                    const unsigned bits = __ballot_sync(0xffffffffu, ok);
+                    if (lane == 0) key_ok[4 * slot + q] = bits;
+                }
                 // lane gi handles boxes gi, gi + 32, ... (R rows each)
                 uint32_t bytes = 0;
                 for (int gi = lane; gi < groups; gi += 32) {
-                    const int64_t k0 = (int64_t)j * kPfKeys + gi * R;
+                    const int64_t k0 = key0 + gi * R;
                     if (k0 >= limit) continue;
                     const int64_t page = table[k0 / p.block_size];
                     if (page < 0 || page >= p.num_blocks) continue;
@@ -239,12 +308,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                 }
 #pragma unroll
                 for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
+                __syncwarp();
                 if (lane == 0) mbar_arrive_expect_tx(&kv_full[slot], bytes);
                 __syncwarp();
                 unsigned char* kdst = sK + slot * L::KV_BYTES;
                 unsigned char* vdst = sV + slot * L::KV_BYTES;
                 for (int gi = lane; gi < groups; gi += 32) {
-                    const int64_t k0 = (int64_t)j * kPfKeys + gi * R;
+                    const int64_t k0 = key0 + gi * R;
                     if (k0 >= limit) continue;
                     const int64_t page = table[k0 / p.block_size];
                     if (page < 0 || page >= p.num_blocks) continue;
@@ -259,123 +329,131 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        // S(j+1) is issued before P V(j), so the tensor cores compute the next
+        // scores while the softmax warps work on the current ones.
         if (lane == 0 && n_tiles > 0) {
             constexpr uint32_t idesc_s = umma_idesc(128, kPfKeys, kBf16, false);
             constexpr uint32_t idesc_o = umma_idesc(128, D, kBf16, true);
-            const uint32_t t_s = tmem, t_o = tmem + kPfKeys;
+            const uint32_t t_o = tmem + 2 * kPfKeys;
             const uint32_t q_addr = smem_addr(sQ), p_addr = smem_addr(sP);
             mbar_wait(q_full, 0);
-            for (int j = 0; j < n_tiles; ++j) {
-                const int slot = j & 1;
-                mbar_wait(&kv_full[slot], (j >> 1) & 1);
-                if (j > 0) mbar_wait(s_free, (j - 1) & 1);
-                tc_fence_after();
-                const uint32_t k_addr = smem_addr(sK + slot * L::KV_BYTES);
+            for (int j = -1; j < n_tiles; ++j) {
+                const int next = j + 1;
+                if (next < n_tiles) {
+                    const int slot = next & 1;
+                    mbar_wait(&kv_full[slot], (next >> 1) & 1);
+                    if (next >= 2) mbar_wait(&s_free[slot], ((next >> 1) - 1) & 1);
+                    tc_fence_after();
+                    const uint32_t k_addr = smem_addr(sK + slot * L::KV_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk) {
-                    const uint32_t off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
-                    umma_f16(t_s, smem_desc(q_addr + off, 16, 1024), smem_desc(k_addr + off, 16, 1024), idesc_s, kk > 0);
+                    for (int kk = 0; kk < D / 16; ++kk) {
+                        const uint32_t off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
+                        umma_f16(tmem + slot * kPfKeys, smem_desc(q_addr + off, 16, 1024),
+                                 smem_desc(k_addr + off, 16, 1024), idesc_s, kk > 0);
+                    }
+                    umma_commit(&s_full[slot]);
                 }
-                umma_commit(s_full);
+                if (j < 0) continue;
                 mbar_wait(p_full, j & 1);
                 tc_fence_after();
-                const uint32_t v_addr = smem_addr(sV + slot * L::KV_BYTES);
+                const uint32_t v_addr = smem_addr(sV + (j & 1) * L::KV_BYTES);
 #pragma unroll
                 for (int kk = 0; kk < kPfKeys / 16; ++kk) {
                     const uint32_t a_off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
                     umma_f16(t_o, smem_desc(p_addr + a_off, 16, 1024),
-                             smem_desc(v_addr + kk * 16 * 128, L::BLOCK_BYTES, 1024), idesc_o, kk > 0);
+                             smem_desc(v_addr + kk * 16 * 128, L::BLOCK_BYTES, 1024), idesc_o, (j > 0 || kk > 0));
                 }
-                umma_commit(o_full);
-                umma_commit(&kv_empty[slot]);
+                umma_commit(o_done);
+                umma_commit(&kv_empty[j & 1]);
             }
         }
     } else {
         // ------------------------------------------------------------ softmax warps
         const int quarter = warp & 3;            // TMEM lane quarter of this warp
         const int row = quarter * 32 + lane;     // tile row = TMEM lane
-        const int st = (warp - 2) * 32 + lane;   // 0..127 for cooperative work
+        const int st = (warp - 2) * 32 + lane;   // 0..127: the key row this thread zeroes when masked
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        const uint32_t t_s = tmem + lane_base, t_o = tmem + lane_base + kPfKeys;
+        const uint32_t t_o = tmem + lane_base + 2 * kPfKeys;
         const int t = t_lo + row / G, g = row % G;
         const int64_t pos = start + t;
         const bool row_valid = t < qlen && pos < limit;
-        float o_acc[D];
-#pragma unroll
-        for (int d = 0; d < D; ++d) o_acc[d] = 0.f;
-        float mrow = -INFINITY, lrow = 0.f, alpha_prev = 1.f;
+        const float scale = p.scale_log2;
+        // Running max (log2 domain) and sum.  The max is raised lazily: P is
+        // computed against m_run as long as no score exceeds it by more than
+        // 2^8, so O (accumulated in TMEM) is rescaled only when m_run moves.
+        float m_run = -INFINITY, l_run = 0.f;
         for (int j = 0; j < n_tiles; ++j) {
             const int slot = j & 1;
-            uint32_t* ok_words = key_ok + 4 * (j & 1);
-            {   // key validity of this tile: thread st checks key j*128 + st
-                const int64_t key = (int64_t)j * kPfKeys + st;
-                bool ok = key < limit;
-                if (ok) {
-                    const int64_t page = table[key / p.block_size];
-                    ok = page >= 0 && page < p.num_blocks;
-                }
-                const unsigned bits = __ballot_sync(0xffffffffu, ok);
-                if (lane == 0) ok_words[warp - 2] = bits;
+            mbar_wait(&kv_full[slot], (j >> 1) & 1);
+            uint32_t w[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) w[q] = key_ok[4 * slot + q];
+            if (!((w[st >> 5] >> (st & 31)) & 1u)) {
                 // V rows of masked keys must be finite zeros before P V runs
-                mbar_wait(&kv_full[slot], (j >> 1) & 1);
-                if (!ok) {
-                    unsigned char* vrow = sV + slot * L::KV_BYTES + st * 128;
+                unsigned char* vrow = sV + slot * L::KV_BYTES + st * 128;
 #pragma unroll
-                    for (int kb = 0; kb < L::KB; ++kb) {
-                        uint4* v4 = reinterpret_cast<uint4*>(vrow + kb * L::BLOCK_BYTES);
+                for (int kb = 0; kb < L::KB; ++kb) {
+                    uint4* v4 = reinterpret_cast<uint4*>(vrow + kb * L::BLOCK_BYTES);
 #pragma unroll
-                        for (int c = 0; c < 8; ++c) v4[c] = make_uint4(0, 0, 0, 0);
-                    }
-                    fence_async_smem();
+                    for (int c = 0; c < 8; ++c) v4[c] = make_uint4(0, 0, 0, 0);
                 }
+                fence_async_smem();
             }
-            softmax_sync();
-            mbar_wait(s_full, j & 1);
+            // keys [0, rel] of this tile are causally visible to the row
+            const int64_t rel = pos - (int64_t)j * kPfKeys;
+            uint32_t bits[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int64_t lim = rel - q * 32;
+                const uint32_t causal = lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : ((2u << (int)lim) - 1u));
+                bits[q] = row_valid ? (w[q] & causal) : 0u;
+            }
+            const bool full = (bits[0] & bits[1] & bits[2] & bits[3]) == 0xffffffffu;
+
+            mbar_wait(&s_full[slot], (j >> 1) & 1);
             tc_fence_after();
-            // pass 1: row max of the masked, scaled scores
-            const int64_t key0 = (int64_t)j * kPfKeys;
+            float s[kPfKeys];
+            tmem_load_128(tmem + lane_base + slot * kPfKeys, s);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[slot]);
+
             float mx = -INFINITY;
+            if (full) {
 #pragma unroll
-            for (int c = 0; c < kPfKeys / 32; ++c) {
-                float v[32];
-                tmem_load_32(t_s + c * 32, v);
-                const uint32_t word = ok_words[c];
+                for (int e = 0; e < kPfKeys; ++e) mx = fmaxf(mx, s[e]);
+            } else {
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const bool ok = row_valid && ((word >> e) & 1u) && key0 + c * 32 + e <= pos;
-                    mx = fmaxf(mx, ok ? v[e] * p.scale_log2 : -INFINITY);
-                }
+                for (int e = 0; e < kPfKeys; ++e)
+                    if ((bits[e >> 5] >> (e & 31)) & 1u) mx = fmaxf(mx, s[e]);
             }
-            const float m_new = fmaxf(mrow, mx);
-            const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(mrow - m_new);
-            // O += previous tile (its PV product is done once o_full flips)
+            const float m_tile = mx * scale;  // -inf when the row sees no key of this tile
+            float m_use = m_run, alpha = 1.f;
+            bool rescale = false;
+            if (m_tile > m_run + 8.f) {
+                alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_tile);
+                rescale = m_run != -INFINITY;  // O holds only zeros while m_run is -inf
+                m_use = m_tile;
+            }
+            // P of this tile replaces the previous one: its P V product must be done
             if (j > 0) {
-                mbar_wait(o_full, (j - 1) & 1);
+                mbar_wait(o_done, (j - 1) & 1);
                 tc_fence_after();
-#pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
-                    float v[32];
-                    tmem_load_32(t_o + c * 32, v);
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) o_acc[c * 32 + e] = fmaf(o_acc[c * 32 + e], alpha_prev, v[e]);
-                }
             }
-            // pass 2: P = exp2(s - m_new) -> shared memory (K-major, 128B swizzle), row sums
             float sum = 0.f;
             unsigned char* prow = sP + row * 128;
+            const float neg = -m_use;
 #pragma unroll
             for (int c = 0; c < kPfKeys / 32; ++c) {
-                float v[32];
-                tmem_load_32(t_s + c * 32, v);
-                const uint32_t word = ok_words[c];
                 uint32_t packed[16];
 #pragma unroll
                 for (int e = 0; e < 32; e += 2) {
                     float pe[2];
 #pragma unroll
                     for (int u = 0; u < 2; ++u) {
-                        const bool ok = row_valid && ((word >> (e + u)) & 1u) && key0 + c * 32 + e + u <= pos;
-                        pe[u] = (ok && m_new != -INFINITY) ? exp2f(v[e + u] * p.scale_log2 - m_new) : 0.f;
+                        const int k = c * 32 + e + u;
+                        const float x = fast_exp2(fmaf(s[k], scale, neg));
+                        pe[u] = (full || ((bits[c] >> (e + u)) & 1u)) ? x : 0.f;
                         sum += pe[u];
                     }
                     packed[e / 2] = Elem<T>::pack(pe[0], pe[1]);
@@ -388,37 +466,51 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                     *dst = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
                 }
             }
-            lrow = lrow * alpha + sum;
-            mrow = m_new;
-            alpha_prev = alpha;
+            // tcgen05.ld / st are warp-wide (.sync.aligned): the whole warp takes
+            // this branch when any of its rows rescales; the others scale by 1.
+            if (__any_sync(0xffffffffu, rescale)) {
+                const float factor = rescale ? alpha : 1.f;
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    float v[32];
+                    tmem_load_32(t_o + c * 32, v);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) v[e] *= factor;
+                    tmem_store_32(t_o + c * 32, v);
+                }
+                tmem_store_wait();
+            }
+            l_run = l_run * alpha + sum;
+            m_run = m_use;
             fence_async_smem();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(s_free);
-                mbar_arrive(p_full);
-            }
+            if (lane == 0) mbar_arrive(p_full);
         }
         if (n_tiles > 0) {
-            mbar_wait(o_full, (n_tiles - 1) & 1);
+            mbar_wait(o_done, (n_tiles - 1) & 1);
             tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-                float v[32];
-                tmem_load_32(t_o + c * 32, v);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) o_acc[c * 32 + e] = fmaf(o_acc[c * 32 + e], alpha_prev, v[e]);
-            }
         }
-        if (t < qlen) {
-            const float inv = (row_valid && lrow > 0.f) ? 1.f / lrow : 0.f;
-            T* orow = static_cast<T*>(p.out) + ((q0 + t) * p.q_heads + h * G + g) * D;
+        // every lane of the warp loads (warp-wide tcgen05.ld); rows past the chunk store nothing
+        const float inv = (row_valid && l_run > 0.f) ? 1.f / l_run : 0.f;
+        T* orow = static_cast<T*>(p.out) + ((q0 + t) * p.q_heads + h * G + g) * D;
 #pragma unroll
-            for (int d = 0; d < D; d += 8) {
-                float f[8];
+        for (int c = 0; c < D / 32; ++c) {
+            float v[32];
+            if (n_tiles > 0) {
+                tmem_load_32(t_o + c * 32, v);
+            } else {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = o_acc[d + e] * inv;
-                *reinterpret_cast<uint4*>(orow + d) = Elem<T>::store(f);
+                for (int e = 0; e < 32; ++e) v[e] = 0.f;
+            }
+            if (t < qlen) {
+#pragma unroll
+                for (int d = 0; d < 32; d += 8) {
+                    float f[8];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) f[e] = v[d + e] * inv;
+                    *reinterpret_cast<uint4*>(orow + c * 32 + d) = Elem<T>::store(f);
+                }
             }
         }
         tc_fence_before();
