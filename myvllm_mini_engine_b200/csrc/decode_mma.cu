@@ -6,12 +6,13 @@
 // the GQA query heads as the N columns:
 //   S^T[16 tokens x 8 heads]  = K[16 x 16 dims] . Q^T          (A = K via ldmatrix)
 //   O^T[16 dims x 8 heads]   += V^T[16 dims x 16 tokens] . P^T (A = V via ldmatrix.trans)
-// so a slice costs D/16 + D/16 MMAs whatever the group size (<= 8), every K/V
+// so a slice costs D/16 + 2 D/16 MMAs whatever the group size (<= 8), every K/V
 // byte staged in shared memory is read once per kv head, and the Q operand
 // (16 registers for D=128) and the O accumulators (32) stay small.  Softmax
 // runs on the S^T fragments: the max and sum of a head are reductions across
-// the 8 lanes that share its column.  P is rounded to the input type, packed
-// and moved into the B-operand layout with four shuffles.  Token rows in
+// the 8 lanes that share its column.  P is split into two terms of the input
+// type (P_hi + P_lo), each packed and moved into the B-operand layout with
+// four shuffles, and both are multiplied into O.  Token rows in
 // shared memory are padded (stride / 16 odd), so ldmatrix is bank-conflict
 // free; masked tokens' V rows are zero (see the producer).
 #include "common.cuh"
@@ -140,20 +141,36 @@ struct MmaConsumer {
                     o[mt][3] *= alpha[1];
                 }
             }
+            // ---- P = P_hi + P_lo, both in the input type (P_lo = P - P_hi rounded), so
+            // the PV product carries P to ~2^-16 relative, as the reference's fp32
+            // probabilities do (fallback.py:59-63), at the cost of one more MMA per m-tile.
+            float rest[4];
+            const uint32_t h01 = Elem<T>::pack(pv[0], pv[1]);  // token sub+g,   heads 2q4, 2q4+1
+            const uint32_t h23 = Elem<T>::pack(pv[2], pv[3]);  // token sub+g+8, heads 2q4, 2q4+1
+            {
+                float back[4];
+                Elem<T>::unpack(h01, back);
+                Elem<T>::unpack(h23, back + 2);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) rest[e] = pv[e] - back[e];
+            }
+            const uint32_t l01 = Elem<T>::pack(rest[0], rest[1]);
+            const uint32_t l23 = Elem<T>::pack(rest[2], rest[3]);
             // ---- P^T into the B layout: lane (g, q4) needs tokens 2q4, 2q4+1 (b0) and
             // 2q4+8, 2q4+9 (b1) of head g; lane (t, h/2) holds tokens t, t+8 of heads h&~1, h|1.
-            const uint32_t lo = Elem<T>::pack(pv[0], pv[1]);  // token sub+g,   heads 2q4, 2q4+1
-            const uint32_t hi = Elem<T>::pack(pv[2], pv[3]);  // token sub+g+8, heads 2q4, 2q4+1
             const int src0 = (2 * q4) * 4 + (g >> 1), src1 = src0 + 4;
             const bool odd = g & 1;
-            const uint32_t b0 = pick_halves(__shfl_sync(0xffffffffu, lo, src0), __shfl_sync(0xffffffffu, lo, src1), odd);
-            const uint32_t b1 = pick_halves(__shfl_sync(0xffffffffu, hi, src0), __shfl_sync(0xffffffffu, hi, src1), odd);
-            // ---- O^T += V^T P^T
+            const uint32_t b0 = pick_halves(__shfl_sync(0xffffffffu, h01, src0), __shfl_sync(0xffffffffu, h01, src1), odd);
+            const uint32_t b1 = pick_halves(__shfl_sync(0xffffffffu, h23, src0), __shfl_sync(0xffffffffu, h23, src1), odd);
+            const uint32_t c0 = pick_halves(__shfl_sync(0xffffffffu, l01, src0), __shfl_sync(0xffffffffu, l01, src1), odd);
+            const uint32_t c1 = pick_halves(__shfl_sync(0xffffffffu, l23, src0), __shfl_sync(0xffffffffu, l23, src1), odd);
+            // ---- O^T += V^T P_hi^T + V^T P_lo^T
             const uint32_t vrow = vs + (sub + v_tok) * stride + v_dim * esize;
 #pragma unroll
             for (int mt = 0; mt < MTILES; ++mt) {
                 uint32_t a[4];
                 ldsm_x4_trans(vrow + 16 * mt * esize, a);
+                Mma::mma(o[mt], a, c0, c1);
                 Mma::mma(o[mt], a, b0, b1);
             }
         }
