@@ -49,10 +49,21 @@ def parse_args(argv=None):
     parser.add_argument("--steps", type=int, default=20000)
     parser.add_argument("--warmup", type=int, default=20)
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    parser.add_argument("--batch", type=int, default=32, help="requests per GPU")
-    parser.add_argument("--context", type=int, default=2048, help="attended tokens per request")
+    parser.add_argument("--workload", choices=("decode", "qwen3", "prefill"), default="decode",
+                        help="decode: append + paged attention per GPU (weak scaling); qwen3: the full "
+                             "Qwen3-0.6B decode step of BASELINE config 5 (strong scaling over --batch); "
+                             "prefill: BASELINE config 4 (copy-on-write + slot scatter + ragged paged prefill)")
+    parser.add_argument("--batch", type=int, default=None,
+                        help="requests per GPU (decode, default 32) or in total (qwen3, default 256)")
+    parser.add_argument("--context", type=int, default=None,
+                        help="attended tokens per request (decode, default 2048) or cached tokens (qwen3, 4096)")
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
-    return parser.parse_args(argv)
+    args = parser.parse_args(argv)
+    if args.batch is None:
+        args.batch = 32 if args.workload == "decode" else 256
+    if args.context is None:
+        args.context = 2048 if args.workload == "decode" else 4096
+    return args
 
 
 # ----------------------------------------------------------------------- setup
@@ -366,11 +377,11 @@ def run_ours(args, world, rank, local):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "traffic": ncu_traffic("decode_b32_ctx2048_bf16"),
-                     "kernel": "paged decode (split kernel + combine kernel) per launch",
+                     "kernel": "paged decode (split-KV with the merge in the same launch)",
                      "bytes_per_launch": step_bytes, "launch_ms": kernel_avg_ms},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms / args.steps},
-        "gpu_launches": 3 * args.steps,
+        "gpu_launches": 2 * args.steps,
         "clocks": clocks.summary(),
     }
     if world == 1:
@@ -378,11 +389,441 @@ def run_ours(args, world, rank, local):
     return line
 
 
+# ------------------------------------------------- config 5: Qwen3 decode step
+QWEN3_SEED = 2025
+
+
+def qwen3_config():
+    from myvllm_mini_engine_b200.engine.qwen3 import Qwen3Config
+    return Qwen3Config.qwen3_0_6b()
+
+
+def qwen3_weight_bytes(cfg, esize=2):
+    """Weights one step reads: every projection of every layer, the norms, and the tied LM head once."""
+    h, d, i = cfg.hidden_size, cfg.head_dim, cfg.intermediate_size
+    per_layer = ((cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * d * h + h * cfg.num_attention_heads * d
+                 + 2 * i * h + h * i + 2 * h + 2 * d)
+    return esize * (cfg.num_hidden_layers * per_layer + cfg.vocab_size * h + h)
+
+
+def qwen3_tables(batch, pages, device, seed):
+    """Seeded permutation of a pool holding exactly ``batch * pages`` pages."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    perm = torch.randperm(batch * pages, device=device, generator=gen)
+    return perm.view(batch, pages).contiguous()
+
+
+class CpuQwen3Reference:
+    """The reference model's decode step on the host cores (oracle restatement) on a bounded sample."""
+
+    SAMPLE_BATCH = 1
+
+    def __init__(self, context, threads=None):
+        from myvllm_mini_engine_b200.engine.qwen3 import Qwen3Weights
+        from oracle import qwen3 as oracle_qwen3
+
+        if threads:
+            torch.set_num_threads(threads)
+        self.oracle = oracle_qwen3
+        self.cfg = cfg = qwen3_config()
+        self.context = context
+        self.weights = Qwen3Weights.random(cfg, dtype=torch.bfloat16, device="cpu", seed=QWEN3_SEED)
+        pages = math.ceil((context + 1) / BS)
+        shape = (cfg.num_hidden_layers, self.SAMPLE_BATCH * pages, BS, cfg.num_key_value_heads, cfg.head_dim)
+        gen = torch.Generator().manual_seed(QWEN3_SEED + 7)
+        self.key = torch.randn(shape, generator=gen).to(torch.bfloat16)
+        self.value = torch.randn(shape, generator=gen).to(torch.bfloat16)
+        self.tables = torch.arange(self.SAMPLE_BATCH * pages, dtype=torch.int64).view(self.SAMPLE_BATCH, pages)
+        self.ids = torch.randint(0, cfg.vocab_size, (self.SAMPLE_BATCH,), generator=gen)
+        self.positions = torch.full((self.SAMPLE_BATCH,), context, dtype=torch.int64)
+
+    def step(self):
+        self.oracle.decode_step(self.cfg, self.weights, self.ids, self.key, self.value, self.tables, self.positions)
+
+    def timed(self, seconds=0.0, min_steps=1, max_steps=None):
+        done, start = 0, time.perf_counter()
+        while done < min_steps or (time.perf_counter() - start < seconds and (max_steps is None or done < max_steps)):
+            self.step()
+            done += 1
+        return (time.perf_counter() - start) / done, done
+
+    def describe(self, per_step, done):
+        threads = torch.get_num_threads()
+        return {"value": self.SAMPLE_BATCH / per_step, "unit": "tok/s", "cores": threads, "kind": "port",
+                "sample": f"{done} decode steps of the oracle restating NativeQwen3.forward_decode_batch "
+                          f"(native_qwen3.py:423-456, torch backends, bf16) on {self.SAMPLE_BATCH} request x "
+                          f"{self.context} cached tokens, 28 layers, {per_step * 1e3:.0f} ms/step, "
+                          f"torch threads={threads}"}
+
+
+def qwen3_line_base(args, world, kind):
+    return {"metric": METRIC, "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random N(0,0.02) weights, N(0,1) KV history, uniform token ids)",
+            "config": {"workload": f"Qwen3-0.6B-architecture batch decode step (BASELINE config 5): "
+                                   f"{args.batch} requests x {args.context} cached tokens (+1 appended), 28 layers, "
+                                   f"hidden 1024, 16/8 heads x 128, SwiGLU 3072, vocab 151936 tied, block 16, "
+                                   f"greedy", "model": "qwen3-0.6b-arch", "global_batch": args.batch,
+                       "seq_len": args.context, "parallelism": kind,
+                       "l2": "KV pool per GPU >> 126 MB L2"}}
+
+
+def run_qwen3_reference(args, world, rank):
+    if rank != 0:
+        return None
+    ref = CpuQwen3Reference(args.context, threads=os.cpu_count() or 1)
+    ref.timed(0.0, min(args.warmup, 1))
+    per_step, done = ref.timed(60.0, 2, args.steps)
+    base = ref.describe(per_step, done)
+    line = qwen3_line_base(args, world, "rank 0 only, host cores")
+    line.update({"value": base["value"], "impl": "reference", "ms_per_step": per_step * 1e3, "cpu_baseline": base,
+                 "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}})
+    return line
+
+
+def run_qwen3(args, world, rank, local):
+    from myvllm_mini_engine_b200 import _lib
+    from myvllm_mini_engine_b200.cache.kv_cache import KVCachePool
+    from myvllm_mini_engine_b200.engine.qwen3 import DecodeGraph, Qwen3DecodeStep, Qwen3Weights
+    from myvllm_mini_engine_b200.kernels import paged_attention
+
+    if args.batch % world:
+        raise SystemExit(f"--batch {args.batch} does not split over {world} GPUs")
+    device = torch.device("cuda", local)
+    cfg = qwen3_config()
+    batch = args.batch // world
+    pages = math.ceil((args.context + 1) / BS)
+    blocks = batch * pages
+    pool_bytes = 2 * cfg.num_hidden_layers * blocks * BS * cfg.num_key_value_heads * cfg.head_dim * 2
+    free, _ = torch.cuda.mem_get_info(device)
+    if pool_bytes + (4 << 30) > free:
+        raise SystemExit(f"KV pool of {pool_bytes / 1e9:.1f} GB does not fit the {free / 1e9:.1f} GB free on "
+                         f"GPU {local}")
+    weights = Qwen3Weights.random(cfg, dtype=torch.bfloat16, device=device, seed=QWEN3_SEED)
+    pool = KVCachePool(cfg.num_hidden_layers, blocks, BS, cfg.num_key_value_heads, cfg.head_dim,
+                       dtype=torch.bfloat16, device=device)
+    gen = torch.Generator(device=device).manual_seed(QWEN3_SEED + 1 + rank)
+    for layer in range(cfg.num_hidden_layers):
+        pool.key[layer].normal_(generator=gen)
+        pool.value[layer].normal_(generator=gen)
+    tables = qwen3_tables(batch, pages, device, QWEN3_SEED + 100 + rank)
+    ids = torch.randint(0, cfg.vocab_size, (batch,), device=device, generator=gen)
+    positions = torch.full((batch,), args.context, dtype=torch.int64, device=device)
+    step = Qwen3DecodeStep(cfg, weights, pool)
+    graph = DecodeGraph(step, batch, pages)
+    graph.load(ids, positions, tables)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+
+    def max_over_ranks(ms):
+        if world > 1:
+            t = torch.tensor([ms], device=device)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        barrier()
+    ms_per_step = max_over_ranks(start.elapsed_time(end)) / args.steps
+
+    # the dominant kernel alone: paged decode over this rank's batch, one launch per layer, graph-replayed
+    lengths = [args.context + 1] * batch
+    launch_bytes = decode_bytes(lengths, batch)
+    q = torch.randn(batch, HQ, D, device=device, dtype=torch.bfloat16, generator=gen)
+    lens = positions + 1
+    side = torch.cuda.Stream(device)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        paged_attention(q, pool.key[0], pool.value[0], tables, lens, BS, validate=False)
+    side.synchronize()
+    decode_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(decode_graph, stream=side):
+        for layer in range(cfg.num_hidden_layers):
+            paged_attention(q, pool.key[layer], pool.value[layer], tables, lens, BS, validate=False)
+    decode_graph.replay()
+    torch.cuda.synchronize(device)
+    d_start, d_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = max(1, min(args.steps, 20))
+    d_start.record(stream)
+    for _ in range(reps):
+        decode_graph.replay()
+    d_end.record(stream)
+    torch.cuda.synchronize(device)
+    launch_ms = d_start.elapsed_time(d_end) / (reps * cfg.num_hidden_layers)
+    achieved = launch_bytes / (launch_ms * 1e-3) / 1e9
+    peak, peak_kind = measured_peaks()
+
+    # end to end through the graph API: host metadata in, host token ids out, every step
+    host_ids, host_pos, host_tables = (t.cpu().pin_memory() for t in (ids, positions, tables))
+    out_host = torch.empty(batch, dtype=torch.int64, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in (host_ids, host_pos, host_tables))
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        graph.load(host_ids, host_pos, host_tables)
+        out_host.copy_(graph.replay(), non_blocking=True)
+
+    for _ in range(min(args.warmup, 3)):
+        e2e_step()
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e_end.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(e_start.elapsed_time(e_end)) / args.steps
+    status = _lib.device_status(device)
+    if status:
+        raise RuntimeError(f"device status bits set during the benchmark: {status}")
+    del graph, decode_graph
+    if rank != 0:
+        return None
+    step_bytes = cfg.num_hidden_layers * (launch_bytes + 2 * batch * HKV * D * 2) + qwen3_weight_bytes(cfg)
+    line = qwen3_line_base(args, world, f"request-sharded x{world} ({batch} requests and an independent KV "
+                                        f"pool per GPU, weights replicated, no collective)")
+    line.update({
+        "value": args.batch / (ms_per_step * 1e-3), "ms_per_step": ms_per_step,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "traffic": ncu_traffic("qwen3_decode_b256_ctx4097_bf16"),
+                     "kernel": f"paged decode, {batch} requests x {args.context + 1} tokens per launch",
+                     "bytes_per_launch": launch_bytes, "launch_ms": launch_ms},
+        "step_roofline": {"bytes_per_step": step_bytes, "achieved": step_bytes / (ms_per_step * 1e-3) / 1e9,
+                          "frac": step_bytes / (ms_per_step * 1e-3) / 1e9 / peak, "unit": "GB/s",
+                          "decode_share": cfg.num_hidden_layers * launch_ms / ms_per_step},
+        "e2e": {"value": args.batch / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": (5 * cfg.num_hidden_layers + 1) * args.steps,
+        "gpu_launches_note": "libminikv kernels only (RMSNorm x2, qk-norm+RoPE+append, paged decode, SiLU*up per "
+                             "layer, plus the first RMSNorm); the 4 projections per layer and the LM head are cuBLAS",
+        "clocks": clocks.summary(),
+    })
+    if world == 1:
+        ref = CpuQwen3Reference(args.context)
+        ref.timed(0.0, 1)
+        per_step, done = ref.timed(args.cpu_seconds, 2)
+        line["cpu_baseline"] = ref.describe(per_step, done)
+    return line
+
+
+# ------------------------------------------- config 4: ragged chunked prefill
+def prefill_flops(starts, chunk, heads=HQ, dim=D):
+    """Causal (query, key) pairs x 4 Hq D: query i of a chunk starting at s attends s + i + 1 keys."""
+    return sum(4 * heads * dim * (chunk * s + chunk * (chunk + 1) // 2) for s in starts)
+
+
+def config4_inputs(device):
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import cases
+    return cases.config4()
+
+
+class CpuPrefillReference:
+    """The reference's torch prefill path on the host cores (oracle restatement), whole config 4."""
+
+    def __init__(self, threads=None):
+        from oracle import kv_write, metadata, prefill
+
+        if threads:
+            torch.set_num_threads(threads)
+        c = config4_inputs("cpu")
+        self.c, self.prefill = c, prefill
+        self.kc, self.vc = c["key_cache"].clone(), c["value_cache"].clone()
+        meta = metadata.prefill_metadata(c["tokens"], c["cow_tables"], c["starts"], block_size=c["block_size"],
+                                         num_blocks=c["num_blocks"])
+        self.t = {k: torch.tensor(v, dtype=torch.int64) for k, v in meta.items()}
+        kv_write.copy_blocks(self.kc.unsqueeze(0), self.vc.unsqueeze(0), [c["cow_pair"]])
+        kv_write.write_kv_cache_slots(self.kc, self.vc, self.t["slot_mapping"], c["key"], c["value"])
+        self.flops = prefill_flops(c["starts"], 128)
+
+    def step(self):
+        t = self.t
+        self.prefill.paged_prefill_fp32(self.c["q"], self.kc, self.vc, t["cu_seqlens_q"], t["query_starts"],
+                                        t["block_tables"], t["context_lens"], self.c["block_size"])
+
+    def timed(self, seconds, min_steps, max_steps=None):
+        done, start = 0, time.perf_counter()
+        while done < min_steps or (time.perf_counter() - start < seconds and (max_steps is None or done < max_steps)):
+            self.step()
+            done += 1
+        return (time.perf_counter() - start) / done, done
+
+    def describe(self, per_step, done):
+        threads = torch.get_num_threads()
+        return {"value": self.flops / per_step / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                "sample": f"{done} runs of the oracle's paged prefill (restating kernels/prefill.py:114-131, "
+                          f"torch path in fp32) over all of config 4 (16 x 128-token chunks), "
+                          f"{per_step * 1e3:.0f} ms/run, torch threads={threads}"}
+
+
+def prefill_line_base(args, world):
+    return {"metric": METRIC, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "BASELINE config 4: copy-on-write of a shared prefix page, slot scatter of "
+                                   "16 x 128-token chunks, ragged causal paged prefill over prefixes U[0,1024] "
+                                   "(8 requests share 32 pages), Hq16/Hkv8/D128, bf16, block 16",
+                       "global_batch": 16 * world, "seq_len": 128, "parallelism": f"independent x{world}",
+                       "l2": "L2 flushed (256 MB write) before every timed step"}}
+
+
+def run_prefill_reference(args, world, rank):
+    if rank != 0:
+        return None
+    ref = CpuPrefillReference(threads=os.cpu_count() or 1)
+    ref.timed(0.0, 1)
+    per_step, done = ref.timed(60.0, 3, args.steps)
+    base = ref.describe(per_step, done)
+    line = prefill_line_base(args, world)
+    line.update({"value": base["value"], "impl": "reference", "ms_per_step": per_step * 1e3, "cpu_baseline": base,
+                 "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                         "d2h_bytes_per_step": 0}})
+    return line
+
+
+def run_prefill(args, world, rank, local):
+    from myvllm_mini_engine_b200 import _lib
+    from myvllm_mini_engine_b200.engine import PrefillBatch
+    from myvllm_mini_engine_b200.kernels import copy_blocks, paged_prefill_attention, write_kv_cache_slots
+
+    device = torch.device("cuda", local)
+    c = config4_inputs(device)
+    bs, chunk = c["block_size"], 128
+    flops = prefill_flops(c["starts"], chunk)
+    gk, gv = c["key_cache"].to(device), c["value_cache"].to(device)
+    q, key, value = (c[k].to(device) for k in ("q", "key", "value"))
+    pairs = torch.tensor([list(c["cow_pair"])], dtype=torch.int64, device=device)
+    batch = PrefillBatch.from_sequences(c["tokens"], c["cow_tables"], c["starts"], block_size=bs,
+                                        num_blocks=c["num_blocks"], device=device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    events = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
+
+    def step(timed=False):
+        copy_blocks(gk.unsqueeze(0), gv.unsqueeze(0), pairs, validate=False)
+        write_kv_cache_slots(gk, gv, batch.slot_mapping, key, value, validate=False)
+        if timed:
+            events[1].record()
+        out = paged_prefill_attention(q, gk, gv, batch.cu_seqlens_q, batch.query_starts, batch.block_tables,
+                                      batch.context_lens, bs, validate=False, max_query_len=chunk)
+        return out
+
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            step()
+    side.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        flush.fill_(1)
+        events[0].record()
+        out = step(timed=True)
+        events[2].record()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+    steps = max(1, min(args.steps, 2000))
+    step_ms, prefill_ms = [], []
+    with ClockSampler(local) as clocks:
+        for _ in range(steps):
+            graph.replay()
+            events[2].synchronize()
+            step_ms.append(events[0].elapsed_time(events[2]))
+            prefill_ms.append(events[1].elapsed_time(events[2]))
+    step_avg, prefill_avg = statistics.mean(step_ms), statistics.mean(prefill_ms)
+    if world > 1:
+        t = torch.tensor([step_avg, prefill_avg], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        step_avg, prefill_avg = (float(x) for x in t.tolist())
+    peak = 1630.4
+    path = ROOT / "MEASURED_PEAKS.json"
+    peak_kind = "fallback"
+    if path.is_file():
+        peak, peak_kind = float(json.loads(path.read_text())["bf16_tflops"]), "measured (burst)"
+
+    # end to end: the chunk's q/k/v from pinned host memory, the output back to the host, every step
+    host = {k: c[k].pin_memory() for k in ("q", "key", "value")}
+    dev = {k: torch.empty_like(v, device=device) for k, v in host.items()}
+    out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+
+    def e2e_step():
+        for k, t in host.items():
+            dev[k].copy_(t, non_blocking=True)
+        copy_blocks(gk.unsqueeze(0), gv.unsqueeze(0), pairs, validate=False)
+        write_kv_cache_slots(gk, gv, batch.slot_mapping, dev["key"], dev["value"], validate=False)
+        result = paged_prefill_attention(dev["q"], gk, gv, batch.cu_seqlens_q, batch.query_starts,
+                                         batch.block_tables, batch.context_lens, bs, validate=False,
+                                         max_query_len=chunk)
+        out_host.copy_(result, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stream = torch.cuda.current_stream(device)
+    e_start.record(stream)
+    for _ in range(steps):
+        flush.fill_(1)
+        e2e_step()
+    e_end.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e_start.elapsed_time(e_end) / steps
+    status = _lib.device_status(device)
+    if status:
+        raise RuntimeError(f"device status bits set during the benchmark: {status}")
+    del graph
+    if rank != 0:
+        return None
+    line = prefill_line_base(args, world)
+    achieved = flops / (prefill_avg * 1e-3) / 1e12
+    kv_read = sum(min(len(t) * bs, s + chunk) for t, s in zip(c["cow_tables"], c["starts"])) * 2 * HKV * D * 2
+    line.update({
+        "value": world * flops / (step_avg * 1e-3) / 1e12, "ms_per_step": step_avg, "steps": steps,
+        "prefill_tokens_s": world * 16 * chunk / (step_avg * 1e-3),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak, "peak_source": peak_kind,
+                     "traffic": ncu_traffic("prefill_config4_bf16"),
+                     "kernel": "paged prefill (tcgen05 + TMEM, TMA page boxes) per launch",
+                     "flops_per_launch": flops, "kv_bytes_per_launch": kv_read,
+                     "launch_ms": prefill_avg},
+        "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in host.values()),
+                "d2h_bytes_per_step": out_host.numel() * out_host.element_size(), "ms_per_step_with_flush": e2e_ms},
+        "gpu_launches": 3 * steps,
+        "clocks": clocks.summary(),
+    })
+    if world == 1:
+        ref = CpuPrefillReference()
+        ref.timed(0.0, 1)
+        per_step, done = ref.timed(args.cpu_seconds, 2)
+        line["cpu_baseline"] = ref.describe(per_step, done)
+    return line
+
+
 def main(argv=None):
     args = parse_args(argv)
     world, rank, local = dist_setup(args)
     try:
-        line = run_reference(args, world, rank) if args.impl == "reference" else run_ours(args, world, rank, local)
+        if args.workload == "qwen3":
+            line = run_qwen3_reference(args, world, rank) if args.impl == "reference" else \
+                run_qwen3(args, world, rank, local)
+        elif args.workload == "prefill":
+            line = run_prefill_reference(args, world, rank) if args.impl == "reference" else \
+                run_prefill(args, world, rank, local)
+        else:
+            line = run_reference(args, world, rank) if args.impl == "reference" else run_ours(args, world, rank, local)
         if line is not None and rank == 0:
             print(json.dumps(line), flush=True)
     finally:

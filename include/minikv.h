@@ -190,6 +190,41 @@ int minikv_build_decode_tables(const int64_t* active, const int64_t* tokens, con
                                int64_t* input_ids, int64_t* out_positions, int64_t* block_tables,
                                void* stream);
 
+/* ---------------------------------------------------------- decode step ---
+ * Fused element-wise steps of the batch decode step around the paged-KV ops
+ * (NativeQwen3.forward_decode_batch, mini_engine/model/native_qwen3.py:175-196
+ * and :260-277).  FP16/BF16 only, like the reference's CUDA element-wise ops
+ * (mini_engine/kernels/elementwise.py, bindings.cpp:209-214).  Every
+ * intermediate is rounded to the 16-bit type where the eager torch path
+ * rounds it (mini_engine/kernels/fallback.py:8-24).  Outputs must not overlap
+ * inputs. */
+
+/* out = RMSNorm(s) * weight over rows of `hidden` elements, where s = x, or
+ * s = x + residual (rounded, and also written to sum_out) when residual is
+ * given.  Replaces rms_norm / residual_rms_norm (elementwise.py:16-34) and,
+ * fused into the next norm, residual_add (elementwise.py:37-44). */
+int minikv_rms_norm(const void* x, const void* residual, const void* weight, void* out, void* sum_out,
+                    int64_t rows, int64_t hidden, double eps, int dtype, void* stream);
+
+/* out[r, j] = silu(gate_up[r, j]) * gate_up[r, inter + j]: silu_and_mul of a
+ * fused gate|up projection (elementwise.py:47-54, native_qwen3.py:232-240). */
+int minikv_silu_mul(const void* gate_up, void* out, int64_t rows, int64_t inter, int dtype, void* stream);
+
+/* Decode-step attention prologue in one launch over the fused q|k|v
+ * projection rows (qkv[b, (q_heads + 2 kv_heads) * head_dim], row stride
+ * qkv_stride elements): RMSNorm of every q and k head (q_weight, k_weight),
+ * rotary embedding with cos/sin[b, head_dim/2], q written to q_out[b, q_heads,
+ * head_dim], and the decode append of k (rotated) and v into the paged caches
+ * at token_offsets[b] through block_tables (write_kv_cache_batch semantics,
+ * data.cu:89-107: an out-of-range page skips the row).  Replaces q_norm,
+ * k_norm, apply_rope and write_kv_cache_batch of native_qwen3.py:178-190.
+ * head_dim 64, 128 or 256. */
+int minikv_qk_rope_append(const void* qkv, int64_t qkv_stride, const void* q_weight, const void* k_weight,
+                          const void* cos, const void* sin, void* q_out, void* key_cache, void* value_cache,
+                          const int64_t* block_tables, const int64_t* token_offsets, int64_t batch,
+                          int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
+                          int64_t block_size, int64_t table_width, double eps, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -39,6 +39,9 @@ SIGNATURES = {
     "minikv_paged_prefill": (_int, [_p] * 8 + [_p, _i64] + [_i64] * 9 + [_int, _p]),
     "minikv_build_prefill_metadata": (_int, [_p] * 5 + [_i64] * 4 + [_p] * 7 + [_p]),
     "minikv_build_decode_tables": (_int, [_p] * 6 + [_i64, _i64] + [_p] * 3 + [_p]),
+    "minikv_rms_norm": (_int, [_p] * 5 + [_i64, _i64, ctypes.c_double, _int, _p]),
+    "minikv_silu_mul": (_int, [_p, _p, _i64, _i64, _int, _p]),
+    "minikv_qk_rope_append": (_int, [_p, _i64] + [_p] * 9 + [_i64] * 7 + [ctypes.c_double, _int, _p]),
 }
 
 _LIB = None

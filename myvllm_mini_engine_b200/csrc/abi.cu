@@ -59,6 +59,7 @@ int sm_count() {
 #include "decode.cu"
 #include "metadata.cu"
 #include "prefill.cu"
+#include "decode_step.cu"
 
 using namespace minikv;
 
@@ -308,6 +309,63 @@ int minikv_build_decode_tables(const int64_t* active, const int64_t* tokens, con
         out_positions, block_tables);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return cuda_fail(err, "minikv_build_decode_tables launch");
+    return MINIKV_OK;
+}
+
+// ---------------------------------------------------------------- decode step
+int minikv_rms_norm(const void* x, const void* residual, const void* weight, void* out, void* sum_out,
+                    int64_t rows, int64_t hidden, double eps, int dtype, void* stream) {
+    MINIKV_REQUIRE(dtype == MINIKV_F16 || dtype == MINIKV_BF16, MINIKV_EUNSUPPORTED, "FP16/BF16 required");
+    MINIKV_REQUIRE(rows >= 0 && hidden > 0 && hidden % 8 == 0 && hidden <= 8192, MINIKV_EINVAL,
+                   "hidden size must be a positive multiple of 8 and at most 8192");
+    MINIKV_REQUIRE(x && weight && out && (residual == nullptr) == (sum_out == nullptr), MINIKV_EINVAL,
+                   "null pointer argument (residual and sum_out go together)");
+    MINIKV_REQUIRE(aligned16(x) && aligned16(weight) && aligned16(out) && (!residual || aligned16(residual)) &&
+                       (!sum_out || aligned16(sum_out)),
+                   MINIKV_EINVAL, "tensors must be 16-byte aligned");
+    cudaError_t err = launch_rms_norm(dtype, x, residual, weight, out, sum_out, rows, (int)hidden, (float)eps,
+                                      static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_rms_norm launch");
+    return MINIKV_OK;
+}
+
+int minikv_silu_mul(const void* gate_up, void* out, int64_t rows, int64_t inter, int dtype, void* stream) {
+    MINIKV_REQUIRE(dtype == MINIKV_F16 || dtype == MINIKV_BF16, MINIKV_EUNSUPPORTED, "FP16/BF16 required");
+    MINIKV_REQUIRE(rows >= 0 && inter > 0 && inter % 8 == 0, MINIKV_EINVAL,
+                   "intermediate size must be a positive multiple of 8");
+    MINIKV_REQUIRE(gate_up && out, MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(gate_up) && aligned16(out), MINIKV_EINVAL, "tensors must be 16-byte aligned");
+    cudaError_t err = launch_silu_mul(dtype, gate_up, out, rows, inter, sm_count(), static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_silu_mul launch");
+    return MINIKV_OK;
+}
+
+int minikv_qk_rope_append(const void* qkv, int64_t qkv_stride, const void* q_weight, const void* k_weight,
+                          const void* cos, const void* sin, void* q_out, void* key_cache, void* value_cache,
+                          const int64_t* block_tables, const int64_t* token_offsets, int64_t batch, int64_t q_heads,
+                          int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                          int64_t table_width, double eps, int dtype, void* stream) {
+    MINIKV_REQUIRE(dtype == MINIKV_F16 || dtype == MINIKV_BF16, MINIKV_EUNSUPPORTED, "FP16/BF16 required");
+    MINIKV_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, MINIKV_EUNSUPPORTED,
+                   "head_dim must be 64, 128 or 256");
+    MINIKV_REQUIRE(batch >= 0 && q_heads > 0 && kv_heads > 0 && q_heads % kv_heads == 0 && num_blocks > 0 &&
+                       block_size > 0 && table_width > 0,
+                   MINIKV_EINVAL, "query heads must be divisible by KV heads");
+    MINIKV_REQUIRE(qkv_stride >= (q_heads + 2 * kv_heads) * head_dim && qkv_stride % 8 == 0, MINIKV_EINVAL,
+                   "qkv rows must hold q, k and v heads and start on 16 bytes");
+    MINIKV_REQUIRE(qkv && q_weight && k_weight && cos && sin && q_out && key_cache && value_cache && block_tables &&
+                       token_offsets,
+                   MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(qkv) && aligned16(q_weight) && aligned16(k_weight) && aligned16(cos) &&
+                       aligned16(sin) && aligned16(q_out) && aligned16(key_cache) && aligned16(value_cache),
+                   MINIKV_EINVAL, "tensors must be 16-byte aligned");
+    QkRopeParams p;
+    p.qkv = qkv; p.q_weight = q_weight; p.k_weight = k_weight; p.cos = cos; p.sin = sin; p.q_out = q_out;
+    p.key_cache = key_cache; p.value_cache = value_cache; p.tables = block_tables; p.offsets = token_offsets;
+    p.batch = batch; p.qkv_stride = qkv_stride; p.width = table_width; p.num_blocks = num_blocks;
+    p.block_size = block_size; p.q_heads = (int)q_heads; p.kv_heads = (int)kv_heads; p.eps = (float)eps;
+    cudaError_t err = launch_qk_rope_append(dtype, p, (int)head_dim, sm_count(), static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_qk_rope_append launch");
     return MINIKV_OK;
 }
 

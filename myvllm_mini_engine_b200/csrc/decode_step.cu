@@ -1,0 +1,266 @@
+// Element-wise steps of the Qwen3 batch decode step that surround the paged-KV
+// ops (mini_engine/model/native_qwen3.py:175-196 attention, :260-277 layer),
+// fused so that a 28-layer step is a few launches per layer:
+//
+//   * rms_norm_kernel        RMSNorm of rows, optionally after a residual add
+//                            (fallback.py:8-10; elementwise.py:24-31, 37-42);
+//   * silu_mul_kernel        SiLU(gate) * up over a fused gate|up row
+//                            (fallback.py:23-24; native_qwen3.py:232-240);
+//   * qk_rope_append_kernel  per-head q/k RMSNorm, rotary embedding and the
+//                            decode KV append in one pass over the fused
+//                            q|k|v projection (native_qwen3.py:178-190;
+//                            fallback.py:13-20; data.py:67-81).
+//
+// Rounding follows the eager reference: every torch op there returns the
+// 16-bit input type, so each intermediate (the sum, the normalised row, the
+// product with the weight, each rotary product and their sum) is rounded to
+// T here at the same point; reductions and transcendental functions run in
+// fp32, as torch's opmath does.
+#include "common.cuh"
+
+namespace minikv {
+
+template <typename T> struct Narrow;
+template <> struct Narrow<__nv_bfloat16> {
+    __device__ static __forceinline__ float round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+};
+template <> struct Narrow<__half> {
+    __device__ static __forceinline__ float round(float x) { return __half2float(__float2half_rn(x)); }
+};
+
+// Sum over the CTA (blockDim.x a multiple of 32, at most 1024).
+__device__ __forceinline__ float block_sum(float v, float* scratch) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    if ((threadIdx.x & 31) == 0) scratch[warp] = v;
+    __syncthreads();
+    float total = 0.f;
+    for (int w = 0; w < warps; ++w) total += scratch[w];
+    return total;
+}
+
+// One CTA per row of `hidden` elements (hidden % 8 == 0, hidden <= 8 * blockDim.x * kVecs).
+//   s   = T(x + residual)           (when residual != nullptr; written to sum_out)
+//   out = T(T(s * rsqrt(mean(s^2) + eps)) * weight)
+template <typename T, int kVecs>
+__global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ residual,
+                                                       const T* __restrict__ weight, T* __restrict__ out,
+                                                       T* __restrict__ sum_out, int hidden, float eps) {
+    __shared__ float scratch[32];
+    const int64_t row = blockIdx.x;
+    const int vecs = hidden / 8;
+    const uint4* xs = reinterpret_cast<const uint4*>(x + row * hidden);
+    const uint4* rs = residual ? reinterpret_cast<const uint4*>(residual + row * hidden) : nullptr;
+    float v[kVecs][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kVecs; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < vecs) {
+            Elem<T>::load(ld_global_nc(xs + c), v[i]);
+            if (rs) {
+                float r[8];
+                Elem<T>::load(ld_global_nc(rs + c), r);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[i][j] = Narrow<T>::round(v[i][j] + r[j]);
+                reinterpret_cast<uint4*>(sum_out + row * hidden)[c] = Elem<T>::store(v[i]);
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+        }
+    }
+    const float inv = rsqrtf(block_sum(ss, scratch) / (float)hidden + eps);
+    const uint4* ws = reinterpret_cast<const uint4*>(weight);
+    uint4* os = reinterpret_cast<uint4*>(out + row * hidden);
+#pragma unroll
+    for (int i = 0; i < kVecs; ++i) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c < vecs) {
+            float w[8];
+            Elem<T>::load(ld_global_nc(ws + c), w);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[i][j] = Narrow<T>::round(v[i][j] * inv) * w[j];
+            os[c] = Elem<T>::store(v[i]);
+        }
+    }
+}
+
+// out[r, j] = T(T(silu(g)) * u) with g = gate_up[r, j], u = gate_up[r, inter + j]
+// (inter % 8 == 0).  silu(g) = g / (1 + exp(-g)) in fp32.
+template <typename T>
+__global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gate_up, T* __restrict__ out,
+                                                       int64_t rows, int64_t inter) {
+    const int64_t vecs_per_row = inter / 8;
+    const int64_t total = rows * vecs_per_row;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / vecs_per_row, c = i % vecs_per_row;
+        const uint4* row = reinterpret_cast<const uint4*>(gate_up + r * 2 * inter);
+        float g[8], u[8];
+        Elem<T>::load(ld_global_nc(row + c), g);
+        Elem<T>::load(ld_global_nc(row + vecs_per_row + c), u);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) g[j] = Narrow<T>::round(g[j] / (1.0f + expf(-g[j]))) * u[j];
+        reinterpret_cast<uint4*>(out + r * inter)[c] = Elem<T>::store(g);
+    }
+}
+
+// Load / store kE consecutive 16-bit elements (kE = 2, 4 or 8).
+template <typename T, int kE> struct Lane;
+template <typename T> struct Lane<T, 2> {
+    __device__ static void load(const T* p, float* f) { Elem<T>::unpack(*reinterpret_cast<const uint32_t*>(p), f); }
+    __device__ static void store(T* p, const float* f) { *reinterpret_cast<uint32_t*>(p) = Elem<T>::pack(f[0], f[1]); }
+};
+template <typename T> struct Lane<T, 4> {
+    __device__ static void load(const T* p, float* f) {
+        const uint2 v = *reinterpret_cast<const uint2*>(p);
+        Elem<T>::unpack(v.x, f); Elem<T>::unpack(v.y, f + 2);
+    }
+    __device__ static void store(T* p, const float* f) {
+        *reinterpret_cast<uint2*>(p) = make_uint2(Elem<T>::pack(f[0], f[1]), Elem<T>::pack(f[2], f[3]));
+    }
+};
+template <typename T> struct Lane<T, 8> {
+    __device__ static void load(const T* p, float* f) { Elem<T>::load(*reinterpret_cast<const uint4*>(p), f); }
+    __device__ static void store(T* p, const float* f) { *reinterpret_cast<uint4*>(p) = Elem<T>::store(f); }
+};
+
+struct QkRopeParams {
+    const void* qkv;          // [batch, (q_heads + 2 kv_heads) * D] row stride qkv_stride elements
+    const void* q_weight;     // [D] q_norm weight
+    const void* k_weight;     // [D] k_norm weight
+    const void* cos;          // [batch, D/2]
+    const void* sin;          // [batch, D/2]
+    void* q_out;              // [batch, q_heads, D]
+    void* key_cache;          // [num_blocks, block_size, kv_heads, D]
+    void* value_cache;
+    const int64_t* tables;    // [batch, width]
+    const int64_t* offsets;   // [batch] position of the appended token
+    int64_t batch, qkv_stride, width, num_blocks, block_size;
+    int q_heads, kv_heads;
+    float eps;
+};
+
+// One warp per (request, head) for the q heads and the kv heads.  Lane l holds
+// elements [l*kE, (l+1)*kE); the rotary partner of element i < D/2 is i + D/2,
+// held by lane l ^ 16.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) qk_rope_append_kernel(const QkRopeParams p) {
+    constexpr int kE = D / 32;
+    constexpr int kHalf = D / 2;
+    const int lane = threadIdx.x & 31;
+    const int64_t heads = p.q_heads + p.kv_heads;
+    const int64_t jobs = p.batch * heads;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t job = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); job < jobs; job += warps) {
+        const int64_t b = job / heads;
+        const int h = (int)(job % heads);
+        const bool is_q = h < p.q_heads;
+        const T* row = static_cast<const T*>(p.qkv) + b * p.qkv_stride;
+        const T* src = row + (int64_t)h * D + lane * kE;  // k heads follow the q heads
+        float x[kE], w[kE];
+        Lane<T, kE>::load(src, x);
+        Lane<T, kE>::load(static_cast<const T*>(is_q ? p.q_weight : p.k_weight) + lane * kE, w);
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < kE; ++j) ss += x[j] * x[j];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float inv = rsqrtf(ss / (float)D + p.eps);
+#pragma unroll
+        for (int j = 0; j < kE; ++j) x[j] = Narrow<T>::round(Narrow<T>::round(x[j] * inv) * w[j]);
+        // rotary: first half  y1 = T(T(x1 c) - T(x2 s)); second half y2 = T(T(x1 s) + T(x2 c))
+        float c[kE], s[kE], y[kE];
+        const int64_t angle = b * kHalf + (int64_t)(lane & 15) * kE;
+        Lane<T, kE>::load(static_cast<const T*>(p.cos) + angle, c);
+        Lane<T, kE>::load(static_cast<const T*>(p.sin) + angle, s);
+        const bool first = lane < 16;
+#pragma unroll
+        for (int j = 0; j < kE; ++j) {
+            const float other = __shfl_xor_sync(0xffffffffu, x[j], 16);
+            if (first) {
+                y[j] = Narrow<T>::round(Narrow<T>::round(x[j] * c[j]) - Narrow<T>::round(other * s[j]));
+            } else {
+                y[j] = Narrow<T>::round(Narrow<T>::round(other * s[j]) + Narrow<T>::round(x[j] * c[j]));
+            }
+        }
+        if (is_q) {
+            Lane<T, kE>::store(static_cast<T*>(p.q_out) + (b * p.q_heads + h) * D + lane * kE, y);
+            continue;
+        }
+        // decode append of this kv head's K (rotated) and V (as projected): data.cu:89-107 guards
+        const int kvh = h - p.q_heads;
+        const int64_t logical = p.offsets[b];
+        if (logical < 0) continue;
+        const int64_t index = logical / p.block_size;
+        if (index >= p.width) continue;
+        const int64_t page = p.tables[b * p.width + index];
+        if (page < 0 || page >= p.num_blocks) continue;
+        const int64_t dst = ((page * p.block_size + logical % p.block_size) * p.kv_heads + kvh) * D + lane * kE;
+        Lane<T, kE>::store(static_cast<T*>(p.key_cache) + dst, y);
+        float v[kE];
+        Lane<T, kE>::load(row + (int64_t)(p.q_heads + p.kv_heads + kvh) * D + lane * kE, v);
+        Lane<T, kE>::store(static_cast<T*>(p.value_cache) + dst, v);
+    }
+}
+
+// ---------------------------------------------------------------- launchers
+template <typename T>
+static cudaError_t launch_rms_norm_typed(const void* x, const void* residual, const void* weight, void* out,
+                                        void* sum_out, int64_t rows, int hidden, float eps, cudaStream_t s) {
+    const int vecs = hidden / 8;
+    int threads = std::min(256, ((vecs + 31) / 32) * 32);
+    const int per = (vecs + threads - 1) / threads;
+    const T* xt = static_cast<const T*>(x);
+    const T* rt = static_cast<const T*>(residual);
+    const T* wt = static_cast<const T*>(weight);
+    T* ot = static_cast<T*>(out);
+    T* st = static_cast<T*>(sum_out);
+    const dim3 grid((unsigned)rows);
+    if (per <= 1) rms_norm_kernel<T, 1><<<grid, threads, 0, s>>>(xt, rt, wt, ot, st, hidden, eps);
+    else if (per <= 2) rms_norm_kernel<T, 2><<<grid, threads, 0, s>>>(xt, rt, wt, ot, st, hidden, eps);
+    else rms_norm_kernel<T, 4><<<grid, threads, 0, s>>>(xt, rt, wt, ot, st, hidden, eps);
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_rms_norm(int dtype, const void* x, const void* residual, const void* weight, void* out,
+                                   void* sum_out, int64_t rows, int hidden, float eps, cudaStream_t s) {
+    if (rows <= 0) return cudaSuccess;
+    if (dtype == MINIKV_BF16)
+        return launch_rms_norm_typed<__nv_bfloat16>(x, residual, weight, out, sum_out, rows, hidden, eps, s);
+    return launch_rms_norm_typed<__half>(x, residual, weight, out, sum_out, rows, hidden, eps, s);
+}
+
+static cudaError_t launch_silu_mul(int dtype, const void* gate_up, void* out, int64_t rows, int64_t inter,
+                                   int sms, cudaStream_t s) {
+    const int64_t total = rows * (inter / 8);
+    if (total <= 0) return cudaSuccess;
+    int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)sms * 8);
+    if (dtype == MINIKV_BF16)
+        silu_mul_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(
+            static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), rows, inter);
+    else
+        silu_mul_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>(static_cast<const __half*>(gate_up),
+                                                                 static_cast<__half*>(out), rows, inter);
+    return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_qk_rope_typed(const QkRopeParams& p, int head_dim, unsigned blocks, cudaStream_t s) {
+    switch (head_dim) {
+        case 64: qk_rope_append_kernel<T, 64><<<blocks, 256, 0, s>>>(p); break;
+        case 128: qk_rope_append_kernel<T, 128><<<blocks, 256, 0, s>>>(p); break;
+        default: qk_rope_append_kernel<T, 256><<<blocks, 256, 0, s>>>(p); break;
+    }
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_qk_rope_append(int dtype, const QkRopeParams& p, int head_dim, int sms, cudaStream_t s) {
+    const int64_t jobs = p.batch * (p.q_heads + p.kv_heads);
+    if (jobs <= 0) return cudaSuccess;
+    const int64_t blocks = std::min<int64_t>((jobs + 7) / 8, (int64_t)sms * 8);
+    if (dtype == MINIKV_BF16) return launch_qk_rope_typed<__nv_bfloat16>(p, head_dim, (unsigned)blocks, s);
+    return launch_qk_rope_typed<__half>(p, head_dim, (unsigned)blocks, s);
+}
+
+}  // namespace minikv

@@ -1,0 +1,260 @@
+"""Batched Qwen3 decode step over the paged KV pool.
+
+The caller of the paged-KV path in the reference engine is
+``NativeQwen3.forward_decode_batch`` (``mini_engine/model/native_qwen3.py:423-456``):
+per layer it runs RMSNorm, the q|k|v projection, q/k RMSNorm + RoPE, the
+decode KV append, paged decode attention, the output projection and the MLP.
+This module runs the same step on B200 with the sm_100a kernels of libminikv
+for everything except the dense projections, which are plain cuBLAS GEMMs
+through ``torch.mm`` (the reference's ``FusedLinear`` torch path,
+``kernels/linear.py:116-130``):
+
+    per layer (9 launches):  RMSNorm | mm(q|k|v) | qk-norm + RoPE + KV append |
+                             paged decode | mm(o) | residual + RMSNorm |
+                             mm(gate|up) | SiLU * up | mm(down)
+
+and the residual add of the MLP is fused into the next layer's RMSNorm.
+Rounding follows the eager reference (every intermediate in the model dtype),
+so the step's greedy tokens match the reference model's on the same weights
+and KV state.  The step never synchronises with the host, so it can be
+captured in a CUDA graph (:class:`DecodeGraph`).
+
+Weights use the fused layouts of ``enable_projection_fusion``
+(native_qwen3.py:362-376): ``qkv = cat(Wq, Wk, Wv)`` and ``gate_up = cat(Wg, Wu)``,
+each ``[out_features, in_features]`` like ``nn.Linear``.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+from torch.nn import functional as F
+
+from .. import _lib
+from ..cache.kv_cache import KVCachePool
+from ..kernels.paged import paged_attention
+
+
+@dataclass(frozen=True)
+class Qwen3Config:
+    """Dense Qwen3 architecture (fields of ``Qwen3Config``, native_qwen3.py:21-42)."""
+
+    vocab_size: int
+    hidden_size: int
+    intermediate_size: int
+    num_hidden_layers: int
+    num_attention_heads: int
+    num_key_value_heads: int
+    head_dim: int
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1000000.0
+    max_position_embeddings: int = 32768
+    attention_bias: bool = False
+    tie_word_embeddings: bool = True
+
+    def __post_init__(self):
+        for name in ("vocab_size", "hidden_size", "intermediate_size", "num_hidden_layers",
+                     "num_attention_heads", "num_key_value_heads", "head_dim", "max_position_embeddings"):
+            if getattr(self, name) <= 0:
+                raise ValueError(f"{name} must be positive")
+        if self.num_attention_heads % self.num_key_value_heads or self.head_dim % 2:
+            raise ValueError("Qwen3 requires divisible GQA heads and an even head_dim")
+        if self.attention_bias:
+            raise ValueError("attention bias is not supported by the decode step")
+
+    @classmethod
+    def qwen3_0_6b(cls, **overrides):
+        """Qwen3-0.6B: 28 layers, hidden 1024, 16/8 heads of 128, SwiGLU 3072, vocab 151936, tied."""
+        values = dict(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                      num_attention_heads=16, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6,
+                      rope_theta=1000000.0, max_position_embeddings=40960, tie_word_embeddings=True)
+        values.update(overrides)
+        return cls(**values)
+
+
+@dataclass
+class LayerWeights:
+    input_norm: torch.Tensor   # [H]
+    qkv: torch.Tensor          # [(Hq + 2 Hkv) D, H]
+    q_norm: torch.Tensor       # [D]
+    k_norm: torch.Tensor       # [D]
+    o: torch.Tensor            # [H, Hq D]
+    post_norm: torch.Tensor    # [H]
+    gate_up: torch.Tensor      # [2 I, H]
+    down: torch.Tensor         # [H, I]
+
+
+@dataclass
+class Qwen3Weights:
+    embed: torch.Tensor                      # [V, H]
+    norm: torch.Tensor                       # [H]
+    layers: list = field(default_factory=list)
+    lm_head_weight: torch.Tensor | None = None  # [V, H]; None when tied to embed
+
+    @property
+    def lm_head(self) -> torch.Tensor:
+        return self.embed if self.lm_head_weight is None else self.lm_head_weight
+
+    @classmethod
+    def random(cls, config: Qwen3Config, *, dtype=torch.bfloat16, device="cuda", seed=0, std=0.02):
+        """Seeded random init: every projection and the embedding ~ N(0, std), norms = 1.
+
+        Draw order (one ``torch.Generator`` on ``device``): embed, then per layer
+        qkv, o, gate_up, down, then the untied LM head if any.  Each tensor is
+        drawn in fp32 and rounded to ``dtype``.
+        """
+        cfg, device = config, torch.device(device)
+        gen = torch.Generator(device=device).manual_seed(seed)
+
+        def normal(*shape):
+            return torch.empty(shape, dtype=torch.float32, device=device).normal_(0.0, std, generator=gen).to(dtype)
+
+        def ones(n):
+            return torch.ones(n, dtype=dtype, device=device)
+
+        h, d, i = cfg.hidden_size, cfg.head_dim, cfg.intermediate_size
+        qkv_rows = (cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * d
+        embed = normal(cfg.vocab_size, h)
+        layers = []
+        for _ in range(cfg.num_hidden_layers):
+            qkv, o = normal(qkv_rows, h), normal(h, cfg.num_attention_heads * d)
+            gate_up, down = normal(2 * i, h), normal(h, i)
+            layers.append(LayerWeights(ones(h), qkv, ones(d), ones(d), o, ones(h), gate_up, down))
+        head = None if cfg.tie_word_embeddings else normal(cfg.vocab_size, h)
+        return cls(embed, ones(h), layers, head)
+
+
+def _check(status, what):
+    _lib.check(status, what)
+
+
+class Qwen3DecodeStep:
+    """One decode token per request through all layers, reading and appending the paged pool.
+
+    ``pool`` is a :class:`KVCachePool` shaped for ``config`` (layers, kv heads,
+    head_dim) in the weights' dtype and device.  ``forward_decode_batch``
+    follows ``NativeQwen3.forward_decode_batch`` (native_qwen3.py:423-456):
+    it returns the logits ``[B, vocab]`` and appends each request's new K/V at
+    ``positions[b]`` through ``block_tables[b]``.
+    """
+
+    def __init__(self, config: Qwen3Config, weights: Qwen3Weights, pool: KVCachePool):
+        shape = pool.shape
+        if (shape.num_layers, shape.num_kv_heads, shape.head_dim) != (
+                config.num_hidden_layers, config.num_key_value_heads, config.head_dim):
+            raise ValueError("KV cache architecture mismatch")
+        if pool.key.device != weights.embed.device or pool.dtype != weights.embed.dtype:
+            raise ValueError("cache must match model device and dtype")
+        if weights.embed.dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("the decode step runs in FP16/BF16")
+        if config.head_dim not in (64, 128, 256):
+            raise ValueError("the decode step supports head_dim 64, 128 or 256")
+        self.config, self.weights, self.pool = config, weights, pool
+        self.code = _lib.dtype_code(weights.embed.dtype)
+        self.lib = _lib.load()
+
+    # ------------------------------------------------------------ fused ops
+    def _rms(self, x, residual, weight, out, sum_out, stream):
+        _check(self.lib.minikv_rms_norm(x.data_ptr(), None if residual is None else residual.data_ptr(),
+                                        weight.data_ptr(), out.data_ptr(),
+                                        None if sum_out is None else sum_out.data_ptr(), x.shape[0],
+                                        x.shape[1], self.config.rms_norm_eps, self.code, stream), "rms_norm")
+
+    def forward_decode_batch(self, input_ids, block_tables, positions):
+        """Logits of one decode step (native_qwen3.py:423-456)."""
+        cfg, pool, w = self.config, self.pool, self.weights
+        if input_ids.ndim != 1 or input_ids.dtype != torch.long or input_ids.numel() == 0:
+            raise ValueError("input_ids must be a nonempty 1D int64 batch")
+        if positions.ndim != 1 or positions.shape != input_ids.shape or positions.dtype != torch.long:
+            raise ValueError("positions must be int64 with one value per request")
+        if block_tables.ndim != 2 or block_tables.shape[0] != input_ids.shape[0]:
+            raise ValueError("block_tables must be [batch, max_blocks]")
+        if block_tables.dtype != torch.long or not block_tables.is_contiguous():
+            raise ValueError("block_tables must be a contiguous int64 tensor")
+        device = w.embed.device
+        if input_ids.device != device or positions.device != device or block_tables.device != device:
+            raise ValueError("decode inputs must be on the model device")
+        capturing = torch.cuda.is_current_stream_capturing()
+        if not capturing and (bool((positions < 0).any())
+                              or bool((positions + 1 > cfg.max_position_embeddings).any())):
+            raise ValueError("decode positions exceed model context")
+        batch = input_ids.shape[0]
+        hq, hkv, dim = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        shape = pool.shape
+        stream = torch.cuda.current_stream(device).cuda_stream
+        x = F.embedding(input_ids, w.embed)
+        inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim))
+        angles = positions.to(dtype=torch.float32)[:, None] * inv_freq[None, :]
+        cos, sin = angles.cos().to(x.dtype), angles.sin().to(x.dtype)
+        lengths = positions + 1
+        h = torch.empty_like(x)
+        self._rms(x, None, w.layers[0].input_norm, h, None, stream)
+        residual = x
+        for index, layer in enumerate(w.layers):
+            qkv = torch.mm(h, layer.qkv.t())
+            q = torch.empty((batch, hq, dim), dtype=x.dtype, device=device)
+            _check(self.lib.minikv_qk_rope_append(
+                qkv.data_ptr(), qkv.stride(0), layer.q_norm.data_ptr(), layer.k_norm.data_ptr(), cos.data_ptr(),
+                sin.data_ptr(), q.data_ptr(), pool.key[index].data_ptr(), pool.value[index].data_ptr(),
+                block_tables.data_ptr(), positions.data_ptr(), batch, hq, hkv, dim, shape.num_blocks,
+                shape.block_size, block_tables.shape[1], cfg.rms_norm_eps, self.code, stream), "qk_rope_append")
+            attention = paged_attention(q, pool.key[index], pool.value[index], block_tables, lengths,
+                                        shape.block_size, validate=False)
+            o = torch.mm(attention.view(batch, hq * dim), layer.o.t())
+            summed, normalized = torch.empty_like(x), torch.empty_like(x)
+            self._rms(o, residual, layer.post_norm, normalized, summed, stream)
+            gate_up = torch.mm(normalized, layer.gate_up.t())
+            act = torch.empty((batch, cfg.intermediate_size), dtype=x.dtype, device=device)
+            _check(self.lib.minikv_silu_mul(gate_up.data_ptr(), act.data_ptr(), batch, cfg.intermediate_size,
+                                            self.code, stream), "silu_mul")
+            down = torch.mm(act, layer.down.t())
+            following = w.layers[index + 1].input_norm if index + 1 < len(w.layers) else w.norm
+            residual, h = torch.empty_like(x), torch.empty_like(x)
+            self._rms(down, summed, following, h, residual, stream)
+        return torch.mm(h, w.lm_head.t())
+
+    def greedy(self, input_ids, block_tables, positions):
+        """Greedy next token of every request (argmax of the step's logits)."""
+        return torch.argmax(self.forward_decode_batch(input_ids, block_tables, positions), dim=-1)
+
+
+class DecodeGraph:
+    """A greedy decode step captured as one CUDA graph for a fixed batch and table width.
+
+    The static inputs (``input_ids``, ``positions``, ``block_tables``) are
+    refilled before every replay, as the reference's ``DecodeGraphBucket``
+    does (``mini_engine/engine/cuda_graph.py:196-275``); the output is
+    ``next_ids``.  The decode workspace of the capture stream is created by a
+    warm-up step on that stream before capture.
+    """
+
+    def __init__(self, step: Qwen3DecodeStep, batch: int, table_width: int, *, warmup_tables=None):
+        device = step.weights.embed.device
+        self.step = step
+        self.device = device
+        self.input_ids = torch.zeros(batch, dtype=torch.long, device=device)
+        self.positions = torch.zeros(batch, dtype=torch.long, device=device)
+        self.block_tables = torch.full((batch, table_width), -1, dtype=torch.long, device=device)
+        if warmup_tables is not None:
+            self.block_tables.copy_(warmup_tables)
+        self.stream = torch.cuda.Stream(device)
+        self.graph = torch.cuda.CUDAGraph()
+        self.stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(self.stream):
+            # warm-up: allocates the stream's decode workspace and cuBLAS state outside the graph
+            step.greedy(self.input_ids, self.block_tables, self.positions)
+        self.stream.synchronize()
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self.next_ids = step.greedy(self.input_ids, self.block_tables, self.positions)
+        torch.cuda.current_stream(device).wait_stream(self.stream)
+
+    def load(self, input_ids, positions, block_tables):
+        """Copy one step's metadata into the static buffers (host or device tensors)."""
+        self.input_ids.copy_(input_ids, non_blocking=True)
+        self.positions.copy_(positions, non_blocking=True)
+        self.block_tables.copy_(block_tables, non_blocking=True)
+
+    def replay(self):
+        self.graph.replay()
+        return self.next_ids

@@ -289,3 +289,69 @@ def metadata_random(seed=107, requests=24, block_size=16, max_start=700, max_chu
     tokens = [[int(t) for t in gen.integers(0, 151936, size=c)] for c in chunks]
     return {"tokens": tokens, "tables": tables, "starts": starts, "block_size": block_size,
             "num_blocks": blocks}
+
+
+# ------------------------------------------------------------------- decode step
+
+def qwen3_weights(config, dtype, *, seed, std=0.02, device="cpu"):
+    """Seeded Qwen3 weights in the fused layouts of enable_projection_fusion.
+
+    Projections and the embedding ~ N(0, std) (numpy PCG64, drawn in the order
+    embed, then per layer q|k|v, o, gate|up, down), norms = 1.  Returns a
+    namespace with the attributes the decode step and the oracle read.
+    """
+    from types import SimpleNamespace
+
+    gen = rng(seed)
+    cfg = config
+
+    def normal(*shape):
+        return (randn(gen, shape, torch.float32) * std).to(dtype).to(device)
+
+    def ones(n):
+        return torch.ones(n, dtype=dtype, device=device)
+
+    h, d, i = cfg.hidden_size, cfg.head_dim, cfg.intermediate_size
+    embed = normal(cfg.vocab_size, h)
+    layers = []
+    for _ in range(cfg.num_hidden_layers):
+        qkv = normal((cfg.num_attention_heads + 2 * cfg.num_key_value_heads) * d, h)
+        o = normal(h, cfg.num_attention_heads * d)
+        gate_up, down = normal(2 * i, h), normal(h, i)
+        layers.append(SimpleNamespace(input_norm=ones(h), qkv=qkv, q_norm=ones(d), k_norm=ones(d), o=o,
+                                      post_norm=ones(h), gate_up=gate_up, down=down))
+    return SimpleNamespace(embed=embed, norm=ones(h), layers=layers, lm_head=embed)
+
+
+def qwen3_tiny_config():
+    """A small architecture of the Qwen3 family for CPU golden runs of the reference model."""
+    from types import SimpleNamespace
+
+    return SimpleNamespace(vocab_size=128, hidden_size=32, intermediate_size=64, num_hidden_layers=2,
+                           num_attention_heads=4, num_key_value_heads=2, head_dim=8, rms_norm_eps=1e-6,
+                           rope_theta=1000000.0, max_position_embeddings=4096, tie_word_embeddings=True)
+
+
+def qwen3_decode_case(config, dtype, *, contexts, block_size, seed, pool_slack=1.25):
+    """One batched decode step: random N(0,1) KV history of ``contexts[b]`` tokens, token ids U[0, vocab).
+
+    Request b appends at position ``contexts[b]``; its pages are a slice of a
+    seeded permutation of the pool.  Pools are ``[layers, blocks, block_size,
+    kv_heads, head_dim]``.
+    """
+    gen = rng(seed)
+    pages = [(c + 1 + block_size - 1) // block_size for c in contexts]
+    width = max(pages)
+    blocks = math.ceil(pool_slack * sum(pages))
+    perm = gen.permutation(blocks).astype(np.int64)
+    table = np.full((len(contexts), width), -1, dtype=np.int64)
+    used = 0
+    for b, n in enumerate(pages):
+        table[b, :n] = perm[used:used + n]
+        used += n
+    shape = (config.num_hidden_layers, blocks, block_size, config.num_key_value_heads, config.head_dim)
+    key_pool, value_pool = randn(gen, shape, dtype), randn(gen, shape, dtype)
+    ids = torch.from_numpy(gen.integers(0, config.vocab_size, size=len(contexts)).astype(np.int64))
+    return {"input_ids": ids, "positions": torch.tensor(contexts, dtype=torch.int64),
+            "block_tables": torch.from_numpy(table), "key_pool": key_pool, "value_pool": value_pool,
+            "block_size": block_size}

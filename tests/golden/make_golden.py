@@ -16,7 +16,9 @@ Fixtures written next to this file:
     ``write_kv_cache_slots`` (torch paths);
   * ``golden_prefill.npz``  -- ``kernels/prefill.py::paged_prefill_attention``
     (backend="torch"), including BASELINE config 4 (subsampled rows);
-  * ``golden_metadata.json`` -- ``engine/batch.py::PrefillBatch.from_sequences``.
+  * ``golden_metadata.json`` -- ``engine/batch.py::PrefillBatch.from_sequences``;
+  * ``golden_qwen3.npz``    -- ``model/native_qwen3.py::NativeQwen3.forward_decode_batch``
+    (all backends torch, projections fused) on a small Qwen3-family model.
 Raw bit patterns are stored for fp16/bf16 tensors (as int16).
 """
 
@@ -151,6 +153,51 @@ def prefill_fixtures(prefill, data, PrefillBatch):
     return out
 
 
+def qwen3_fixtures():
+    """NativeQwen3.forward_decode_batch (native_qwen3.py:423-456), all backends torch, projections fused."""
+    from mini_engine.model.native_qwen3 import NativeQwen3, Qwen3Config
+
+    out = {}
+    cfg = cases.qwen3_tiny_config()
+    ref_cfg = Qwen3Config(**{k: getattr(cfg, k) for k in Qwen3Config.__dataclass_fields__ if hasattr(cfg, k)})
+    for name in ("fp32", "bf16"):
+        dtype = DTYPES[name]
+        w = cases.qwen3_weights(cfg, dtype, seed=501)
+        model = NativeQwen3(ref_cfg, prefill_backend="math", decode_backend="torch", elementwise_backend="torch",
+                            data_backend="torch", linear_backend="torch")
+        q_rows, kv_rows = cfg.num_attention_heads * cfg.head_dim, cfg.num_key_value_heads * cfg.head_dim
+        state = {"model.embed_tokens.weight": w.embed, "model.norm.weight": w.norm, "lm_head.weight": w.embed}
+        for i, layer in enumerate(w.layers):
+            p = f"model.layers.{i}."
+            state[p + "self_attn.q_proj.weight"] = layer.qkv[:q_rows]
+            state[p + "self_attn.k_proj.weight"] = layer.qkv[q_rows:q_rows + kv_rows]
+            state[p + "self_attn.v_proj.weight"] = layer.qkv[q_rows + kv_rows:]
+            state[p + "self_attn.o_proj.weight"] = layer.o
+            state[p + "self_attn.q_norm.weight"] = layer.q_norm
+            state[p + "self_attn.k_norm.weight"] = layer.k_norm
+            state[p + "mlp.gate_proj.weight"] = layer.gate_up[:cfg.intermediate_size]
+            state[p + "mlp.up_proj.weight"] = layer.gate_up[cfg.intermediate_size:]
+            state[p + "mlp.down_proj.weight"] = layer.down
+            state[p + "input_layernorm.weight"] = layer.input_norm
+            state[p + "post_attention_layernorm.weight"] = layer.post_norm
+        model = model.to(dtype)
+        model.load_state_dict({k: v.clone() for k, v in state.items()}, strict=True)
+        model.enable_projection_fusion()
+        c = cases.qwen3_decode_case(cfg, dtype, contexts=(5, 11, 2, 16), block_size=4, seed=502)
+        cache = model.create_cache(c["key_pool"].shape[1], c["block_size"])
+        cache.key.copy_(c["key_pool"])
+        cache.value.copy_(c["value_pool"])
+        logits = model.forward_decode_batch(c["input_ids"], cache, c["block_tables"], c["positions"])
+        key = f"qwen3_{name}"
+        out[key + "/inputs_sha256"] = np.array(cases.sha256_of(
+            [c["input_ids"], c["positions"], c["block_tables"], c["key_pool"], c["value_pool"], w.embed]
+            + [t for layer in w.layers for t in (layer.qkv, layer.o, layer.gate_up, layer.down)]))
+        out[key + "/logits"] = raw(logits)
+        out[key + "/key_pool"] = raw(cache.key)
+        out[key + "/value_pool"] = raw(cache.value)
+    return out
+
+
 def metadata_fixtures(PrefillBatch):
     names = ("input_ids", "positions", "slot_mapping", "cu_seqlens_q", "query_starts",
              "context_lens", "block_tables")
@@ -186,6 +233,7 @@ def main():
     np.savez_compressed(HERE / "golden_decode.npz", **decode_fixtures(paged, data, compare))
     np.savez_compressed(HERE / "golden_kv.npz", **kv_fixtures(data))
     np.savez_compressed(HERE / "golden_prefill.npz", **prefill_fixtures(prefill, data, PrefillBatch))
+    np.savez_compressed(HERE / "golden_qwen3.npz", **qwen3_fixtures())
     (HERE / "golden_metadata.json").write_text(json.dumps(metadata_fixtures(PrefillBatch)))
     for path in sorted(HERE.glob("golden_*")):
         print(f"{path.name}: {path.stat().st_size} bytes")

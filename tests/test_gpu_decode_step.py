@@ -1,0 +1,226 @@
+"""The Qwen3 batch decode step (BASELINE config 5 architecture) against the reference model.
+
+Checker: ``oracle.qwen3`` -- the reference's ``NativeQwen3.forward_decode_batch``
+with every backend "torch", pinned bit-exact to the reference on the CPU
+(test_oracle_golden.py) -- run on the same GPU with the same weights and KV
+state, which is how the reference validates its own model paths.  The decode
+step under test runs the sm_100a kernels (fused q/k-norm + RoPE + KV append,
+paged decode, RMSNorm, SiLU*up) and cuBLAS projections.
+
+Bars:
+  * each fused kernel against the reference's op chain on identical inputs:
+    SiLU*up within one ulp, RMSNorm and q/k RMSNorm + RoPE within two (their
+    fp32 reductions run in their own order, and a one-ulp change of the
+    rounded normalised value can grow to two through the weight product),
+    the appended V rows bit-exact;
+  * the whole 28-layer step with the reference's decode attention in place of
+    the paged decode kernel is bit-identical to the reference model: every
+    other kernel of the step (and the cuBLAS projections) reproduces the
+    reference's rounding exactly;
+  * with the paged decode kernel, whose fp32 sums run in another order than
+    torch's, the step differs from the reference only by that rounding,
+    amplified through 28 random-weight layers (about one bf16 ulp of a logit
+    after one layer, ~0.13 after 28): logits within atol=0.25, rtol=0.01
+    (twice the largest difference seen; the reference's own model check
+    uses 0.125 on trained weights, VALIDATION_AND_BENCHMARKS.md:11), the
+    appended K/V rows within the same bound, nothing else in the pools
+    changed, and identical greedy tokens for every request whose reference
+    top-2 margin exceeds twice the step's largest logit difference, over
+    several steps that feed the chosen tokens back in (closer calls are
+    near-ties at the bf16 resolution of the logits and are reported);
+  * the CUDA-graph replay gives the same tokens as the eager step.
+"""
+
+import pytest
+import torch
+
+import cases
+from myvllm_mini_engine_b200 import _lib
+from myvllm_mini_engine_b200.cache.kv_cache import KVCachePool
+from myvllm_mini_engine_b200.engine.qwen3 import DecodeGraph, Qwen3Config, Qwen3DecodeStep, Qwen3Weights
+from oracle import qwen3 as ref
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 0.25, 0.01
+
+
+def ulps(a, b):
+    """Distance in units of the last place between two bf16/fp16 tensors of equal shape."""
+    def ordered(t):
+        i = t.contiguous().view(torch.int16).to(torch.int32)
+        return torch.where(i < 0, -32768 - i, i)
+    return (ordered(a) - ordered(b)).abs()
+
+
+def stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("hidden", [1024, 4096])
+def test_rms_norm_and_residual_match_reference_rounding(cuda_device, dtype, hidden):
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(37, hidden, device="cuda", generator=gen).to(dtype)
+    r = torch.randn(37, hidden, device="cuda", generator=gen).to(dtype)
+    w = (1 + 0.1 * torch.randn(hidden, device="cuda", generator=gen)).to(dtype)
+    lib, code = _lib.load(), _lib.dtype_code(dtype)
+    out, summed = torch.empty_like(x), torch.empty_like(x)
+    _lib.check(lib.minikv_rms_norm(x.data_ptr(), None, w.data_ptr(), out.data_ptr(), None, 37, hidden, 1e-6,
+                                   code, stream()), "rms_norm")
+    # the normalised row is rounded before the weight product: one ulp there can
+    # become two after a product with a weight below 1 that drops a binade
+    expected = ref.rms_norm(x, w, 1e-6)
+    assert ulps(out, expected).max().item() <= 2
+    assert (out != expected).float().mean().item() < 1e-3
+    _lib.check(lib.minikv_rms_norm(x.data_ptr(), r.data_ptr(), w.data_ptr(), out.data_ptr(), summed.data_ptr(),
+                                   37, hidden, 1e-6, code, stream()), "residual rms_norm")
+    assert torch.equal(summed, x + r)
+    expected = ref.rms_norm(x + r, w, 1e-6)
+    assert ulps(out, expected).max().item() <= 2
+    assert (out != expected).float().mean().item() < 1e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_silu_mul_matches_reference(cuda_device, dtype):
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    gate_up = (3 * torch.randn(29, 2 * 3072, device="cuda", generator=gen)).to(dtype)
+    out = torch.empty(29, 3072, dtype=dtype, device="cuda")
+    lib = _lib.load()
+    _lib.check(lib.minikv_silu_mul(gate_up.data_ptr(), out.data_ptr(), 29, 3072, _lib.dtype_code(dtype), stream()),
+               "silu_mul")
+    gate, up = (part.contiguous() for part in gate_up.chunk(2, dim=-1))
+    expected = ref.silu_and_mul(gate, up)
+    assert ulps(out, expected).max().item() <= 1
+    assert (out != expected).float().mean().item() < 1e-3
+
+
+@pytest.mark.parametrize("dim", [64, 128, 256])
+def test_qk_rope_append_matches_reference_chain(cuda_device, dim):
+    dtype, hq, hkv, bs = torch.bfloat16, 16, 8, 16
+    cfg = Qwen3Config(vocab_size=64, hidden_size=256, intermediate_size=256, num_hidden_layers=1,
+                      num_attention_heads=hq, num_key_value_heads=hkv, head_dim=dim)
+    c = cases.qwen3_decode_case(cfg, dtype, contexts=(0, 15, 16, 300, 77), block_size=bs, seed=11)
+    batch = len(c["positions"])
+    gen = torch.Generator(device="cuda").manual_seed(9)
+    qkv = torch.randn(batch, (hq + 2 * hkv) * dim, device="cuda", generator=gen).to(dtype)
+    qw = (1 + 0.1 * torch.randn(dim, device="cuda", generator=gen)).to(dtype)
+    kw = (1 + 0.1 * torch.randn(dim, device="cuda", generator=gen)).to(dtype)
+    positions, tables = c["positions"].cuda(), c["block_tables"].cuda()
+    cos, sin = ref.rope_tables(positions, dim, cfg.rope_theta, dtype)
+    kc, vc = c["key_pool"][0].cuda(), c["value_pool"][0].cuda()
+    kc_ref, vc_ref = kc.clone(), vc.clone()
+    q = torch.empty(batch, hq, dim, dtype=dtype, device="cuda")
+    lib = _lib.load()
+    _lib.check(lib.minikv_qk_rope_append(qkv.data_ptr(), qkv.stride(0), qw.data_ptr(), kw.data_ptr(), cos.data_ptr(),
+                                         sin.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                         tables.data_ptr(), positions.data_ptr(), batch, hq, hkv, dim, kc.shape[0],
+                                         bs, tables.shape[1], 1e-6, _lib.BF16, stream()), "qk_rope_append")
+    q_raw, k_raw, v_raw = qkv.split((hq * dim, hkv * dim, hkv * dim), dim=-1)
+    q_ref = ref.rms_norm(q_raw.contiguous().view(batch, hq, dim), qw, 1e-6)
+    k_ref = ref.rms_norm(k_raw.contiguous().view(batch, hkv, dim), kw, 1e-6)
+    q_ref, k_ref = ref.apply_rope(q_ref, k_ref, cos.unsqueeze(1), sin.unsqueeze(1))
+    ref.append_rows(kc_ref, vc_ref, tables, positions, k_ref, v_raw.contiguous().view(batch, hkv, dim), bs)
+    assert ulps(q, q_ref).max().item() <= 2
+    assert ulps(kc, kc_ref).max().item() <= 2
+    assert torch.equal(vc, vc_ref)
+    assert _lib.device_status() == 0
+
+
+def model_case(batch_contexts, seed, layers=None):
+    cfg = Qwen3Config.qwen3_0_6b() if layers is None else Qwen3Config.qwen3_0_6b(num_hidden_layers=layers)
+    weights = Qwen3Weights.random(cfg, dtype=torch.bfloat16, device="cuda", seed=seed)
+    bs = 16
+    pages = [(c + 1 + 3 + bs - 1) // bs for c in batch_contexts]  # room for 3 more steps
+    width = max(pages)
+    blocks = int(1.2 * sum(pages)) + 1
+    gen = torch.Generator(device="cuda").manual_seed(seed + 1)
+    perm = torch.randperm(blocks, device="cuda", generator=gen)
+    tables = torch.full((len(batch_contexts), width), -1, dtype=torch.int64, device="cuda")
+    used = 0
+    for b, n in enumerate(pages):
+        tables[b, :n] = perm[used:used + n]
+        used += n
+    pool = KVCachePool(cfg.num_hidden_layers, blocks, bs, cfg.num_key_value_heads, cfg.head_dim,
+                       dtype=torch.bfloat16, device="cuda")
+    pool.key.normal_(generator=gen)
+    pool.value.normal_(generator=gen)
+    ids = torch.randint(0, cfg.vocab_size, (len(batch_contexts),), device="cuda", generator=gen)
+    positions = torch.tensor(batch_contexts, dtype=torch.int64, device="cuda")
+    return cfg, weights, pool, tables, ids, positions
+
+
+def appended(pool_tensor, tables, positions, block_size):
+    """The rows a decode step appends: ``[layers, batch, kv_heads, head_dim]``."""
+    pages = tables.gather(1, (positions // block_size)[:, None]).squeeze(1)
+    return pages, positions % block_size, pool_tensor[:, pages, positions % block_size]
+
+
+def test_decode_step_matches_reference_model_over_greedy_steps(cuda_device):
+    # 48 requests: block boundaries, short and long contexts, and enough requests
+    # that some are decided beyond the near-tie margin at every step
+    contexts = (1, 17, 255, 256, 700, 1031, 1500, 2047) + tuple(int(x) for x in cases.rng(34).integers(1, 2048, 40))
+    cfg, weights, pool, tables, ids, positions = model_case(contexts, seed=31)
+    ref_key, ref_value = pool.key.clone(), pool.value.clone()
+    step = Qwen3DecodeStep(cfg, weights, pool)
+    ours_ids, ref_ids = ids, ids.clone()
+    bs = pool.shape.block_size
+    for i in range(3):
+        before = (pool.key.clone(), pool.value.clone())
+        logits = step.forward_decode_batch(ours_ids, tables, positions)
+        expected = ref.decode_step(cfg, weights, ref_ids, ref_key, ref_value, tables, positions)
+        torch.testing.assert_close(logits.float(), expected.float(), atol=ATOL, rtol=RTOL)
+        margin = ref.top2_margin(expected)
+        diff = (logits.float() - expected.float()).abs().max().item()
+        ours_ids, ref_ids = logits.argmax(-1), expected.argmax(-1)
+        decided = margin > 2 * diff
+        assert torch.equal(ours_ids[decided], ref_ids[decided]), (
+            f"step {i}: greedy ids differ; reference top-2 margins {margin.tolist()}, max |dlogit| {diff:.4f}")
+        print(f"step {i}: {int(decided.sum())}/{len(contexts)} requests beyond the near-tie margin, "
+              f"ids equal on all: {torch.equal(ours_ids, ref_ids)}, max |dlogit| {diff:.4f}")
+        ref_ids = ours_ids.clone()  # both paths continue from the same tokens
+        # the appended K/V rows agree within the model tolerance; nothing else in the pools changed
+        for mine, theirs, old in ((pool.key, ref_key, before[0]), (pool.value, ref_value, before[1])):
+            pages, slots, rows = appended(mine, tables, positions, bs)
+            torch.testing.assert_close(rows.float(), appended(theirs, tables, positions, bs)[2].float(),
+                                       atol=ATOL, rtol=RTOL)
+            rest = mine.clone()
+            rest[:, pages, slots] = old[:, pages, slots]
+            assert torch.equal(rest, old)
+            del rest
+        positions = positions + 1
+    assert _lib.device_status() == 0
+
+
+def test_decode_step_is_bit_exact_with_the_reference_attention(cuda_device, monkeypatch):
+    """Isolates the paged decode kernel: with the reference's attention the step equals the reference."""
+    import myvllm_mini_engine_b200.engine.qwen3 as engine_qwen3
+    from oracle import paged_decode
+
+    contexts = (1, 17, 255, 700, 2047)
+    cfg, weights, pool, tables, ids, positions = model_case(contexts, seed=33)
+    ref_key, ref_value = pool.key.clone(), pool.value.clone()
+    monkeypatch.setattr(engine_qwen3, "paged_attention",
+                        lambda q, kc, vc, t, lens, bs, validate=False: paged_decode.paged_attention(q, kc, vc, t, lens, bs))
+    logits = Qwen3DecodeStep(cfg, weights, pool).forward_decode_batch(ids, tables, positions)
+    expected = ref.decode_step(cfg, weights, ids, ref_key, ref_value, tables, positions)
+    assert torch.equal(logits, expected)
+    assert torch.equal(pool.key, ref_key) and torch.equal(pool.value, ref_value)
+
+
+def test_decode_graph_replays_the_eager_step(cuda_device):
+    contexts = (5, 63, 64, 900)
+    cfg, weights, pool, tables, ids, positions = model_case(contexts, seed=41, layers=4)
+    step = Qwen3DecodeStep(cfg, weights, pool)
+    graph = DecodeGraph(step, len(contexts), tables.shape[1])
+    for i in range(2):
+        state = (pool.key.clone(), pool.value.clone())
+        graph.load(ids, positions, tables)
+        replayed = graph.replay().clone()
+        after = (pool.key.clone(), pool.value.clone())
+        pool.key.copy_(state[0])
+        pool.value.copy_(state[1])
+        eager = step.greedy(ids, tables, positions)
+        assert torch.equal(replayed, eager), f"step {i}"
+        assert torch.equal(pool.key, after[0]) and torch.equal(pool.value, after[1])
+        ids, positions = replayed, positions + 1
+    assert _lib.device_status() == 0

@@ -196,3 +196,29 @@ def test_decode_bucket_metadata_padding_rows():
                                           padding_pages=[10, 11, 12, 13])
     assert got["input_ids"] == [7, 9, 0, 0] and got["positions"] == [17, 3, 0, 0]
     assert got["block_tables"] == [[4, 5, -1], [6, -1, -1], [12, -1, -1], [13, -1, -1]]
+
+
+QWEN3 = np.load(GOLDEN / "golden_qwen3.npz")
+
+
+@pytest.mark.parametrize("name", ["fp32", "bf16"])
+def test_decode_step_oracle_matches_reference_model(name):
+    """oracle.qwen3.decode_step == NativeQwen3.forward_decode_batch (torch backends, fused projections)."""
+    from oracle import qwen3
+
+    dtype = DTYPES[name]
+    cfg = cases.qwen3_tiny_config()
+    w = cases.qwen3_weights(cfg, dtype, seed=501)
+    c = cases.qwen3_decode_case(cfg, dtype, contexts=(5, 11, 2, 16), block_size=4, seed=502)
+    key = f"qwen3_{name}"
+    inputs = ([c["input_ids"], c["positions"], c["block_tables"], c["key_pool"], c["value_pool"], w.embed]
+              + [t for layer in w.layers for t in (layer.qkv, layer.o, layer.gate_up, layer.down)])
+    assert cases.sha256_of(inputs) == str(QWEN3[key + "/inputs_sha256"])
+    kp, vp = c["key_pool"].clone(), c["value_pool"].clone()
+    logits = qwen3.decode_step(cfg, w, c["input_ids"], kp, vp, c["block_tables"], c["positions"])
+    assert torch.equal(logits, cooked(QWEN3[key + "/logits"], logits))
+    assert torch.equal(kp, cooked(QWEN3[key + "/key_pool"], kp))
+    assert torch.equal(vp, cooked(QWEN3[key + "/value_pool"], vp))
+    # the step appended exactly one row per request and layer
+    changed = (kp != c["key_pool"]).any(dim=-1).any(dim=-1).sum().item()
+    assert changed == cfg.num_hidden_layers * len(c["positions"])
