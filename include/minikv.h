@@ -74,6 +74,24 @@ int minikv_paged_decode(const void* query, const void* key_cache, const void* va
                         int64_t num_blocks, int64_t block_size, int64_t table_width,
                         int dtype, void* stream);
 
+/* minikv_paged_decode for a launch chain: the same arguments and results,
+ * for a caller whose context_lens and block_tables were written before the
+ * previous kernel on the stream started (typically that kernel is the KV
+ * append of the same step, as in NativeQwen3.forward_decode_batch,
+ * native_qwen3.py:185-195).  The kernel is launched with programmatic
+ * dependent launch and reads the lengths and page tables while the previous
+ * kernel finishes; it reads KV, q and the workspace only after that kernel has
+ * completed.  Every libminikv kernel is a chained launch that lets its
+ * successor start early, so calling this right after minikv_kv_append_batch
+ * or minikv_qk_rope_append overlaps the decode prologue with the append.
+ * No counterpart in the reference (its decode is launched after a full
+ * stream serialisation, bindings.cpp:152-184). */
+int minikv_paged_decode_chained(const void* query, const void* key_cache, const void* value_cache,
+                                const int64_t* block_tables, const int64_t* context_lens, void* out,
+                                void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
+                                int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                int64_t table_width, int dtype, void* stream);
+
 /* Same decode attention, for callers that cannot allocate device memory when
  * they call (a CUDA graph being captured under a framework that owns every
  * allocation, a serving loop that bans cudaMalloc after start-up, a cgo/JNI

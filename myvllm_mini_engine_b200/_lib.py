@@ -30,6 +30,7 @@ SIGNATURES = {
     "minikv_device_status": (_int, [ctypes.POINTER(ctypes.c_uint), _int, _p]),
     "minikv_paged_decode_workspace_bytes": (_i64, [_i64] * 7 + [_int]),
     "minikv_paged_decode": (_int, [_p] * 6 + [_p, _i64] + [_i64] * 7 + [_int, _p]),
+    "minikv_paged_decode_chained": (_int, [_p] * 6 + [_p, _i64] + [_i64] * 7 + [_int, _p]),
     "minikv_paged_decode_noalloc": (_int, [_p] * 6 + [_i64] * 7 + [_int, _p]),
     "minikv_kv_scatter_slots": (_int, [_p] * 5 + [_i64] * 7 + [_int, _p]),
     "minikv_kv_append_batch": (_int, [_p] * 6 + [_i64] * 8 + [_int, _p]),

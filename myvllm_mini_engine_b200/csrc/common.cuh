@@ -168,6 +168,34 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
     return p;
 }
 
+// --------------------------------------------- programmatic dependent launch
+// Kernels of a launch chain are launched with programmatic stream
+// serialization (launch_chained): such a kernel may start while the previous
+// kernel on the stream is still running, so it must execute griddep_wait()
+// before it touches anything that kernel (or an earlier one) writes.  A kernel
+// that calls griddep_launch_dependents() lets the next chained kernel start
+// early.  Launched without the attribute, both instructions are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_chained(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                  Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 __device__ __forceinline__ uint4 ld_global_nc(const void* p) {
     uint4 v;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

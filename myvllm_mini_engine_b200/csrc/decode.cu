@@ -66,6 +66,7 @@ struct DecodeParams {
     int tile_tokens;      // TT, multiple of the consumer's sub-chunk, <= 64
     int stages;
     int row_stride;       // shared-memory stride of one token row (padded)
+    int early_prologue;   // 1: lens/tables predate the previous kernel; read them before griddep_wait
     float scale_log2;     // log2(e) / sqrt(D)
 };
 
@@ -374,6 +375,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t cap = (int64_t)p.table_width * p.block_size;
 
+    // Chained launch: with early_prologue the lengths, the tile split and the
+    // page-table reads below overlap the previous kernel (the KV append of the
+    // same step), and the wait comes just before the first KV copy / q read.
+    if (!p.early_prologue) griddep_wait();
     tile_prefix(p.lens, B, cap, TT, prefix, lens_s, warp_sums);
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
@@ -386,6 +391,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
 
     const int total = prefix[B];
     const int G = gridDim.x, c = blockIdx.x;
+    if (p.early_prologue && warp < kConsumerWarps) griddep_wait();
     // Requests with no usable tokens get zero rows (reference: count 0 -> 0).
     if (blockIdx.y == 0 && warp < kConsumerWarps) {
         for (int b = c; b < B; b += G) {
@@ -450,6 +456,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                 for (; j < TT; ++j) rows[j] = -1;
             }
             __syncwarp();
+            if (p.early_prologue && w0 == tile_lo) griddep_wait();  // KV rows may come from the previous kernel
             const int count = min(kWindowTiles, tile_hi - w0);
             for (int i = 0; i < count; ++i, ++gt) {
                 const int slot = gt % NS;
@@ -623,8 +630,7 @@ static cudaError_t launch_decode_typed(const DecodeParams& p, const DecodePlan& 
     auto kernel = paged_decode_kernel<T, D, Consumer>;
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.smem_bytes);
     if (err != cudaSuccess) return err;
-    kernel<<<dim3(plan.grid, plan.head_groups), kDecodeThreads, plan.smem_bytes, stream>>>(p);
-    return cudaGetLastError();
+    return launch_chained(kernel, dim3(plan.grid, plan.head_groups), dim3(kDecodeThreads), plan.smem_bytes, stream, p);
 }
 
 template <typename T>
@@ -689,7 +695,7 @@ static int run_decode(const void* query, const void* key_cache, const void* valu
                       const int64_t* block_tables, const int64_t* context_lens, const int64_t* table_rows,
                       void* out, void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
                       int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
-                      int64_t table_width, int dtype, cudaStream_t stream) {
+                      int64_t table_width, int dtype, cudaStream_t stream, bool early_prologue = false) {
     DecodePlan plan;
     if (!make_decode_plan(batch, q_heads, kv_heads, head_dim, block_size, table_width, dtype, sm_count(), &plan))
         return fail(MINIKV_EUNSUPPORTED, "decode shape does not fit shared memory (batch too large?)");
@@ -701,7 +707,9 @@ static int run_decode(const void* query, const void* key_cache, const void* valu
     const DecodeParams p = decode_params(query, key_cache, value_cache, block_tables, context_lens, table_rows,
                                          out, ws, batch, q_heads, kv_heads, head_dim, num_blocks, block_size,
                                          table_width, plan);
-    const cudaError_t err = launch_decode(dtype, (int)head_dim, p, plan, stream);
+    DecodeParams q = p;
+    q.early_prologue = early_prologue ? 1 : 0;
+    const cudaError_t err = launch_decode(dtype, (int)head_dim, q, plan, stream);
     if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_decode launch");
     return MINIKV_OK;
 }

@@ -11,6 +11,9 @@
 //                            q|k|v projection (native_qwen3.py:178-190;
 //                            fallback.py:13-20; data.py:67-81).
 //
+// All three are chained launches (programmatic dependent launch): each waits
+// for the previous kernel at entry, so only its launch latency overlaps.
+//
 // Rounding follows the eager reference: every torch op there returns the
 // 16-bit input type, so each intermediate (the sum, the normalised row, the
 // product with the weight, each rotary product and their sum) is rounded to
@@ -48,6 +51,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, 
                                                        const T* __restrict__ weight, T* __restrict__ out,
                                                        T* __restrict__ sum_out, int hidden, float eps) {
     __shared__ float scratch[32];
+    griddep_wait();
+    griddep_launch_dependents();
     const int64_t row = blockIdx.x;
     const int vecs = hidden / 8;
     const uint4* xs = reinterpret_cast<const uint4*>(x + row * hidden);
@@ -91,6 +96,8 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, 
 template <typename T>
 __global__ void __launch_bounds__(256) silu_mul_kernel(const T* __restrict__ gate_up, T* __restrict__ out,
                                                        int64_t rows, int64_t inter) {
+    griddep_wait();
+    griddep_launch_dependents();
     const int64_t vecs_per_row = inter / 8;
     const int64_t total = rows * vecs_per_row;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -148,6 +155,8 @@ template <typename T, int D>
 __global__ void __launch_bounds__(256) qk_rope_append_kernel(const QkRopeParams p) {
     constexpr int kE = D / 32;
     constexpr int kHalf = D / 2;
+    griddep_wait();
+    griddep_launch_dependents();  // the decode of the same layer may start its prologue
     const int lane = threadIdx.x & 31;
     const int64_t heads = p.q_heads + p.kv_heads;
     const int64_t jobs = p.batch * heads;
@@ -217,10 +226,9 @@ static cudaError_t launch_rms_norm_typed(const void* x, const void* residual, co
     T* ot = static_cast<T*>(out);
     T* st = static_cast<T*>(sum_out);
     const dim3 grid((unsigned)rows);
-    if (per <= 1) rms_norm_kernel<T, 1><<<grid, threads, 0, s>>>(xt, rt, wt, ot, st, hidden, eps);
-    else if (per <= 2) rms_norm_kernel<T, 2><<<grid, threads, 0, s>>>(xt, rt, wt, ot, st, hidden, eps);
-    else rms_norm_kernel<T, 4><<<grid, threads, 0, s>>>(xt, rt, wt, ot, st, hidden, eps);
-    return cudaGetLastError();
+    if (per <= 1) return launch_chained(rms_norm_kernel<T, 1>, grid, dim3(threads), 0, s, xt, rt, wt, ot, st, hidden, eps);
+    if (per <= 2) return launch_chained(rms_norm_kernel<T, 2>, grid, dim3(threads), 0, s, xt, rt, wt, ot, st, hidden, eps);
+    return launch_chained(rms_norm_kernel<T, 4>, grid, dim3(threads), 0, s, xt, rt, wt, ot, st, hidden, eps);
 }
 
 static cudaError_t launch_rms_norm(int dtype, const void* x, const void* residual, const void* weight, void* out,
@@ -237,22 +245,20 @@ static cudaError_t launch_silu_mul(int dtype, const void* gate_up, void* out, in
     if (total <= 0) return cudaSuccess;
     int64_t blocks = std::min<int64_t>((total + 255) / 256, (int64_t)sms * 8);
     if (dtype == MINIKV_BF16)
-        silu_mul_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(
-            static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), rows, inter);
-    else
-        silu_mul_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>(static_cast<const __half*>(gate_up),
-                                                                 static_cast<__half*>(out), rows, inter);
-    return cudaGetLastError();
+        return launch_chained(silu_mul_kernel<__nv_bfloat16>, dim3((unsigned)blocks), dim3(256), 0, s,
+                              static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), rows,
+                              inter);
+    return launch_chained(silu_mul_kernel<__half>, dim3((unsigned)blocks), dim3(256), 0, s,
+                          static_cast<const __half*>(gate_up), static_cast<__half*>(out), rows, inter);
 }
 
 template <typename T>
 static cudaError_t launch_qk_rope_typed(const QkRopeParams& p, int head_dim, unsigned blocks, cudaStream_t s) {
     switch (head_dim) {
-        case 64: qk_rope_append_kernel<T, 64><<<blocks, 256, 0, s>>>(p); break;
-        case 128: qk_rope_append_kernel<T, 128><<<blocks, 256, 0, s>>>(p); break;
-        default: qk_rope_append_kernel<T, 256><<<blocks, 256, 0, s>>>(p); break;
+        case 64: return launch_chained(qk_rope_append_kernel<T, 64>, dim3(blocks), dim3(256), 0, s, p);
+        case 128: return launch_chained(qk_rope_append_kernel<T, 128>, dim3(blocks), dim3(256), 0, s, p);
+        default: return launch_chained(qk_rope_append_kernel<T, 256>, dim3(blocks), dim3(256), 0, s, p);
     }
-    return cudaGetLastError();
 }
 
 static cudaError_t launch_qk_rope_append(int dtype, const QkRopeParams& p, int head_dim, int sms, cudaStream_t s) {

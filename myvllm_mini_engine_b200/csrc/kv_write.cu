@@ -1,6 +1,8 @@
 // KV writes: packed scatter by slot, decode append, contiguous range, and
 // copy-on-write of whole pages.  Pure byte moves: one warp per token row,
 // 16-byte vector loads/stores, grid sized to the SM count (grid-stride).
+// Launched as chained kernels: each waits for the previous kernel first and
+// then lets the next one (typically the decode of the same step) launch.
 //
 // Reference behaviour kept (mini_engine/kernels/csrc/data.cu):
 //  * rows whose destination is out of range are skipped, never clamped
@@ -51,6 +53,8 @@ __global__ void __launch_bounds__(256) write_rows_kernel(
     uint4* __restrict__ kc, uint4* __restrict__ vc, const uint4* __restrict__ k,
     const uint4* __restrict__ v, int64_t rows, int64_t row_vecs, int64_t k_stride_vecs,
     int64_t v_stride_vecs, Rows map) {
+    griddep_wait();
+    griddep_launch_dependents();
     const int lane = threadIdx.x & 31;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < rows; t += warps) {
@@ -74,6 +78,8 @@ __global__ void __launch_bounds__(256) write_rows_kernel(
 __global__ void __launch_bounds__(256) copy_blocks_kernel(
     uint4* __restrict__ kpool, uint4* __restrict__ vpool, const int64_t* __restrict__ pairs,
     int64_t num_pairs, int64_t num_layers, int64_t num_blocks, int64_t page_vecs) {
+    griddep_wait();
+    griddep_launch_dependents();
     const int64_t units = num_pairs * num_layers * 2;
     for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
         const int64_t pair = u / (num_layers * 2);
@@ -108,10 +114,10 @@ static cudaError_t launch_write_rows(void* kc, void* vc, const void* k, const vo
     int64_t blocks = (rows + per_block - 1) / per_block;
     const int64_t cap = (int64_t)sm_count_for_current_device() * 8;
     if (blocks > cap) blocks = cap;
-    write_rows_kernel<Rows><<<(unsigned)blocks, 256, 0, stream>>>(
-        static_cast<uint4*>(kc), static_cast<uint4*>(vc), static_cast<const uint4*>(k),
-        static_cast<const uint4*>(v), rows, row_bytes / 16, k_stride_bytes / 16, v_stride_bytes / 16, map);
-    return cudaGetLastError();
+    return launch_chained(write_rows_kernel<Rows>, dim3((unsigned)blocks), dim3(256), 0, stream,
+                          static_cast<uint4*>(kc), static_cast<uint4*>(vc), static_cast<const uint4*>(k),
+                          static_cast<const uint4*>(v), rows, row_bytes / 16, k_stride_bytes / 16,
+                          v_stride_bytes / 16, map);
 }
 
 static cudaError_t launch_copy_blocks(void* kpool, void* vpool, const int64_t* pairs, int64_t num_pairs,
@@ -122,10 +128,9 @@ static cudaError_t launch_copy_blocks(void* kpool, void* vpool, const int64_t* p
     int64_t blocks = units;
     const int64_t cap = (int64_t)sm_count_for_current_device() * 8;
     if (blocks > cap) blocks = cap;
-    copy_blocks_kernel<<<(unsigned)blocks, 256, 0, stream>>>(
-        static_cast<uint4*>(kpool), static_cast<uint4*>(vpool), pairs, num_pairs, num_layers,
-        num_blocks, page_bytes / 16);
-    return cudaGetLastError();
+    return launch_chained(copy_blocks_kernel, dim3((unsigned)blocks), dim3(256), 0, stream,
+                          static_cast<uint4*>(kpool), static_cast<uint4*>(vpool), pairs, num_pairs, num_layers,
+                          num_blocks, page_bytes / 16);
 }
 
 }  // namespace minikv

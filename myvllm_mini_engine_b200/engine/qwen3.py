@@ -199,8 +199,9 @@ class Qwen3DecodeStep:
                 sin.data_ptr(), q.data_ptr(), pool.key[index].data_ptr(), pool.value[index].data_ptr(),
                 block_tables.data_ptr(), positions.data_ptr(), batch, hq, hkv, dim, shape.num_blocks,
                 shape.block_size, block_tables.shape[1], cfg.rms_norm_eps, self.code, stream), "qk_rope_append")
+            # lengths and tables predate the append kernel just launched: chained decode
             attention = paged_attention(q, pool.key[index], pool.value[index], block_tables, lengths,
-                                        shape.block_size, validate=False)
+                                        shape.block_size, validate=False, chained=True)
             o = torch.mm(attention.view(batch, hq * dim), layer.o.t())
             summed, normalized = torch.empty_like(x), torch.empty_like(x)
             self._rms(o, residual, layer.post_norm, normalized, summed, stream)

@@ -32,7 +32,7 @@ def check_backend(backend):
 
 
 def paged_attention(query, key_cache, value_cache, block_tables, context_lens, block_size,
-                    *, backend="cuda", validate=True, workspace=None):
+                    *, backend="cuda", validate=True, workspace=None, chained=False):
     """Decode attention ``out[b, h] = softmax(q . K^T / sqrt(D)) V`` over paged K/V.
 
     ``query [B, Hq, D]``, ``key_cache``/``value_cache`` ``[num_blocks, block_size,
@@ -43,6 +43,11 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
     stream gets a buffer kept by this module (see :func:`_workspace`).  Before
     capturing a CUDA graph, make one call on the capture stream so the buffer
     exists and its zero fill stays out of the graph.
+
+    ``chained=True`` (an extension) declares that ``context_lens`` and
+    ``block_tables`` were written before the previous kernel on the stream
+    started -- e.g. the KV append of the same step is that kernel -- so the
+    launch overlaps its prologue with that kernel (``minikv_paged_decode_chained``).
     """
     check_backend(backend)
     _require(query.is_cuda, "query must be CUDA")
@@ -90,7 +95,8 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
         elif workspace.numel() < need:
             raise RuntimeError("decode workspace too small")
         out = torch.empty_like(query)
-        status = lib.minikv_paged_decode(
+        entry = lib.minikv_paged_decode_chained if chained else lib.minikv_paged_decode
+        status = entry(
             query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
             context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
             batch, heads, kv_heads, dim, num_blocks, block_size, width, code, stream.cuda_stream)

@@ -163,3 +163,34 @@ def test_graph_replay_with_new_lengths_and_queries(cuda_device, dtype, block_siz
     expected = paged_decode.paged_attention_fp32(*[a.cpu() for a in args], block_size)
     assert_close(captured, expected, dtype)
     assert torch.equal(original_k, args[1]) and torch.equal(original_v, args[2])
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_chained_decode_after_append_in_a_graph(cuda_device, dtype):
+    """Append + chained decode (prologue overlapped with the append) equals the plain launches, bit for bit."""
+    c = cases.append_decode_case(dtype, batch=6, contexts=[0, 15, 16, 300, 1023, 77], block_size=16, seed=91)
+    names = ("key_cache", "value_cache", "block_tables", "token_offsets", "key", "value")
+    g = {k: c[k].cuda() for k in names + ("query", "context_lens")}
+    plain_k, plain_v = g["key_cache"].clone(), g["value_cache"].clone()
+    write_kv_cache_batch(plain_k, plain_v, g["block_tables"], g["token_offsets"], g["key"], g["value"], 16,
+                         validate=False)
+    expected = paged_attention(g["query"], plain_k, plain_v, g["block_tables"], g["context_lens"], 16,
+                               validate=False)
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        paged_attention(g["query"], g["key_cache"], g["value_cache"], g["block_tables"], g["context_lens"], 16,
+                        validate=False, chained=True)  # workspace of this stream, outside the graph
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        write_kv_cache_batch(g["key_cache"], g["value_cache"], g["block_tables"], g["token_offsets"], g["key"],
+                             g["value"], 16, validate=False)
+        out = paged_attention(g["query"], g["key_cache"], g["value_cache"], g["block_tables"], g["context_lens"],
+                              16, validate=False, chained=True)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, expected)
+    assert torch.equal(g["key_cache"], plain_k) and torch.equal(g["value_cache"], plain_v)
+    assert _lib.device_status() == 0

@@ -200,7 +200,7 @@ def test_decode_step_is_bit_exact_with_the_reference_attention(cuda_device, monk
     cfg, weights, pool, tables, ids, positions = model_case(contexts, seed=33)
     ref_key, ref_value = pool.key.clone(), pool.value.clone()
     monkeypatch.setattr(engine_qwen3, "paged_attention",
-                        lambda q, kc, vc, t, lens, bs, validate=False: paged_decode.paged_attention(q, kc, vc, t, lens, bs))
+                        lambda q, kc, vc, t, lens, bs, **_: paged_decode.paged_attention(q, kc, vc, t, lens, bs))
     logits = Qwen3DecodeStep(cfg, weights, pool).forward_decode_batch(ids, tables, positions)
     expected = ref.decode_step(cfg, weights, ids, ref_key, ref_value, tables, positions)
     assert torch.equal(logits, expected)
