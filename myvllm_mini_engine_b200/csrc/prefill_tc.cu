@@ -7,20 +7,24 @@
 // tile's last query position (causal):
 //   S_j = Q K_j^T   tcgen05.mma kind::f16, M=128, N=128, K=D -> TMEM (fp32),
 //                   double-buffered (two 128-column S buffers)
-//   P_j = exp2(S_j * log2(e)/sqrt(D) - m)                      (softmax warps)
-//   O  += P_j V_j   tcgen05.mma, M=128, N=D, K=128 -> TMEM (fp32), accumulated
-//                   across key tiles
+//   P_j = exp2(S_j * log2(e)/sqrt(D) - m)   (softmax warps), written as 16-bit
+//                   values over the first 64 columns of S_j's own TMEM buffer
+//   O  += P_j V_j   tcgen05.mma with A = P_j read from TMEM, M=128, N=D, K=128
+//                   -> TMEM (fp32), accumulated across key tiles
 // The running max m is raised lazily: while no score exceeds it by more than
 // 8 (log2 units) P is formed against the old m, so O is rescaled in TMEM
 // (tcgen05.ld / st by the row's thread) only when m moves by more than that.
-// Warp roles: warp 0 issues the TMA loads (Q once; the K and V boxes of each
-// key tile straight from the physical pages of the block table, SWIZZLE_128B,
-// two-stage ring) and publishes each tile's key-validity bits; warp 1 owns
-// the TMEM allocation and one of its lanes issues every MMA, S_{j+1} before
-// P_j V_j so the scores of the next tile are computed while the softmax warps
-// work; warps 2-5 own one TMEM lane (= one row) each for the softmax, the P
-// tile (written to shared memory in the swizzled K-major layout the MMA
-// reads) and the epilogue.  No TMA multicast.
+// Warp roles: warps 0 and 10 issue the TMA loads (Q once; the K and V boxes of
+// each key tile straight from the physical pages of the block table,
+// SWIZZLE_128B; warp 0 runs the K ring and warp 10 the V ring, two slots each,
+// each slot freed by the MMA that reads it) and warp 0 publishes each tile's
+// key-validity bits; warp 1 owns the TMEM allocation and one of its lanes issues every MMA
+// as soon as its operands are ready, so S runs up to two tiles ahead of P V
+// and the scores of the next tile are computed while the softmax warps work;
+// warps 2-9 are two softmax warpgroups: a row (= TMEM lane) has one thread in
+// each, for half of its keys and half of O, so the P tile, the rescale and the
+// epilogue are split two ways.  Because P stays in TMEM, the softmax of tile
+// j+1 runs while P_j V_j is on the tensor cores.  No TMA multicast.
 //
 // Semantics follow the reference kernel (mini_engine/kernels/csrc/prefill.cu:
 // 104-185): row t of request r attends keys [0, start_r + t]; keys on a page
@@ -33,7 +37,8 @@
 
 namespace minikv {
 
-constexpr int kPfThreads = 192;  // warp 0 TMA, warp 1 MMA/TMEM, warps 2-5 softmax
+constexpr int kPfThreads = 352;  // warp 0 K loads, 1 MMA/TMEM, 2-9 softmax (two warpgroups), 10 V loads
+constexpr int kPfVWarp = 10;
 constexpr int kPfRows = 128;     // M rows per CTA (tokens x GQA heads)
 constexpr int kPfKeys = 128;     // keys per tile
 
@@ -67,6 +72,15 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint6
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
         ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
+}
+
+// Same, with the A operand (M x 16, 16-bit elements two per column) read from TMEM.
+__device__ __forceinline__ void umma_f16_tmem_a(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate) : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -158,8 +172,9 @@ __host__ __device__ constexpr uint32_t umma_idesc(int M, int N, bool bf16, bool 
            ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
+// Barrier of the 256 softmax threads (both warpgroups).
 __device__ __forceinline__ void softmax_sync() {
-    asm volatile("bar.sync 2, 128;" ::: "memory");
+    asm volatile("bar.sync 2, 256;" ::: "memory");
 }
 
 template <typename T, int D>
@@ -167,14 +182,13 @@ struct PfLayout {
     static constexpr int KB = D / 64;                     // 128-byte K-blocks per row
     static constexpr int Q_BYTES = kPfRows * D * 2;
     static constexpr int KV_BYTES = kPfKeys * D * 2;
-    static constexpr int P_BYTES = kPfRows * kPfKeys * 2;
     static constexpr int BLOCK_BYTES = 128 * 128;         // one K-block of a 128-row operand
     static constexpr int OFF_K = Q_BYTES;
     static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
-    static constexpr int OFF_P = OFF_V + 2 * KV_BYTES;
-    static constexpr int OFF_BAR = OFF_P + P_BYTES;
-    static constexpr int SMEM = OFF_BAR + 256 + 1024;     // + barriers/flags + alignment slack
-    static constexpr uint32_t TMEM_COLS = 512;  // S0, S1 (128 columns each) and O (D columns)
+    static constexpr int OFF_BAR = OFF_V + 2 * KV_BYTES;
+    static constexpr int OFF_RED = OFF_BAR + 256;          // [2][2][128] partial row maxima, [2][128] sums
+    static constexpr int SMEM = OFF_RED + 3 * 1024 + 1024;  // + alignment slack
+    static constexpr uint32_t TMEM_COLS = 512;  // S/P 0, S/P 1 (128 columns each) and O (D columns)
 };
 
 template <typename T, int D>
@@ -188,18 +202,21 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     unsigned char* sQ = smem;
     unsigned char* sK = smem + L::OFF_K;
     unsigned char* sV = smem + L::OFF_V;
-    unsigned char* sP = smem + L::OFF_P;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
     uint64_t* q_full = bar + 0;
-    uint64_t* kv_full = bar + 1;   // [2] K and V of a key tile landed (+ its key_ok words)
-    uint64_t* kv_empty = bar + 3;  // [2] both MMAs of the tile are done with its K/V slot
-    uint64_t* s_full = bar + 5;    // [2] S of a tile is in its TMEM buffer
-    uint64_t* s_free = bar + 7;    // [2] the softmax warps have read that S buffer
-    uint64_t* p_full = bar + 9;    // P of the tile is in shared memory and O is rescaled
-    uint64_t* o_done = bar + 10;   // the P V product of the tile has been accumulated into O
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 11);
-    int* info = reinterpret_cast<int*>(bar + 12);               // request, tile
-    uint32_t* key_ok = reinterpret_cast<uint32_t*>(bar + 14);   // [2][4] validity bits of a key tile
+    uint64_t* k_full = bar + 1;    // [2] K of a key tile landed (+ its key_ok words)
+    uint64_t* k_empty = bar + 3;   // [2] the S MMA is done with that K slot
+    uint64_t* v_full = bar + 5;    // [2] V of a key tile landed
+    uint64_t* v_empty = bar + 7;   // [2] the P V MMA is done with that V slot
+    uint64_t* s_full = bar + 9;    // [2] S of a tile is in its TMEM buffer
+    uint64_t* p_full = bar + 13;   // P of the tile is in its TMEM buffer, O rescaled, masked V rows zeroed
+    uint64_t* o_done = bar + 14;   // the P V product of the tile has been accumulated into O
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 15);
+    int* info = reinterpret_cast<int*>(bar + 16);               // request, tile
+    // [4][4] validity bits of key tile j in slot j % 4: the producer rewrites a
+    // slot for tile j + 4 only after S(j + 2), which needs the softmax of tile j
+    // to have read its S buffer (and these words) first
+    uint32_t* key_ok = reinterpret_cast<uint32_t*>(bar + 18);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int B = p.requests, G = p.group, TM = p.tm;
@@ -252,12 +269,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     if (tid == 0) {
         mbar_init(q_full, 1);
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
             mbar_init(&s_full[s], 1);
-            mbar_init(&s_free[s], 4);
         }
-        mbar_init(p_full, 4);
+        mbar_init(p_full, 8);
         mbar_init(o_done, 1);
         mbar_init_fence();
     }
@@ -271,162 +289,202 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;  // columns: S0 [0,128) | S1 [128,256) | O [256, 256+D)
 
-    if (warp == 0) {
-        // ------------------------------------------------------------ TMA producer
+    if (warp == 0 || warp == kPfVWarp) {
+        // ------------------------------------------------------------ TMA producers
+        // Warp 0 loads K and warp 10 loads V, each on its own ring of two
+        // slots, so a K slot is refilled as soon as the S MMA has read it,
+        // whatever the P V MMAs are doing (two warps, because a warp that ran
+        // both rings would reconverge after every wait).  Lane l owns box l
+        // (R keys on one page) of a tile; its page id is read one tile ahead.
         if (n_tiles > 0) {
-            if (lane == 0) {
+            if (warp == 0 && lane == 0) {
                 mbar_arrive_expect_tx(q_full, (uint32_t)L::Q_BYTES);
 #pragma unroll
                 for (int kb = 0; kb < L::KB; ++kb)
                     tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, h * G, (int)(q0 + t_lo), q_full);
             }
-            const int R = p.box_rows, groups = kPfKeys / R;
+            const bool is_v = warp == kPfVWarp;
+            const int box = lane;
+            const unsigned full_mask = 0xffffffffu;
+            const int R = p.box_rows, groups = kPfKeys / R;  // groups <= 16
+            auto box_page = [&](int j) -> int64_t {  // physical page of this lane's box of tile j, or -1
+                const int64_t k0 = (int64_t)j * kPfKeys + box * R;
+                if (box >= groups || j >= n_tiles || k0 >= limit) return -1;
+                const int64_t page = table[k0 / p.block_size];
+                return (page >= 0 && page < p.num_blocks) ? page : -1;
+            };
+            uint64_t* full = is_v ? v_full : k_full;
+            uint64_t* empty = is_v ? v_empty : k_empty;
+            const CUtensorMap* map = is_v ? &tm_v : &tm_k;
+            unsigned char* ring = is_v ? sV : sK;
+            int64_t page = box_page(0);
             for (int j = 0; j < n_tiles; ++j) {
                 const int slot = j & 1;
-                if (j >= 2) mbar_wait(&kv_empty[slot], ((j >> 1) - 1) & 1);
                 const int64_t key0 = (int64_t)j * kPfKeys;
-                // validity of the tile's keys (in the context and on a valid page), for the softmax warps
+                const int64_t next_page = box_page(j + 1);  // in flight while this tile is issued
+                const bool valid = page >= 0;
+                uint32_t words[4] = {0u, 0u, 0u, 0u};
+                if (!is_v) {
+                    // validity bits of the tile's keys: a key is valid when its box is and it is < limit
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int64_t key = key0 + q * 32 + lane;
-                    bool ok = key < limit;
-                    if (ok) {
-                        const int64_t page = table[key / p.block_size];
-                        ok = page >= 0 && page < p.num_blocks;
-                    }
-                    const unsigned bits = __ballot_sync(0xffffffffu, ok);
-                    if (lane == 0) key_ok[4 * slot + q] = bits;
-                }
-                // lane gi handles boxes gi, gi + 32, ... (R rows each)
-                uint32_t bytes = 0;
-                for (int gi = lane; gi < groups; gi += 32) {
-                    const int64_t k0 = key0 + gi * R;
-                    if (k0 >= limit) continue;
-                    const int64_t page = table[k0 / p.block_size];
-                    if (page < 0 || page >= p.num_blocks) continue;
-                    bytes += (uint32_t)(2 * L::KB * R * 128);
-                }
-#pragma unroll
-                for (int off = 16; off > 0; off >>= 1) bytes += __shfl_xor_sync(0xffffffffu, bytes, off);
-                __syncwarp();
-                if (lane == 0) mbar_arrive_expect_tx(&kv_full[slot], bytes);
-                __syncwarp();
-                unsigned char* kdst = sK + slot * L::KV_BYTES;
-                unsigned char* vdst = sV + slot * L::KV_BYTES;
-                for (int gi = lane; gi < groups; gi += 32) {
-                    const int64_t k0 = key0 + gi * R;
-                    if (k0 >= limit) continue;
-                    const int64_t page = table[k0 / p.block_size];
-                    if (page < 0 || page >= p.num_blocks) continue;
-                    const int z = (int)(page * p.block_size + k0 % p.block_size);
-#pragma unroll
-                    for (int kb = 0; kb < L::KB; ++kb) {
-                        tma_load_3d(kdst + kb * L::BLOCK_BYTES + gi * R * 128, &tm_k, kb * 64, h, z, &kv_full[slot]);
-                        tma_load_3d(vdst + kb * L::BLOCK_BYTES + gi * R * 128, &tm_v, kb * 64, h, z, &kv_full[slot]);
+                    for (int q = 0; q < 4; ++q) {
+                        uint32_t bits = 0;
+                        if (valid) {
+                            const int64_t lo = max((int64_t)q * 32, (int64_t)box * R);
+                            const int64_t hi = min(min((int64_t)q * 32 + 32, (int64_t)box * R + R), limit - key0);
+                            if (hi > lo) {
+                                const int n = (int)(hi - lo);
+                                bits = (n == 32 ? 0xffffffffu : ((1u << n) - 1u)) << (int)(lo - q * 32);
+                            }
+                        }
+                        words[q] = __reduce_or_sync(full_mask, bits);
                     }
                 }
+                const uint32_t bytes = (uint32_t)__popc(__ballot_sync(full_mask, valid)) * L::KB * R * 128;
+                if (j >= 2) mbar_wait(&empty[slot], ((j >> 1) - 1) & 1);
+                if (box == 0) {
+                    if (!is_v) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) key_ok[4 * (j & 3) + q] = words[q];
+                    }
+                    mbar_arrive_expect_tx(&full[slot], bytes);
+                }
+                __syncwarp(full_mask);
+                if (valid) {
+                    const int z = (int)(page * p.block_size + (key0 + box * R) % p.block_size);
+                    unsigned char* dst = ring + slot * L::KV_BYTES + box * R * 128;
+#pragma unroll
+                    for (int kb = 0; kb < L::KB; ++kb)
+                        tma_load_3d(dst + kb * L::BLOCK_BYTES, map, kb * 64, h, z, &full[slot]);
+                }
+                page = next_page;
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        // S(j+1) is issued before P V(j), so the tensor cores compute the next
-        // scores while the softmax warps work on the current ones.
+        // S(j) and P V(j) are issued in whichever order their operands become
+        // ready (non-blocking probes), so a late K tile never holds back a
+        // P V product whose P is done, and S runs up to two tiles ahead.
         if (lane == 0 && n_tiles > 0) {
             constexpr uint32_t idesc_s = umma_idesc(128, kPfKeys, kBf16, false);
             constexpr uint32_t idesc_o = umma_idesc(128, D, kBf16, true);
             const uint32_t t_o = tmem + 2 * kPfKeys;
-            const uint32_t q_addr = smem_addr(sQ), p_addr = smem_addr(sP);
+            const uint32_t q_addr = smem_addr(sQ);
             mbar_wait(q_full, 0);
-            for (int j = -1; j < n_tiles; ++j) {
-                const int next = j + 1;
-                if (next < n_tiles) {
-                    const int slot = next & 1;
-                    mbar_wait(&kv_full[slot], (next >> 1) & 1);
-                    if (next >= 2) mbar_wait(&s_free[slot], ((next >> 1) - 1) & 1);
-                    tc_fence_after();
-                    const uint32_t k_addr = smem_addr(sK + slot * L::KV_BYTES);
+            int ns = 0, npv = 0;  // next S and next P V to issue
+            uint64_t idle_since = 0;
+            while (npv < n_tiles) {
+                bool progressed = false;
+                if (ns < n_tiles) {
+                    const int slot = ns & 1;
+                    // the buffer of S(ns) holds P(ns - 2) until P V(ns - 2) has read it: MMAs of
+                    // one thread run in issue order, so S(ns) goes after that product is issued
+                    if ((ns < 2 || npv >= ns - 1) && mbar_test_wait(&k_full[slot], (ns >> 1) & 1)) {
+                        tc_fence_after();
+                        const uint32_t k_addr = smem_addr(sK + slot * L::KV_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < D / 16; ++kk) {
-                        const uint32_t off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
-                        umma_f16(tmem + slot * kPfKeys, smem_desc(q_addr + off, 16, 1024),
-                                 smem_desc(k_addr + off, 16, 1024), idesc_s, kk > 0);
+                        for (int kk = 0; kk < D / 16; ++kk) {
+                            const uint32_t off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
+                            umma_f16(tmem + slot * kPfKeys, smem_desc(q_addr + off, 16, 1024),
+                                     smem_desc(k_addr + off, 16, 1024), idesc_s, kk > 0);
+                        }
+                        umma_commit(&s_full[slot]);
+                        umma_commit(&k_empty[slot]);
+                        ++ns;
+                        progressed = true;
                     }
-                    umma_commit(&s_full[slot]);
                 }
-                if (j < 0) continue;
-                mbar_wait(p_full, j & 1);
-                tc_fence_after();
-                const uint32_t v_addr = smem_addr(sV + (j & 1) * L::KV_BYTES);
+                if (npv < ns && mbar_test_wait(&v_full[npv & 1], (npv >> 1) & 1) && mbar_test_wait(p_full, npv & 1)) {
+                    tc_fence_after();
+                    const uint32_t v_addr = smem_addr(sV + (npv & 1) * L::KV_BYTES);
 #pragma unroll
-                for (int kk = 0; kk < kPfKeys / 16; ++kk) {
-                    const uint32_t a_off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
-                    umma_f16(t_o, smem_desc(p_addr + a_off, 16, 1024),
-                             smem_desc(v_addr + kk * 16 * 128, L::BLOCK_BYTES, 1024), idesc_o, (j > 0 || kk > 0));
+                    for (int kk = 0; kk < kPfKeys / 16; ++kk)  // P: 16 keys = 8 TMEM columns per step
+                        umma_f16_tmem_a(t_o, tmem + (npv & 1) * kPfKeys + kk * 8,
+                                        smem_desc(v_addr + kk * 16 * 128, L::BLOCK_BYTES, 1024), idesc_o,
+                                        (npv > 0 || kk > 0));
+                    umma_commit(o_done);
+                    umma_commit(&v_empty[npv & 1]);
+                    ++npv;
+                    progressed = true;
                 }
-                umma_commit(o_done);
-                umma_commit(&kv_empty[j & 1]);
+                if (progressed) {
+                    idle_since = 0;
+                } else {
+                    // bounded: the same limit as every other wait, then give up (status bit set)
+                    __nanosleep(32);
+                    const uint64_t now = global_ns();
+                    if (idle_since == 0) {
+                        idle_since = now;
+                    } else if (now - idle_since > kWaitLimitNs ||
+                               (now - idle_since > kWaitCheckNs &&
+                                (*reinterpret_cast<volatile unsigned int*>(&g_status) & kStatusWaitTimeout))) {
+                        raise_status(kStatusWaitTimeout);
+                        break;
+                    }
+                }
             }
         }
     } else {
         // ------------------------------------------------------------ softmax warps
+        // Two warpgroups; the thread of warpgroup `half` for a row owns key
+        // columns [64 half, 64 half + 64) of S and P and O columns
+        // [half D/2, (half + 1) D/2).  The two threads of a row exchange their
+        // partial maxima once per tile (shared memory + a 256-thread barrier),
+        // keep partial sums, and add them at the end.
+        constexpr int kHalfKeys = kPfKeys / 2, kHalfD = D / 2;
+        float* red = reinterpret_cast<float*>(smem + L::OFF_RED);  // [2][2][128] maxima, then [2][128] sums
+        const int sw = warp - 2;                 // 0..7
+        const int half = sw >> 2;                // warpgroup
         const int quarter = warp & 3;            // TMEM lane quarter of this warp
         const int row = quarter * 32 + lane;     // tile row = TMEM lane
-        const int st = (warp - 2) * 32 + lane;   // 0..127: the key row this thread zeroes when masked
+        const int st = sw * 32 + lane;           // 0..255: masked-key V zeroing (row st & 127, K-blocks from st >> 7)
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
-        const uint32_t t_o = tmem + lane_base + 2 * kPfKeys;
+        const uint32_t t_o = tmem + lane_base + 2 * kPfKeys + half * kHalfD;
         const int t = t_lo + row / G, g = row % G;
         const int64_t pos = start + t;
         const bool row_valid = t < qlen && pos < limit;
         const float scale = p.scale_log2;
-        // Running max (log2 domain) and sum.  The max is raised lazily: P is
-        // computed against m_run as long as no score exceeds it by more than
+        // Running max (log2 domain) and partial sum.  The max is raised lazily: P
+        // is computed against m_run as long as no score exceeds it by more than
         // 2^8, so O (accumulated in TMEM) is rescaled only when m_run moves.
         float m_run = -INFINITY, l_run = 0.f;
         for (int j = 0; j < n_tiles; ++j) {
             const int slot = j & 1;
-            mbar_wait(&kv_full[slot], (j >> 1) & 1);
+            mbar_wait(&k_full[slot], (j >> 1) & 1);
             uint32_t w[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) w[q] = key_ok[4 * slot + q];
-            if (!((w[st >> 5] >> (st & 31)) & 1u)) {
-                // V rows of masked keys must be finite zeros before P V runs
-                unsigned char* vrow = sV + slot * L::KV_BYTES + st * 128;
-#pragma unroll
-                for (int kb = 0; kb < L::KB; ++kb) {
-                    uint4* v4 = reinterpret_cast<uint4*>(vrow + kb * L::BLOCK_BYTES);
-#pragma unroll
-                    for (int c = 0; c < 8; ++c) v4[c] = make_uint4(0, 0, 0, 0);
-                }
-                fence_async_smem();
-            }
+            for (int q = 0; q < 4; ++q) w[q] = key_ok[4 * (j & 3) + q];
             // keys [0, rel] of this tile are causally visible to the row
             const int64_t rel = pos - (int64_t)j * kPfKeys;
-            uint32_t bits[4];
+            uint32_t bits[2];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
+            for (int qq = 0; qq < 2; ++qq) {
+                const int q = 2 * half + qq;
                 const int64_t lim = rel - q * 32;
                 const uint32_t causal = lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : ((2u << (int)lim) - 1u));
-                bits[q] = row_valid ? (w[q] & causal) : 0u;
+                bits[qq] = row_valid ? (w[q] & causal) : 0u;
             }
-            const bool full = (bits[0] & bits[1] & bits[2] & bits[3]) == 0xffffffffu;
+            const bool full = (bits[0] & bits[1]) == 0xffffffffu;
 
             mbar_wait(&s_full[slot], (j >> 1) & 1);
             tc_fence_after();
-            float s[kPfKeys];
-            tmem_load_128(tmem + lane_base + slot * kPfKeys, s);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[slot]);
+            float s[kHalfKeys];
+            tmem_load_32(tmem + lane_base + slot * kPfKeys + half * kHalfKeys, s);
+            tmem_load_32(tmem + lane_base + slot * kPfKeys + half * kHalfKeys + 32, s + 32);
 
-            float mx = -INFINITY;
+            float mxs[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
             if (full) {
 #pragma unroll
-                for (int e = 0; e < kPfKeys; ++e) mx = fmaxf(mx, s[e]);
+                for (int e = 0; e < kHalfKeys; ++e) mxs[e & 3] = fmaxf(mxs[e & 3], s[e]);
             } else {
 #pragma unroll
-                for (int e = 0; e < kPfKeys; ++e)
-                    if ((bits[e >> 5] >> (e & 31)) & 1u) mx = fmaxf(mx, s[e]);
+                for (int e = 0; e < kHalfKeys; ++e)
+                    if ((bits[e >> 5] >> (e & 31)) & 1u) mxs[e & 3] = fmaxf(mxs[e & 3], s[e]);
             }
+            float* mred = red + (j & 1) * 256;
+            mred[half * 128 + row] = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
+            softmax_sync();  // also: both halves of the S buffer have been read, P may overwrite it
+            const float mx = fmaxf(mred[row], mred[128 + row]);
             const float m_tile = mx * scale;  // -inf when the row sees no key of this tile
             float m_use = m_run, alpha = 1.f;
             bool rescale = false;
@@ -435,43 +493,36 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                 rescale = m_run != -INFINITY;  // O holds only zeros while m_run is -inf
                 m_use = m_tile;
             }
-            // P of this tile replaces the previous one: its P V product must be done
+            // P (16-bit, two keys per column) over the first 64 columns of this
+            // tile's S buffer: keys 64 half .. 64 half + 63 at columns 32 half ..
+            float sums[4] = {0.f, 0.f, 0.f, 0.f};
+            const float neg = -m_use;
+            float packed[32];
+#pragma unroll
+            for (int e = 0; e < kHalfKeys; e += 2) {
+                float pe[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int k = e + u;
+                    const float x = fast_exp2(fmaf(s[k], scale, neg));
+                    pe[u] = (full || ((bits[k >> 5] >> (k & 31)) & 1u)) ? x : 0.f;
+                    sums[k & 3] += pe[u];
+                }
+                packed[e / 2] = __uint_as_float(Elem<T>::pack(pe[0], pe[1]));
+            }
+            tmem_store_32(tmem + lane_base + slot * kPfKeys + half * 32, packed);
+            tmem_store_wait();
+            // O may be rescaled only once the previous P V product has landed in it
             if (j > 0) {
                 mbar_wait(o_done, (j - 1) & 1);
                 tc_fence_after();
-            }
-            float sum = 0.f;
-            unsigned char* prow = sP + row * 128;
-            const float neg = -m_use;
-#pragma unroll
-            for (int c = 0; c < kPfKeys / 32; ++c) {
-                uint32_t packed[16];
-#pragma unroll
-                for (int e = 0; e < 32; e += 2) {
-                    float pe[2];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int k = c * 32 + e + u;
-                        const float x = fast_exp2(fmaf(s[k], scale, neg));
-                        pe[u] = (full || ((bits[c] >> (e + u)) & 1u)) ? x : 0.f;
-                        sum += pe[u];
-                    }
-                    packed[e / 2] = Elem<T>::pack(pe[0], pe[1]);
-                }
-                // keys c*32 .. c*32+31: K-block c/2, 16-byte chunks (c%2)*4 .. +3
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int chunk = (c & 1) * 4 + q;
-                    uint4* dst = reinterpret_cast<uint4*>(prow + (c >> 1) * L::BLOCK_BYTES + ((chunk ^ (row & 7)) * 16));
-                    *dst = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
-                }
             }
             // tcgen05.ld / st are warp-wide (.sync.aligned): the whole warp takes
             // this branch when any of its rows rescales; the others scale by 1.
             if (__any_sync(0xffffffffu, rescale)) {
                 const float factor = rescale ? alpha : 1.f;
 #pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
+                for (int c = 0; c < kHalfD / 32; ++c) {
                     float v[32];
                     tmem_load_32(t_o + c * 32, v);
 #pragma unroll
@@ -480,22 +531,39 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                 }
                 tmem_store_wait();
             }
-            l_run = l_run * alpha + sum;
+            l_run = l_run * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
             m_run = m_use;
+            const int vrow_key = st & 127;
+            if (!((w[vrow_key >> 5] >> (vrow_key & 31)) & 1u)) {
+                // V rows of masked keys must be finite zeros before P V runs (a
+                // loaded box can hold rows past the context; unloaded rows hold stale data)
+                mbar_wait(&v_full[slot], (j >> 1) & 1);
+                unsigned char* vrow = sV + slot * L::KV_BYTES + vrow_key * 128;
+                for (int kb = st >> 7; kb < L::KB; kb += 2) {
+                    uint4* v4 = reinterpret_cast<uint4*>(vrow + kb * L::BLOCK_BYTES);
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) v4[c] = make_uint4(0, 0, 0, 0);
+                }
+            }
             fence_async_smem();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(p_full);
         }
+        // row sum = the two threads' partial sums
+        float* lred = red + 512;
+        lred[half * 128 + row] = l_run;
+        softmax_sync();
+        const float l_row = lred[row] + lred[128 + row];
         if (n_tiles > 0) {
             mbar_wait(o_done, (n_tiles - 1) & 1);
             tc_fence_after();
         }
         // every lane of the warp loads (warp-wide tcgen05.ld); rows past the chunk store nothing
-        const float inv = (row_valid && l_run > 0.f) ? 1.f / l_run : 0.f;
-        T* orow = static_cast<T*>(p.out) + ((q0 + t) * p.q_heads + h * G + g) * D;
+        const float inv = (row_valid && l_row > 0.f) ? 1.f / l_row : 0.f;
+        T* orow = static_cast<T*>(p.out) + ((q0 + t) * p.q_heads + h * G + g) * D + half * kHalfD;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < kHalfD / 32; ++c) {
             float v[32];
             if (n_tiles > 0) {
                 tmem_load_32(t_o + c * 32, v);
