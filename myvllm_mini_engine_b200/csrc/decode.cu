@@ -135,59 +135,77 @@ __device__ __forceinline__ int request_of_tile(const int* prefix, int B, int t) 
     return lo;
 }
 
-// One warp merges the partial records of request b, query head qh: records
-// b + c for the CTAs c in [c0, c1] that own tiles.  Loads of up to eight
-// records are issued together before they are combined.
+// One warp merges the partial records of request b for query heads qh0 and
+// (when two is set) qh0 + 1: records b + c for the CTAs c in [c0, c1] that own
+// tiles.  Online over chunks of four records: every load of a chunk (the
+// log-sum-exps and the partial rows of both heads) is issued before any of it
+// is combined, so the merge of a request split over k CTAs costs ceil(k / 4)
+// rounds of L2 loads for two heads.  Records of empty segments have lse = -inf
+// and weigh nothing.
 template <typename T, int D>
-__device__ void merge_head(const DecodeParams& p, int b, int qh, int c0, int c1, int G, int total, int lane) {
-    constexpr int kBatch = 8;
+__device__ void merge_heads(const DecodeParams& p, int b, int qh0, bool two, int c0, int c1, int G, int total,
+                            int lane) {
+    constexpr int kBatch = 4;
     constexpr int kDims = (D + 31) / 32;
+    const int nh = two ? 2 : 1;
     const int n = c1 - c0 + 1;
     const int64_t first = (int64_t)b + c0;
-    float mx = -INFINITY;
-    for (int k = lane; k < n; k += 32)
-        if (cta_owns_tiles(c0 + k, G, total)) mx = fmaxf(mx, __ldcg(p.lse + (first + k) * p.q_heads + qh));
+    float m_run[2] = {-INFINITY, -INFINITY}, wsum[2] = {0.f, 0.f};
+    float acc[2][kDims];
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-    float acc[kDims];
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-    for (int i = 0; i < kDims; ++i) acc[i] = 0.f;
-    float wsum = 0.f;
-    for (int base = 0; base < n; base += 32) {
-        float w = 0.f;
-        if (base + lane < n && mx != -INFINITY && cta_owns_tiles(c0 + base + lane, G, total)) {
-            const float lse = __ldcg(p.lse + (first + base + lane) * p.q_heads + qh);
-            w = (lse == -INFINITY) ? 0.f : exp2f(lse - mx);
-        }
-        const int count = min(32, n - base);
-        for (int k0 = 0; k0 < count; k0 += kBatch) {
-            float vals[kBatch][kDims];
-            float wk[kBatch];
+        for (int i = 0; i < kDims; ++i) acc[h][i] = 0.f;
+    for (int k0 = 0; k0 < n; k0 += kBatch) {
+        float lse[2][kBatch];
+        float vals[2][kBatch][kDims];
 #pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                wk[u] = __shfl_sync(0xffffffffu, w, (k0 + u) & 31);
-                const bool use = k0 + u < count && wk[u] != 0.f;
-                const float* part = p.partial + ((first + base + k0 + u) * p.q_heads + qh) * D;
+        for (int u = 0; u < kBatch; ++u) {
+            const int k = k0 + u;
+            const bool use = k < n && cta_owns_tiles(c0 + k, G, total);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const bool on = use && h < nh;
+                const int64_t rec = (first + k) * p.q_heads + qh0 + h;
+                lse[h][u] = on ? __ldcg(p.lse + rec) : -INFINITY;
+                const float* part = p.partial + rec * D;
 #pragma unroll
                 for (int i = 0; i < kDims; ++i) {
                     const int d = lane + 32 * i;
-                    vals[u][i] = (use && d < D) ? __ldcg(part + d) : 0.f;
+                    vals[h][u][i] = (on && d < D) ? __ldcg(part + d) : 0.f;
                 }
-                if (k0 + u >= count) wk[u] = 0.f;
-            }
-#pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                wsum += wk[u];
-#pragma unroll
-                for (int i = 0; i < kDims; ++i) acc[i] = fmaf(wk[u], vals[u][i], acc[i]);
             }
         }
-    }
-    T* out = static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh) * D;
 #pragma unroll
-    for (int i = 0; i < kDims; ++i) {
-        const int d = lane + 32 * i;
-        if (d < D) out[d] = Elem<T>::from_float(wsum > 0.f ? acc[i] / wsum : 0.f);
+        for (int h = 0; h < 2; ++h) {
+            float cm = -INFINITY;
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) cm = fmaxf(cm, lse[h][u]);
+            const float m_new = fmaxf(m_run[h], cm);
+            if (m_new == -INFINITY) continue;
+            const float keep = (m_run[h] == -INFINITY) ? 0.f : exp2f(m_run[h] - m_new);
+            wsum[h] *= keep;
+#pragma unroll
+            for (int i = 0; i < kDims; ++i) acc[h][i] *= keep;
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+                const float w = (lse[h][u] == -INFINITY) ? 0.f : exp2f(lse[h][u] - m_new);
+                wsum[h] += w;
+#pragma unroll
+                for (int i = 0; i < kDims; ++i) acc[h][i] = fmaf(w, vals[h][u][i], acc[h][i]);
+            }
+            m_run[h] = m_new;
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        if (h >= nh) break;
+        T* out = static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh0 + h) * D;
+#pragma unroll
+        for (int i = 0; i < kDims; ++i) {
+            const int d = lane + 32 * i;
+            if (d < D) out[d] = Elem<T>::from_float(wsum[h] > 0.f ? acc[h][i] / wsum[h] : 0.f);
+        }
     }
 }
 
@@ -531,20 +549,27 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
         if (active) cons.finish(p, b, qh0, item_heads, final_row, (int64_t)b + c);
         if (!final_row) {
             // Ticket: the CTA that completes request b last merges its records.
+            // The consumer barrier orders every thread's partial stores before
+            // thread 0's ticket, an acquire-release atomic at GPU scope: it
+            // publishes this CTA's records (release, cumulative over the
+            // barrier) and, for the last ticket, makes the other CTAs' records
+            // visible to this CTA once the second barrier has passed (acquire).
             int owners = 0;
             for (int cc = c0; cc <= c1; ++cc) owners += cta_owns_tiles(cc, G, total) ? 1 : 0;
-            __threadfence();
             consumers_sync();
             if (tid == 0) {
-                const unsigned int ticket =
-                    atomicInc(p.tickets + (int64_t)b * gridDim.y + blockIdx.y, (unsigned int)(owners - 1));
+                unsigned int ticket;
+                asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
+                             : "=r"(ticket)
+                             : "l"(p.tickets + (int64_t)b * gridDim.y + blockIdx.y), "r"((unsigned int)(owners - 1))
+                             : "memory");
                 last_ticket = (ticket == (unsigned int)(owners - 1)) ? 1 : 0;
             }
             consumers_sync();
             if (last_ticket) {
-                __threadfence();
                 if (active)
-                    for (int h = 0; h < item_heads; ++h) merge_head<T, D>(p, b, qh0 + h, c0, c1, G, total, lane);
+                    for (int h = 0; h < item_heads; h += 2)
+                        merge_heads<T, D>(p, b, qh0 + h, h + 1 < item_heads, c0, c1, G, total, lane);
             }
             consumers_sync();  // last_ticket is reused by the next segment
         }
