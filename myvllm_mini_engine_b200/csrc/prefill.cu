@@ -31,10 +31,9 @@ static int64_t prefill_core_workspace(int64_t tokens, int64_t q_heads, int64_t k
 static int64_t prefill_workspace_bytes(int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
                                        int64_t head_dim, int64_t block_size, int64_t table_width,
                                        int64_t max_query_len, int dtype, int sms) {
-    (void)requests;
     (void)max_query_len;
     if (tokens <= 0) return 0;
-    if (prefill_tc_supported(q_heads, kv_heads, head_dim, block_size, dtype, 1, tokens)) return 0;
+    if (prefill_tc_supported(q_heads, kv_heads, head_dim, block_size, dtype, 1, tokens, requests)) return 0;
     return prefill_core_workspace(tokens, q_heads, kv_heads, head_dim, block_size, table_width, dtype, sms,
                                   nullptr);
 }
@@ -45,7 +44,7 @@ static int run_prefill(const void* q, const void* key_cache, const void* value_c
                        int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
                        int64_t table_width, int64_t max_query_len, int dtype, cudaStream_t stream) {
     (void)max_query_len;
-    if (prefill_tc_supported(q_heads, kv_heads, head_dim, block_size, dtype, num_blocks, tokens))
+    if (prefill_tc_supported(q_heads, kv_heads, head_dim, block_size, dtype, num_blocks, tokens, requests))
         return run_prefill_tc(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens, out,
                               tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width,
                               dtype, stream);

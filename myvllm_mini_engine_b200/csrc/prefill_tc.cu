@@ -1,10 +1,17 @@
 // Ragged causal paged prefill on the 5th-generation tensor cores (tcgen05 + TMEM).
 //
-// One CTA computes one 128-row tile of one request for one kv head: the rows
+// Work item = one 128-row query tile of one request for one kv head: the rows
 // are tm = 128 / group consecutive query tokens x the group's query heads
 // (GQA packing, so every K/V tile is loaded once for all query heads that
-// read it).  The CTA walks the request's key tiles of 128 keys, up to the
-// tile's last query position (causal):
+// read it).  The grid is persistent (one CTA per SM): every CTA orders the
+// query tiles by their number of key tiles, longest first (the same order in
+// every CTA, computed from the device metadata), and takes items in
+// boustrophedon order, so the long items start first and the CTAs end
+// together.  TMEM, the barriers and the warp pipeline live across items: the
+// next item's Q is loaded as soon as the last S MMA of the current item has
+// read Q, and its first P V waits only until the epilogue has read O.  An
+// item walks the request's key tiles of 128 keys, up to its last query
+// position (causal):
 //   S_j = Q K_j^T   tcgen05.mma kind::f16, M=128, N=128, K=D -> TMEM (fp32),
 //                   double-buffered (two 128-column S buffers)
 //   P_j = exp2(S_j * log2(e)/sqrt(D) - m)   (softmax warps), written as 16-bit
@@ -39,6 +46,8 @@ namespace minikv {
 
 constexpr int kPfThreads = 352;  // warp 0 K loads, 1 MMA/TMEM, 2-9 softmax (two warpgroups), 10 V loads
 constexpr int kPfVWarp = 10;
+constexpr int kPfMaxRequests = 4096;  // requests of one launch on this route (query-tile prefix in smem)
+constexpr int kPfMaxSort = 1024;      // query tiles sorted by cost; beyond that, natural order
 constexpr int kPfRows = 128;     // M rows per CTA (tokens x GQA heads)
 constexpr int kPfKeys = 128;     // keys per tile
 
@@ -48,7 +57,7 @@ struct PrefillTcParams {
     const int64_t* tables;
     const int64_t* ctx;
     void* out;
-    int requests, q_heads, group, num_blocks, block_size, table_width;
+    int requests, q_heads, kv_heads, group, num_blocks, block_size, table_width;
     int tm;        // query tokens per tile = 128 / group
     int box_rows;  // rows per K/V TMA box (divides block_size and 128, >= 8)
     float scale_log2;
@@ -187,9 +196,68 @@ struct PfLayout {
     static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
     static constexpr int OFF_BAR = OFF_V + 2 * KV_BYTES;
     static constexpr int OFF_RED = OFF_BAR + 256;          // [2][2][128] partial row maxima, [2][128] sums
-    static constexpr int SMEM = OFF_RED + 3 * 1024 + 1024;  // + alignment slack
+    static constexpr int OFF_PFX = OFF_RED + 3 * 1024;      // [kPfMaxRequests + 1] query-tile prefix
+    static constexpr int OFF_ORD = OFF_PFX + 4 * (kPfMaxRequests + 4);  // [kPfMaxSort] sorted query tiles
+    static constexpr int SMEM = OFF_ORD + 8 * kPfMaxSort + 1024;        // + alignment slack
     static constexpr uint32_t TMEM_COLS = 512;  // S/P 0, S/P 1 (128 columns each) and O (D columns)
 };
+
+// Query tiles of the batch, for the persistent schedule: qt_pfx[r] = number of
+// 128-row query tiles of requests < r.  One work item = (query tile, kv head).
+struct PfItem {
+    int r, m, h, n_tiles, qlen, t_lo;
+    int64_t q0, start, limit;
+    const int64_t* table;
+};
+
+// Key tiles (of 128 keys) the item's rows attend, causally: 0 for an empty item.
+__device__ __forceinline__ int pf_item_tiles(const PrefillTcParams& p, int r, int m, int64_t* q0_out, int* qlen_out,
+                                             int64_t* start_out, int64_t* limit_out) {
+    const int64_t q0 = p.cu_q[r];
+    const int qlen = (int)(p.cu_q[r + 1] - q0);
+    const int64_t start = p.starts[r];
+    const int64_t cap = (int64_t)p.table_width * p.block_size;
+    const int64_t limit = min(p.ctx[r], cap);  // keys [0, limit) exist
+    const int t_lo = m * p.tm;
+    const int64_t p_last = min(start + min(t_lo + p.tm, qlen) - 1, limit - 1);
+    if (q0_out) {
+        *q0_out = q0;
+        *qlen_out = qlen;
+        *start_out = start;
+        *limit_out = limit;
+    }
+    return (p_last < 0 || start < 0) ? 0 : (int)(p_last / kPfKeys + 1);
+}
+
+// Request owning natural query tile qt: largest r with qt_pfx[r] <= qt.
+__device__ __forceinline__ int pf_request_of(const int* qt_pfx, int B, int qt) {
+    int lo = 0, hi = B - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (qt_pfx[mid] <= qt) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ PfItem pf_item(const PrefillTcParams& p, const int* qt_pfx, const uint32_t* order,
+                                          bool sorted, int item, int kv_heads) {
+    PfItem w;
+    const int slot = item / kv_heads;
+    const int qt = sorted ? (int)(order[slot] & 0xFFFFFu) : slot;
+    w.h = item % kv_heads;
+    w.r = pf_request_of(qt_pfx, p.requests, qt);
+    w.m = qt - qt_pfx[w.r];
+    w.t_lo = w.m * p.tm;
+    w.n_tiles = pf_item_tiles(p, w.r, w.m, &w.q0, &w.qlen, &w.start, &w.limit);
+    w.table = p.tables + (int64_t)w.r * p.table_width;
+    return w;
+}
+
+// Item `k`-th of CTA c (boustrophedon over the cost-sorted items), or -1.
+__device__ __forceinline__ int pf_nth_item(int k, int c, int G, int n_items) {
+    const int i = k * G + ((k & 1) ? (G - 1 - c) : c);
+    return i < n_items ? i : -1;
+}
 
 template <typename T, int D>
 __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
@@ -203,30 +271,33 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     unsigned char* sK = smem + L::OFF_K;
     unsigned char* sV = smem + L::OFF_V;
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-    uint64_t* q_full = bar + 0;
+    uint64_t* q_full = bar + 0;    // Q of the CTA's current item landed
     uint64_t* k_full = bar + 1;    // [2] K of a key tile landed (+ its key_ok words)
     uint64_t* k_empty = bar + 3;   // [2] the S MMA is done with that K slot
     uint64_t* v_full = bar + 5;    // [2] V of a key tile landed
     uint64_t* v_empty = bar + 7;   // [2] the P V MMA is done with that V slot
     uint64_t* s_full = bar + 9;    // [2] S of a tile is in its TMEM buffer
+    uint64_t* q_empty = bar + 11;  // the last S MMA of an item has read Q
+    uint64_t* o_free = bar + 12;   // the epilogue of an item has read O
     uint64_t* p_full = bar + 13;   // P of the tile is in its TMEM buffer, O rescaled, masked V rows zeroed
     uint64_t* o_done = bar + 14;   // the P V product of the tile has been accumulated into O
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 15);
-    int* info = reinterpret_cast<int*>(bar + 16);               // request, tile
-    // [4][4] validity bits of key tile j in slot j % 4: the producer rewrites a
-    // slot for tile j + 4 only after S(j + 2), which needs the softmax of tile j
-    // to have read its S buffer (and these words) first
+    int* info = reinterpret_cast<int*>(bar + 16);               // number of query tiles, sorted flag
+    // [4][4] validity bits of key tile g (CTA-wide tile counter) in slot g % 4:
+    // the producer rewrites a slot for tile g + 4 only after S(g + 2), which
+    // needs the softmax of tile g to have read its S buffer (and these words)
     uint32_t* key_ok = reinterpret_cast<uint32_t*>(bar + 18);
+    int* qt_pfx = reinterpret_cast<int*>(smem + L::OFF_PFX);         // [requests + 1]
+    uint32_t* order = reinterpret_cast<uint32_t*>(smem + L::OFF_ORD);  // [kPfMaxSort] sorted keys, then the keys
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int B = p.requests, G = p.group, TM = p.tm;
-    const int h = blockIdx.y;  // kv head
+    const int Hkv = p.kv_heads;
 
-    // ---- which (request, query tile) this CTA computes
+    // ---- query-tile prefix over the requests (warp 0)
     if (warp == 0) {
-        const int target = blockIdx.x;
-        int run = 0, found = -1, tile = 0;
-        for (int base = 0; base < B && found < 0; base += 32) {
+        int run = 0;
+        for (int base = 0; base < B; base += 32) {
             const int r = base + lane;
             int t = 0;
             if (r < B) t = (int)((p.cu_q[r + 1] - p.cu_q[r] + TM - 1) / TM);
@@ -237,37 +308,19 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                 const int v = __shfl_up_sync(0xffffffffu, incl, off);
                 if (lane >= off) incl += v;
             }
-            const bool hit = r < B && t > 0 && run + incl - t <= target && target < run + incl;
-            const unsigned who = __ballot_sync(0xffffffffu, hit);
-            if (who) {
-                const int src = __ffs(who) - 1;
-                found = base + src;
-                tile = target - (run + __shfl_sync(0xffffffffu, incl - t, src));
-            }
+            if (r < B) qt_pfx[r] = run + incl - t;
             run += __shfl_sync(0xffffffffu, incl, 31);
         }
         if (lane == 0) {
-            info[0] = found;
-            info[1] = tile;
+            qt_pfx[B] = run;
+            info[0] = run;
+            info[1] = run <= kPfMaxSort ? 1 : 0;
         }
     }
-    __syncthreads();
-    const int r = info[0];
-    if (r < 0) return;  // grid is an upper bound on the number of query tiles
-    const int m = info[1];
-
-    const int64_t q0 = p.cu_q[r];
-    const int qlen = (int)(p.cu_q[r + 1] - q0);
-    const int64_t start = p.starts[r];
-    const int64_t cap = (int64_t)p.table_width * p.block_size;
-    const int64_t limit = min(p.ctx[r], cap);  // keys [0, limit) exist
-    const int t_lo = m * TM;
-    const int64_t p_last = min(start + min(t_lo + TM, qlen) - 1, limit - 1);
-    const int n_tiles = (p_last < 0 || start < 0) ? 0 : (int)(p_last / kPfKeys + 1);
-    const int64_t* table = p.tables + (int64_t)r * p.table_width;
-
     if (tid == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
+        mbar_init(o_free, 8);
         for (int s = 0; s < 2; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
@@ -288,38 +341,68 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;  // columns: S0 [0,128) | S1 [128,256) | O [256, 256+D)
+    const int n_qt = info[0];
+    const bool sorted = info[1] != 0;
+    const int n_items = n_qt * Hkv;
+
+    // ---- longest first: order the query tiles by key tiles (descending), ties by
+    // index, identically in every CTA.  Keys are unique, so a key's rank is the
+    // number of smaller keys: two barriers, O(n^2 / threads) compares.
+    if (sorted) {
+        uint32_t* keys = order + kPfMaxSort;
+        for (int i = tid; i < n_qt; i += blockDim.x) {
+            const int r = pf_request_of(qt_pfx, B, i);
+            const int cost = min(pf_item_tiles(p, r, i - qt_pfx[r], nullptr, nullptr, nullptr, nullptr), 1023);
+            keys[i] = ((uint32_t)(1023 - cost) << 20) | (uint32_t)i;
+        }
+        __syncthreads();
+        for (int i = tid; i < n_qt; i += blockDim.x) {
+            const uint32_t key = keys[i];
+            int rank = 0;
+            for (int j = 0; j < n_qt; ++j) rank += keys[j] < key ? 1 : 0;
+            order[rank] = key;
+        }
+        __syncthreads();
+    }
+    const int c = blockIdx.x, nC = gridDim.x;
 
     if (warp == 0 || warp == kPfVWarp) {
         // ------------------------------------------------------------ TMA producers
-        // Warp 0 loads K and warp 10 loads V, each on its own ring of two
+        // Warp 0 loads Q and K, warp 10 loads V, each on its own ring of two
         // slots, so a K slot is refilled as soon as the S MMA has read it,
         // whatever the P V MMAs are doing (two warps, because a warp that ran
         // both rings would reconverge after every wait).  Lane l owns box l
         // (R keys on one page) of a tile; its page id is read one tile ahead.
-        if (n_tiles > 0) {
-            if (warp == 0 && lane == 0) {
+        const bool is_v = warp == kPfVWarp;
+        const int box = lane;
+        const unsigned full_mask = 0xffffffffu;
+        const int R = p.box_rows, groups = kPfKeys / R;  // groups <= 16
+        uint64_t* full = is_v ? v_full : k_full;
+        uint64_t* empty = is_v ? v_empty : k_empty;
+        const CUtensorMap* map = is_v ? &tm_v : &tm_k;
+        unsigned char* ring = is_v ? sV : sK;
+        int gt = 0, active = 0;
+        for (int k = 0;; ++k) {
+            const int it = pf_nth_item(k, c, nC, n_items);
+            if (it < 0) break;
+            const PfItem w = pf_item(p, qt_pfx, order, sorted, it, Hkv);
+            if (w.n_tiles == 0) continue;
+            if (!is_v && lane == 0) {
+                if (active > 0) mbar_wait(q_empty, (active - 1) & 1);
                 mbar_arrive_expect_tx(q_full, (uint32_t)L::Q_BYTES);
 #pragma unroll
                 for (int kb = 0; kb < L::KB; ++kb)
-                    tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, h * G, (int)(q0 + t_lo), q_full);
+                    tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, w.h * G, (int)(w.q0 + w.t_lo), q_full);
             }
-            const bool is_v = warp == kPfVWarp;
-            const int box = lane;
-            const unsigned full_mask = 0xffffffffu;
-            const int R = p.box_rows, groups = kPfKeys / R;  // groups <= 16
             auto box_page = [&](int j) -> int64_t {  // physical page of this lane's box of tile j, or -1
                 const int64_t k0 = (int64_t)j * kPfKeys + box * R;
-                if (box >= groups || j >= n_tiles || k0 >= limit) return -1;
-                const int64_t page = table[k0 / p.block_size];
+                if (box >= groups || j >= w.n_tiles || k0 >= w.limit) return -1;
+                const int64_t page = w.table[k0 / p.block_size];
                 return (page >= 0 && page < p.num_blocks) ? page : -1;
             };
-            uint64_t* full = is_v ? v_full : k_full;
-            uint64_t* empty = is_v ? v_empty : k_empty;
-            const CUtensorMap* map = is_v ? &tm_v : &tm_k;
-            unsigned char* ring = is_v ? sV : sK;
             int64_t page = box_page(0);
-            for (int j = 0; j < n_tiles; ++j) {
-                const int slot = j & 1;
+            for (int j = 0; j < w.n_tiles; ++j, ++gt) {
+                const int slot = gt & 1;
                 const int64_t key0 = (int64_t)j * kPfKeys;
                 const int64_t next_page = box_page(j + 1);  // in flight while this tile is issued
                 const bool valid = page >= 0;
@@ -331,7 +414,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                         uint32_t bits = 0;
                         if (valid) {
                             const int64_t lo = max((int64_t)q * 32, (int64_t)box * R);
-                            const int64_t hi = min(min((int64_t)q * 32 + 32, (int64_t)box * R + R), limit - key0);
+                            const int64_t hi = min(min((int64_t)q * 32 + 32, (int64_t)box * R + R), w.limit - key0);
                             if (hi > lo) {
                                 const int n = (int)(hi - lo);
                                 bits = (n == 32 ? 0xffffffffu : ((1u << n) - 1u)) << (int)(lo - q * 32);
@@ -341,11 +424,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                     }
                 }
                 const uint32_t bytes = (uint32_t)__popc(__ballot_sync(full_mask, valid)) * L::KB * R * 128;
-                if (j >= 2) mbar_wait(&empty[slot], ((j >> 1) - 1) & 1);
+                if (gt >= 2) mbar_wait(&empty[slot], ((gt >> 1) - 1) & 1);
                 if (box == 0) {
                     if (!is_v) {
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) key_ok[4 * (j & 3) + q] = words[q];
+                        for (int q = 0; q < 4; ++q) key_ok[4 * (gt & 3) + q] = words[q];
                     }
                     mbar_arrive_expect_tx(&full[slot], bytes);
                 }
@@ -355,73 +438,90 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                     unsigned char* dst = ring + slot * L::KV_BYTES + box * R * 128;
 #pragma unroll
                     for (int kb = 0; kb < L::KB; ++kb)
-                        tma_load_3d(dst + kb * L::BLOCK_BYTES, map, kb * 64, h, z, &full[slot]);
+                        tma_load_3d(dst + kb * L::BLOCK_BYTES, map, kb * 64, w.h, z, &full[slot]);
                 }
                 page = next_page;
             }
+            ++active;
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         // S(j) and P V(j) are issued in whichever order their operands become
         // ready (non-blocking probes), so a late K tile never holds back a
         // P V product whose P is done, and S runs up to two tiles ahead.
-        if (lane == 0 && n_tiles > 0) {
+        if (lane == 0) {
             constexpr uint32_t idesc_s = umma_idesc(128, kPfKeys, kBf16, false);
             constexpr uint32_t idesc_o = umma_idesc(128, D, kBf16, true);
             const uint32_t t_o = tmem + 2 * kPfKeys;
             const uint32_t q_addr = smem_addr(sQ);
-            mbar_wait(q_full, 0);
-            int ns = 0, npv = 0;  // next S and next P V to issue
-            uint64_t idle_since = 0;
-            while (npv < n_tiles) {
-                bool progressed = false;
-                if (ns < n_tiles) {
-                    const int slot = ns & 1;
-                    // the buffer of S(ns) holds P(ns - 2) until P V(ns - 2) has read it: MMAs of
-                    // one thread run in issue order, so S(ns) goes after that product is issued
-                    if ((ns < 2 || npv >= ns - 1) && mbar_test_wait(&k_full[slot], (ns >> 1) & 1)) {
-                        tc_fence_after();
-                        const uint32_t k_addr = smem_addr(sK + slot * L::KV_BYTES);
+            int gt = 0, active = 0;
+            bool failed = false;
+            for (int k = 0; !failed; ++k) {
+                const int it = pf_nth_item(k, c, nC, n_items);
+                if (it < 0) break;
+                const PfItem w = pf_item(p, qt_pfx, order, sorted, it, Hkv);
+                const int n_tiles = w.n_tiles;
+                if (n_tiles == 0) continue;
+                mbar_wait(q_full, active & 1);
+                int ns = 0, npv = 0;  // next S and next P V of this item
+                uint64_t idle_since = 0;
+                while (npv < n_tiles) {
+                    bool progressed = false;
+                    if (ns < n_tiles) {
+                        const int gs = gt + ns, slot = gs & 1;
+                        // the buffer of S(gs) holds P(gs - 2) until P V(gs - 2) has read it: MMAs of
+                        // one thread run in issue order, so S(gs) goes after that product is issued
+                        // (for the first two tiles of an item, every earlier product is issued)
+                        if ((ns < 2 || npv >= ns - 1) && mbar_test_wait(&k_full[slot], (gs >> 1) & 1)) {
+                            tc_fence_after();
+                            const uint32_t k_addr = smem_addr(sK + slot * L::KV_BYTES);
 #pragma unroll
-                        for (int kk = 0; kk < D / 16; ++kk) {
-                            const uint32_t off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
-                            umma_f16(tmem + slot * kPfKeys, smem_desc(q_addr + off, 16, 1024),
-                                     smem_desc(k_addr + off, 16, 1024), idesc_s, kk > 0);
+                            for (int kk = 0; kk < D / 16; ++kk) {
+                                const uint32_t off = (kk >> 2) * L::BLOCK_BYTES + (kk & 3) * 32;
+                                umma_f16(tmem + slot * kPfKeys, smem_desc(q_addr + off, 16, 1024),
+                                         smem_desc(k_addr + off, 16, 1024), idesc_s, kk > 0);
+                            }
+                            umma_commit(&s_full[slot]);
+                            umma_commit(&k_empty[slot]);
+                            if (ns == n_tiles - 1) umma_commit(q_empty);
+                            ++ns;
+                            progressed = true;
                         }
-                        umma_commit(&s_full[slot]);
-                        umma_commit(&k_empty[slot]);
-                        ++ns;
+                    }
+                    const int gp = gt + npv;
+                    if (npv < ns && (npv > 0 || active == 0 || mbar_test_wait(o_free, (active - 1) & 1)) &&
+                        mbar_test_wait(&v_full[gp & 1], (gp >> 1) & 1) && mbar_test_wait(p_full, gp & 1)) {
+                        tc_fence_after();
+                        const uint32_t v_addr = smem_addr(sV + (gp & 1) * L::KV_BYTES);
+#pragma unroll
+                        for (int kk = 0; kk < kPfKeys / 16; ++kk)  // P: 16 keys = 8 TMEM columns per step
+                            umma_f16_tmem_a(t_o, tmem + (gp & 1) * kPfKeys + kk * 8,
+                                            smem_desc(v_addr + kk * 16 * 128, L::BLOCK_BYTES, 1024), idesc_o,
+                                            (npv > 0 || kk > 0));
+                        umma_commit(o_done);
+                        umma_commit(&v_empty[gp & 1]);
+                        ++npv;
                         progressed = true;
                     }
-                }
-                if (npv < ns && mbar_test_wait(&v_full[npv & 1], (npv >> 1) & 1) && mbar_test_wait(p_full, npv & 1)) {
-                    tc_fence_after();
-                    const uint32_t v_addr = smem_addr(sV + (npv & 1) * L::KV_BYTES);
-#pragma unroll
-                    for (int kk = 0; kk < kPfKeys / 16; ++kk)  // P: 16 keys = 8 TMEM columns per step
-                        umma_f16_tmem_a(t_o, tmem + (npv & 1) * kPfKeys + kk * 8,
-                                        smem_desc(v_addr + kk * 16 * 128, L::BLOCK_BYTES, 1024), idesc_o,
-                                        (npv > 0 || kk > 0));
-                    umma_commit(o_done);
-                    umma_commit(&v_empty[npv & 1]);
-                    ++npv;
-                    progressed = true;
-                }
-                if (progressed) {
-                    idle_since = 0;
-                } else {
-                    // bounded: the same limit as every other wait, then give up (status bit set)
-                    __nanosleep(32);
-                    const uint64_t now = global_ns();
-                    if (idle_since == 0) {
-                        idle_since = now;
-                    } else if (now - idle_since > kWaitLimitNs ||
-                               (now - idle_since > kWaitCheckNs &&
-                                (*reinterpret_cast<volatile unsigned int*>(&g_status) & kStatusWaitTimeout))) {
-                        raise_status(kStatusWaitTimeout);
-                        break;
+                    if (progressed) {
+                        idle_since = 0;
+                    } else {
+                        // bounded: the same limit as every other wait, then give up (status bit set)
+                        __nanosleep(32);
+                        const uint64_t now = global_ns();
+                        if (idle_since == 0) {
+                            idle_since = now;
+                        } else if (now - idle_since > kWaitLimitNs ||
+                                   (now - idle_since > kWaitCheckNs &&
+                                    (*reinterpret_cast<volatile unsigned int*>(&g_status) & kStatusWaitTimeout))) {
+                            raise_status(kStatusWaitTimeout);
+                            failed = true;
+                            break;
+                        }
                     }
                 }
+                gt += n_tiles;
+                ++active;
             }
         }
     } else {
@@ -430,7 +530,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
         // columns [64 half, 64 half + 64) of S and P and O columns
         // [half D/2, (half + 1) D/2).  The two threads of a row exchange their
         // partial maxima once per tile (shared memory + a 256-thread barrier),
-        // keep partial sums, and add them at the end.
+        // keep partial sums, and add them at the end of the item.
         constexpr int kHalfKeys = kPfKeys / 2, kHalfD = D / 2;
         float* red = reinterpret_cast<float*>(smem + L::OFF_RED);  // [2][2][128] maxima, then [2][128] sums
         const int sw = warp - 2;                 // 0..7
@@ -440,146 +540,161 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
         const int st = sw * 32 + lane;           // 0..255: masked-key V zeroing (row st & 127, K-blocks from st >> 7)
         const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
         const uint32_t t_o = tmem + lane_base + 2 * kPfKeys + half * kHalfD;
-        const int t = t_lo + row / G, g = row % G;
-        const int64_t pos = start + t;
-        const bool row_valid = t < qlen && pos < limit;
         const float scale = p.scale_log2;
-        // Running max (log2 domain) and partial sum.  The max is raised lazily: P
-        // is computed against m_run as long as no score exceeds it by more than
-        // 2^8, so O (accumulated in TMEM) is rescaled only when m_run moves.
-        float m_run = -INFINITY, l_run = 0.f;
-        for (int j = 0; j < n_tiles; ++j) {
-            const int slot = j & 1;
-            mbar_wait(&k_full[slot], (j >> 1) & 1);
-            uint32_t w[4];
+        int gt = 0;
+        for (int k = 0;; ++k) {
+            const int it = pf_nth_item(k, c, nC, n_items);
+            if (it < 0) break;
+            const PfItem w = pf_item(p, qt_pfx, order, sorted, it, Hkv);
+            const int n_tiles = w.n_tiles;
+            const int t = w.t_lo + row / G, g = row % G;
+            const int64_t pos = w.start + t;
+            const bool row_valid = t < w.qlen && pos < w.limit;
+            // Running max (log2 domain) and partial sum.  The max is raised lazily: P
+            // is computed against m_run as long as no score exceeds it by more than
+            // 2^8, so O (accumulated in TMEM) is rescaled only when m_run moves.
+            float m_run = -INFINITY, l_run = 0.f;
+            for (int j = 0; j < n_tiles; ++j) {
+                const int gj = gt + j, slot = gj & 1;
+                mbar_wait(&k_full[slot], (gj >> 1) & 1);
+                uint32_t wk[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) w[q] = key_ok[4 * (j & 3) + q];
-            // keys [0, rel] of this tile are causally visible to the row
-            const int64_t rel = pos - (int64_t)j * kPfKeys;
-            uint32_t bits[2];
+                for (int q = 0; q < 4; ++q) wk[q] = key_ok[4 * (gj & 3) + q];
+                // keys [0, rel] of this tile are causally visible to the row
+                const int64_t rel = pos - (int64_t)j * kPfKeys;
+                uint32_t bits[2];
 #pragma unroll
-            for (int qq = 0; qq < 2; ++qq) {
-                const int q = 2 * half + qq;
-                const int64_t lim = rel - q * 32;
-                const uint32_t causal = lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : ((2u << (int)lim) - 1u));
-                bits[qq] = row_valid ? (w[q] & causal) : 0u;
-            }
-            const bool full = (bits[0] & bits[1]) == 0xffffffffu;
-
-            mbar_wait(&s_full[slot], (j >> 1) & 1);
-            tc_fence_after();
-            float s[kHalfKeys];
-            tmem_load_32(tmem + lane_base + slot * kPfKeys + half * kHalfKeys, s);
-            tmem_load_32(tmem + lane_base + slot * kPfKeys + half * kHalfKeys + 32, s + 32);
-
-            float mxs[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-            if (full) {
-#pragma unroll
-                for (int e = 0; e < kHalfKeys; ++e) mxs[e & 3] = fmaxf(mxs[e & 3], s[e]);
-            } else {
-#pragma unroll
-                for (int e = 0; e < kHalfKeys; ++e)
-                    if ((bits[e >> 5] >> (e & 31)) & 1u) mxs[e & 3] = fmaxf(mxs[e & 3], s[e]);
-            }
-            float* mred = red + (j & 1) * 256;
-            mred[half * 128 + row] = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
-            softmax_sync();  // also: both halves of the S buffer have been read, P may overwrite it
-            const float mx = fmaxf(mred[row], mred[128 + row]);
-            const float m_tile = mx * scale;  // -inf when the row sees no key of this tile
-            float m_use = m_run, alpha = 1.f;
-            bool rescale = false;
-            if (m_tile > m_run + 8.f) {
-                alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_tile);
-                rescale = m_run != -INFINITY;  // O holds only zeros while m_run is -inf
-                m_use = m_tile;
-            }
-            // P (16-bit, two keys per column) over the first 64 columns of this
-            // tile's S buffer: keys 64 half .. 64 half + 63 at columns 32 half ..
-            float sums[4] = {0.f, 0.f, 0.f, 0.f};
-            const float neg = -m_use;
-            float packed[32];
-#pragma unroll
-            for (int e = 0; e < kHalfKeys; e += 2) {
-                float pe[2];
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int k = e + u;
-                    const float x = fast_exp2(fmaf(s[k], scale, neg));
-                    pe[u] = (full || ((bits[k >> 5] >> (k & 31)) & 1u)) ? x : 0.f;
-                    sums[k & 3] += pe[u];
+                for (int qq = 0; qq < 2; ++qq) {
+                    const int q = 2 * half + qq;
+                    const int64_t lim = rel - q * 32;
+                    const uint32_t causal = lim >= 31 ? 0xffffffffu : (lim < 0 ? 0u : ((2u << (int)lim) - 1u));
+                    bits[qq] = row_valid ? (wk[q] & causal) : 0u;
                 }
-                packed[e / 2] = __uint_as_float(Elem<T>::pack(pe[0], pe[1]));
+                const bool full = (bits[0] & bits[1]) == 0xffffffffu;
+
+                mbar_wait(&s_full[slot], (gj >> 1) & 1);
+                tc_fence_after();
+                float s[kHalfKeys];
+                tmem_load_32(tmem + lane_base + slot * kPfKeys + half * kHalfKeys, s);
+                tmem_load_32(tmem + lane_base + slot * kPfKeys + half * kHalfKeys + 32, s + 32);
+
+                float mxs[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+                if (full) {
+#pragma unroll
+                    for (int e = 0; e < kHalfKeys; ++e) mxs[e & 3] = fmaxf(mxs[e & 3], s[e]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < kHalfKeys; ++e)
+                        if ((bits[e >> 5] >> (e & 31)) & 1u) mxs[e & 3] = fmaxf(mxs[e & 3], s[e]);
+                }
+                float* mred = red + (gj & 1) * 256;
+                mred[half * 128 + row] = fmaxf(fmaxf(mxs[0], mxs[1]), fmaxf(mxs[2], mxs[3]));
+                softmax_sync();  // also: both halves of the S buffer have been read, P may overwrite it
+                const float mx = fmaxf(mred[row], mred[128 + row]);
+                const float m_tile = mx * scale;  // -inf when the row sees no key of this tile
+                float m_use = m_run, alpha = 1.f;
+                bool rescale = false;
+                if (m_tile > m_run + 8.f) {
+                    alpha = (m_run == -INFINITY) ? 0.f : fast_exp2(m_run - m_tile);
+                    rescale = m_run != -INFINITY;  // O holds only zeros while m_run is -inf
+                    m_use = m_tile;
+                }
+                // P (16-bit, two keys per column) over the first 64 columns of this
+                // tile's S buffer: keys 64 half .. 64 half + 63 at columns 32 half ..
+                float sums[4] = {0.f, 0.f, 0.f, 0.f};
+                const float neg = -m_use;
+                float packed[32];
+#pragma unroll
+                for (int e = 0; e < kHalfKeys; e += 2) {
+                    float pe[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const int kx = e + u;
+                        const float x = fast_exp2(fmaf(s[kx], scale, neg));
+                        pe[u] = (full || ((bits[kx >> 5] >> (kx & 31)) & 1u)) ? x : 0.f;
+                        sums[kx & 3] += pe[u];
+                    }
+                    packed[e / 2] = __uint_as_float(Elem<T>::pack(pe[0], pe[1]));
+                }
+                tmem_store_32(tmem + lane_base + slot * kPfKeys + half * 32, packed);
+                tmem_store_wait();
+                // O may be rescaled only once the previous P V product has landed in it
+                if (j > 0) {
+                    mbar_wait(o_done, (gj - 1) & 1);
+                    tc_fence_after();
+                }
+                // tcgen05.ld / st are warp-wide (.sync.aligned): the whole warp takes
+                // this branch when any of its rows rescales; the others scale by 1.
+                if (__any_sync(0xffffffffu, rescale)) {
+                    const float factor = rescale ? alpha : 1.f;
+#pragma unroll
+                    for (int cc = 0; cc < kHalfD / 32; ++cc) {
+                        float v[32];
+                        tmem_load_32(t_o + cc * 32, v);
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) v[e] *= factor;
+                        tmem_store_32(t_o + cc * 32, v);
+                    }
+                    tmem_store_wait();
+                }
+                l_run = l_run * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
+                m_run = m_use;
+                const int vrow_key = st & 127;
+                if (!((wk[vrow_key >> 5] >> (vrow_key & 31)) & 1u)) {
+                    // V rows of masked keys must be finite zeros before P V runs (a
+                    // loaded box can hold rows past the context; unloaded rows hold stale data)
+                    mbar_wait(&v_full[slot], (gj >> 1) & 1);
+                    unsigned char* vrow = sV + slot * L::KV_BYTES + vrow_key * 128;
+                    for (int kb = st >> 7; kb < L::KB; kb += 2) {
+                        uint4* v4 = reinterpret_cast<uint4*>(vrow + kb * L::BLOCK_BYTES);
+#pragma unroll
+                        for (int cc = 0; cc < 8; ++cc) v4[cc] = make_uint4(0, 0, 0, 0);
+                    }
+                }
+                fence_async_smem();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(p_full);
             }
-            tmem_store_32(tmem + lane_base + slot * kPfKeys + half * 32, packed);
-            tmem_store_wait();
-            // O may be rescaled only once the previous P V product has landed in it
-            if (j > 0) {
-                mbar_wait(o_done, (j - 1) & 1);
+            // row sum = the two threads' partial sums
+            float* lred = red + 512;
+            lred[half * 128 + row] = l_run;
+            softmax_sync();
+            const float l_row = lred[row] + lred[128 + row];
+            if (n_tiles > 0) {
+                mbar_wait(o_done, (gt + n_tiles - 1) & 1);
                 tc_fence_after();
             }
-            // tcgen05.ld / st are warp-wide (.sync.aligned): the whole warp takes
-            // this branch when any of its rows rescales; the others scale by 1.
-            if (__any_sync(0xffffffffu, rescale)) {
-                const float factor = rescale ? alpha : 1.f;
+            // every lane of the warp loads (warp-wide tcgen05.ld); rows past the chunk store nothing
+            const float inv = (row_valid && l_row > 0.f) ? 1.f / l_row : 0.f;
+            T* orow = static_cast<T*>(p.out) + ((w.q0 + t) * p.q_heads + w.h * G + g) * D + half * kHalfD;
 #pragma unroll
-                for (int c = 0; c < kHalfD / 32; ++c) {
-                    float v[32];
-                    tmem_load_32(t_o + c * 32, v);
+            for (int cc = 0; cc < kHalfD / 32; ++cc) {
+                float v[32];
+                if (n_tiles > 0) {
+                    tmem_load_32(t_o + cc * 32, v);
+                } else {
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) v[e] *= factor;
-                    tmem_store_32(t_o + c * 32, v);
+                    for (int e = 0; e < 32; ++e) v[e] = 0.f;
                 }
-                tmem_store_wait();
-            }
-            l_run = l_run * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
-            m_run = m_use;
-            const int vrow_key = st & 127;
-            if (!((w[vrow_key >> 5] >> (vrow_key & 31)) & 1u)) {
-                // V rows of masked keys must be finite zeros before P V runs (a
-                // loaded box can hold rows past the context; unloaded rows hold stale data)
-                mbar_wait(&v_full[slot], (j >> 1) & 1);
-                unsigned char* vrow = sV + slot * L::KV_BYTES + vrow_key * 128;
-                for (int kb = st >> 7; kb < L::KB; kb += 2) {
-                    uint4* v4 = reinterpret_cast<uint4*>(vrow + kb * L::BLOCK_BYTES);
+                if (t < w.qlen) {
 #pragma unroll
-                    for (int c = 0; c < 8; ++c) v4[c] = make_uint4(0, 0, 0, 0);
+                    for (int d = 0; d < 32; d += 8) {
+                        float f[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) f[e] = v[d + e] * inv;
+                        *reinterpret_cast<uint4*>(orow + cc * 32 + d) = Elem<T>::store(f);
+                    }
                 }
             }
-            fence_async_smem();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-        }
-        // row sum = the two threads' partial sums
-        float* lred = red + 512;
-        lred[half * 128 + row] = l_run;
-        softmax_sync();
-        const float l_row = lred[row] + lred[128 + row];
-        if (n_tiles > 0) {
-            mbar_wait(o_done, (n_tiles - 1) & 1);
-            tc_fence_after();
-        }
-        // every lane of the warp loads (warp-wide tcgen05.ld); rows past the chunk store nothing
-        const float inv = (row_valid && l_row > 0.f) ? 1.f / l_row : 0.f;
-        T* orow = static_cast<T*>(p.out) + ((q0 + t) * p.q_heads + h * G + g) * D + half * kHalfD;
-#pragma unroll
-        for (int c = 0; c < kHalfD / 32; ++c) {
-            float v[32];
             if (n_tiles > 0) {
-                tmem_load_32(t_o + c * 32, v);
-            } else {
-#pragma unroll
-                for (int e = 0; e < 32; ++e) v[e] = 0.f;
+                // O has been read: the next item's first P V may overwrite it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(o_free);
             }
-            if (t < qlen) {
-#pragma unroll
-                for (int d = 0; d < 32; d += 8) {
-                    float f[8];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) f[e] = v[d + e] * inv;
-                    *reinterpret_cast<uint4*>(orow + c * 32 + d) = Elem<T>::store(f);
-                }
-            }
+            softmax_sync();  // the sums of this item are read before the next item writes them
+            gt += n_tiles;
         }
         tc_fence_before();
     }
@@ -635,8 +750,9 @@ static int gcd_int(int a, int b) {
 
 // Shapes the tensor-core route handles.
 static bool prefill_tc_supported(int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t block_size,
-                                 int dtype, int64_t num_blocks, int64_t tokens) {
+                                 int dtype, int64_t num_blocks, int64_t tokens, int64_t requests) {
     if (dtype == MINIKV_F32 || (head_dim != 64 && head_dim != 128)) return false;
+    if (requests > kPfMaxRequests) return false;
     const int64_t group = q_heads / kv_heads;
     if (group < 1 || 128 % group != 0 || kv_heads > 65535) return false;
     if (gcd_int((int)std::min<int64_t>(block_size, 1 << 20), 128) < 8) return false;
@@ -645,12 +761,12 @@ static bool prefill_tc_supported(int64_t q_heads, int64_t kv_heads, int64_t head
 
 template <typename T, int D>
 static cudaError_t launch_prefill_tc_typed(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                                           const PrefillTcParams& p, int grid_x, int kv_heads, cudaStream_t stream) {
+                                           const PrefillTcParams& p, int grid, cudaStream_t stream) {
     using L = PfLayout<T, D>;
     auto kernel = paged_prefill_tc_kernel<T, D>;
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
     if (err != cudaSuccess) return err;
-    kernel<<<dim3(grid_x, kv_heads), kPfThreads, L::SMEM, stream>>>(mq, mk, mv, p);
+    kernel<<<dim3(grid), kPfThreads, L::SMEM, stream>>>(mq, mk, mv, p);
     return cudaGetLastError();
 }
 
@@ -676,6 +792,7 @@ static int run_prefill_tc(const void* q, const void* key_cache, const void* valu
     p.out = out;
     p.requests = (int)requests;
     p.q_heads = (int)q_heads;
+    p.kv_heads = (int)kv_heads;
     p.group = group;
     p.num_blocks = (int)num_blocks;
     p.block_size = (int)block_size;
@@ -683,15 +800,18 @@ static int run_prefill_tc(const void* q, const void* key_cache, const void* valu
     p.tm = tm;
     p.box_rows = box_rows;
     p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
-    const int64_t grid_x = (tokens + tm - 1) / tm + requests;  // >= number of query tiles
-    if (grid_x > 2147483647) return fail(MINIKV_EINVAL, "too many paged prefill tiles");
+    // persistent grid: one CTA per SM, or fewer when the batch has fewer work items
+    // (an upper bound: query tiles <= tokens / tm + requests, times the kv heads)
+    const int64_t items_bound = ((tokens + tm - 1) / tm + requests) * kv_heads;
+    if ((tokens + tm - 1) / tm + requests >= (1 << 20)) return fail(MINIKV_EINVAL, "too many paged prefill tiles");
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items_bound, sm_count()));
     cudaError_t err;
     if (bf16)
-        err = head_dim == 64 ? launch_prefill_tc_typed<__nv_bfloat16, 64>(mq, mk, mv, p, (int)grid_x, (int)kv_heads, stream)
-                             : launch_prefill_tc_typed<__nv_bfloat16, 128>(mq, mk, mv, p, (int)grid_x, (int)kv_heads, stream);
+        err = head_dim == 64 ? launch_prefill_tc_typed<__nv_bfloat16, 64>(mq, mk, mv, p, grid, stream)
+                             : launch_prefill_tc_typed<__nv_bfloat16, 128>(mq, mk, mv, p, grid, stream);
     else
-        err = head_dim == 64 ? launch_prefill_tc_typed<__half, 64>(mq, mk, mv, p, (int)grid_x, (int)kv_heads, stream)
-                             : launch_prefill_tc_typed<__half, 128>(mq, mk, mv, p, (int)grid_x, (int)kv_heads, stream);
+        err = head_dim == 64 ? launch_prefill_tc_typed<__half, 64>(mq, mk, mv, p, grid, stream)
+                             : launch_prefill_tc_typed<__half, 128>(mq, mk, mv, p, grid, stream);
     if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_prefill tcgen05 launch");
     return MINIKV_OK;
 }
