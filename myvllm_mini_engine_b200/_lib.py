@@ -8,6 +8,7 @@ raises RuntimeError.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 from pathlib import Path
@@ -76,6 +77,16 @@ def dtype_code(dtype):
         return DTYPE_CODES[dtype]
     except KeyError:
         raise RuntimeError("FP32/FP16/BF16 required") from None
+
+
+_NO_SWITCH = contextlib.nullcontext()
+
+
+def on_device(device):
+    """Context that makes ``device`` the current CUDA device; free when it already is."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return _NO_SWITCH
+    return torch.cuda.device(device)
 
 
 def stream_of(device) -> int:

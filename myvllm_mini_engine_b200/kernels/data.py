@@ -75,7 +75,7 @@ def write_kv_cache(key_cache, value_cache, block_ids, token_offset, key, value,
         return
     lib = _lib.load()
     row = key.shape[1] * key.shape[2]
-    with torch.cuda.device(key_cache.device):
+    with _lib.on_device(key_cache.device):
         status = lib.minikv_kv_write_range(
             key_cache.data_ptr(), value_cache.data_ptr(), ids.data_ptr(), ids.numel(), int(token_offset),
             key.data_ptr(), value.data_ptr(), tokens, key_cache.shape[0], block_size, key.shape[1], key.shape[2],
@@ -112,7 +112,7 @@ def write_kv_cache_batch(key_cache, value_cache, block_tables, token_offsets, ke
         return
     lib = _lib.load()
     row = key.shape[1] * key.shape[2]
-    with torch.cuda.device(key_cache.device):
+    with _lib.on_device(key_cache.device):
         status = lib.minikv_kv_append_batch(
             key_cache.data_ptr(), value_cache.data_ptr(), tables.data_ptr(), offsets.data_ptr(), key.data_ptr(),
             value.data_ptr(), batch, tables.shape[1], key_cache.shape[0], block_size, key.shape[1], key.shape[2],
@@ -164,7 +164,7 @@ def write_kv_cache_slots(key_cache, value_cache, slot_mapping, key, value, *, ba
     key, key_stride = _rows(key)
     value, value_stride = _rows(value)
     lib = _lib.load()
-    with torch.cuda.device(key_cache.device):
+    with _lib.on_device(key_cache.device):
         status = lib.minikv_kv_scatter_slots(
             key_cache.data_ptr(), value_cache.data_ptr(), slot_mapping.data_ptr(), key.data_ptr(),
             value.data_ptr(), tokens, key_cache.shape[0], key_cache.shape[1], key_cache.shape[2],
@@ -204,7 +204,7 @@ def copy_blocks(key_pool, value_pool, pairs, *, validate=True):
     lib = _lib.load()
     layers, num_blocks = key_pool.shape[:2]
     block_elems = key_pool[0, 0].numel()
-    with torch.cuda.device(key_pool.device):
+    with _lib.on_device(key_pool.device):
         status = lib.minikv_copy_blocks(key_pool.data_ptr(), value_pool.data_ptr(), pairs.data_ptr(),
                                         pairs.shape[0], layers, num_blocks, block_elems,
                                         _lib.dtype_code(key_pool.dtype), _lib.stream_of(key_pool.device))

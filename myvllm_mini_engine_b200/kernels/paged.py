@@ -88,7 +88,7 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
         if need < 0:
             _lib.check(_lib.EINVAL, "paged_attention")
         _WS_BYTES[key] = need
-    with torch.cuda.device(query.device):
+    with _lib.on_device(query.device):
         stream = torch.cuda.current_stream(query.device)
         if workspace is None:
             workspace = _workspace(query.device, stream, need)

@@ -88,7 +88,7 @@ def paged_prefill_attention(q, key_cache, value_cache, cu_seqlens_q, query_start
     if need < 0:
         _lib.check(_lib.EINVAL, "paged_prefill_attention")
     workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
-    with torch.cuda.device(q.device):
+    with _lib.on_device(q.device):
         status = lib.minikv_paged_prefill(
             q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), cu_seqlens_q.data_ptr(),
             query_starts.data_ptr(), block_tables.data_ptr(), context_lens.data_ptr(), output.data_ptr(),
