@@ -58,6 +58,10 @@ def parse_args(argv=None):
     parser.add_argument("--context", type=int, default=None,
                         help="attended tokens per request (decode, default 2048) or cached tokens (qwen3, 4096)")
     parser.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU baseline sample budget")
+    parser.add_argument("--projections", choices=("fused", "cublas"), default="fused",
+                        help="qwen3: tcgen05 projections with the element-wise steps fused in for per-GPU batches "
+                             "up to Qwen3DecodeStep.FUSED_MAX_BATCH (default), or cuBLAS projections around the "
+                             "element-wise kernels")
     args = parser.parse_args(argv)
     if args.batch is None:
         args.batch = 32 if args.workload == "decode" else 256
@@ -538,7 +542,8 @@ def run_qwen3(args, world, rank, local):
     tables = qwen3_tables(batch, pages, device, QWEN3_SEED + 100 + rank)
     ids = torch.randint(0, cfg.vocab_size, (batch,), device=device, generator=gen)
     positions = torch.full((batch,), args.context, dtype=torch.int64, device=device)
-    step = Qwen3DecodeStep(cfg, weights, pool)
+    step = Qwen3DecodeStep(cfg, weights, pool, fused_projections=args.projections == "fused")
+    fused = step.fused_projections and batch <= step.FUSED_MAX_BATCH  # the path this batch takes
     graph = DecodeGraph(step, batch, pages)
     graph.load(ids, positions, tables)
     for _ in range(args.warmup):
@@ -635,9 +640,14 @@ def run_qwen3(args, world, rank, local):
                           "decode_share": cfg.num_hidden_layers * launch_ms / ms_per_step},
         "e2e": {"value": args.batch / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-        "gpu_launches": (5 * cfg.num_hidden_layers + 1) * args.steps,
-        "gpu_launches_note": "libminikv kernels only (RMSNorm x2, qk-norm+RoPE+append, paged decode, SiLU*up per "
-                             "layer, plus the first RMSNorm); the 4 projections per layer and the LM head are cuBLAS",
+        "gpu_launches": ((5 * cfg.num_hidden_layers + 2) if fused else (5 * cfg.num_hidden_layers + 1)) * args.steps,
+        "gpu_launches_note": ("libminikv kernels only: per layer the q|k|v, o, gate|up and down projections "
+                              "(tcgen05, element-wise steps fused) and the paged decode, plus the first and the "
+                              "final RMSNorm; the LM head is cuBLAS" if fused else
+                              "libminikv kernels only (RMSNorm x2, qk-norm+RoPE+append, paged decode, SiLU*up per "
+                              "layer, plus the first RMSNorm); the 4 projections per layer and the LM head are "
+                              "cuBLAS"),
+        "projections": "fused tcgen05" if fused else "cublas",
         "clocks": clocks.summary(),
     })
     if world == 1:

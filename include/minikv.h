@@ -243,6 +243,75 @@ int minikv_qk_rope_append(const void* qkv, int64_t qkv_stride, const void* q_wei
                           int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
                           int64_t block_size, int64_t table_width, double eps, int dtype, void* stream);
 
+/* ---------------------------------------------------- fused projections ---
+ * The dense projections of the batch decode step (FusedLinear, torch path
+ * kernels/linear.py:116-130, i.e. y = x @ W^T with W [out, in] as in
+ * nn.Linear) on the tcgen05 tensor cores, with the element-wise steps around
+ * them fused in.  No counterpart in the reference's C++ API: these replace
+ * the torch.mm + element-wise chains of native_qwen3.py:175-196 and
+ * :232-277.  FP16/BF16; in_features a multiple of 64; x rows x_stride
+ * elements apart (16-byte aligned).  The fp32 accumulation runs in the tensor
+ * core's order and the split over in-features is summed in a fixed order, so
+ * results are deterministic but not bit-equal to cuBLAS.
+ *
+ * Weights are passed packed (minikv_pack_linear, once at load time): the
+ * [out, in] weight as [out / 128][in / 64] blocks of 128 rows x 64 elements,
+ * each block contiguous and laid out as the tensor core reads it from shared
+ * memory (16-byte chunk c of row r stored at chunk c ^ (r % 8)).
+ *
+ * RMSNorm prologue (ss_in != NULL): x is first normalised row by row,
+ * T(T(x * rsqrt(ss / in_features + eps)) * norm_weight), where ss for token t
+ * is the sum over j of ss_in[j * tokens + t], j < in_features / 128: the
+ * partial sums of squares that minikv_linear_residual writes for its output.
+ * in_features must then be a multiple of 128.  Outputs must not overlap
+ * inputs. */
+
+/* packed <- weight [out_features, in_features] (row-major, out_features a
+ * multiple of 128) in the packed layout.  pair_offset > 0 packs a fused
+ * gate|up weight (out_features = 2 pair_offset rows, pair_offset a multiple
+ * of 64) for minikv_linear_silu_mul: block row-tile j then holds gate rows
+ * [64 j, 64 j + 64) followed by up rows [pair_offset + 64 j, ...).  packed has
+ * the size of weight and must not overlap it. */
+int minikv_pack_linear(const void* weight, void* packed, int64_t out_features, int64_t in_features,
+                       int64_t pair_offset, int dtype, void* stream);
+
+/* out[t, n] = T(sum_k xn[t, k] weight[n, k]), out [tokens, out_features]
+ * contiguous; out_features a multiple of 128. */
+int minikv_linear(const void* x, int64_t x_stride, const float* ss_in, const void* norm_weight, double eps,
+                  const void* packed_weight, void* out, int64_t tokens, int64_t in_features, int64_t out_features,
+                  int dtype, void* stream);
+
+/* out = T(T(x @ weight^T) + residual) (both [tokens, out_features]
+ * contiguous) and, when ss_out != NULL, ss_out[j * tokens + t] = sum of
+ * out[t, 128 j + i]^2 over i < 128 (fp32): the o projection or the down
+ * projection with the residual add of native_qwen3.py:270-277, handing the
+ * next RMSNorm its statistics. */
+int minikv_linear_residual(const void* x, int64_t x_stride, const void* packed_weight, const void* residual,
+                           void* out, float* ss_out, int64_t tokens, int64_t in_features, int64_t out_features,
+                           int dtype, void* stream);
+
+/* out[t, j] = T(T(silu(g)) * u) with g = T(xn @ gate^T)[t, j], u = T(xn @ up^T)[t, j],
+ * where the fused weight cat(gate, up) [2 intermediate, in_features]
+ * (enable_projection_fusion, native_qwen3.py:362-376) is packed with
+ * pair_offset = intermediate; out [tokens, intermediate] contiguous,
+ * intermediate a multiple of 64. */
+int minikv_linear_silu_mul(const void* x, int64_t x_stride, const float* ss_in, const void* norm_weight, double eps,
+                           const void* packed_gate_up, void* out, int64_t tokens, int64_t in_features,
+                           int64_t intermediate, int dtype, void* stream);
+
+/* The q|k|v projection (packed qkv weight [(q_heads + 2 kv_heads) * 128, in_features])
+ * followed by what minikv_qk_rope_append does with its output: q/k RMSNorm,
+ * rotary embedding (cos/sin [tokens, 64]), q to q_out [tokens, q_heads, 128],
+ * K (rotated) and V appended at positions[t] through block_tables.  The
+ * projection rows are never written to memory.  head_dim 128. */
+int minikv_linear_qk_rope_append(const void* x, int64_t x_stride, const float* ss_in, const void* norm_weight,
+                                 double eps, const void* packed_qkv, const void* q_weight, const void* k_weight,
+                                 const void* cos, const void* sin, void* q_out, void* key_cache, void* value_cache,
+                                 const int64_t* block_tables, const int64_t* positions, int64_t tokens,
+                                 int64_t in_features, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                 int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype,
+                                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

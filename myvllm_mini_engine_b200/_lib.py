@@ -44,6 +44,12 @@ SIGNATURES = {
     "minikv_rms_norm": (_int, [_p] * 5 + [_i64, _i64, ctypes.c_double, _int, _p]),
     "minikv_silu_mul": (_int, [_p, _p, _i64, _i64, _int, _p]),
     "minikv_qk_rope_append": (_int, [_p, _i64] + [_p] * 9 + [_i64] * 7 + [ctypes.c_double, _int, _p]),
+    "minikv_pack_linear": (_int, [_p, _p, _i64, _i64, _i64, _int, _p]),
+    "minikv_linear": (_int, [_p, _i64, _p, _p, ctypes.c_double, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "minikv_linear_residual": (_int, [_p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "minikv_linear_silu_mul": (_int, [_p, _i64, _p, _p, ctypes.c_double, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "minikv_linear_qk_rope_append": (_int, [_p, _i64, _p, _p, ctypes.c_double] + [_p] * 10 + [_i64] * 8
+                                     + [_int, _p]),
 }
 
 _LIB = None

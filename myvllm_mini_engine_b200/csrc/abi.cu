@@ -60,6 +60,7 @@ int sm_count() {
 #include "metadata.cu"
 #include "prefill.cu"
 #include "decode_step.cu"
+#include "proj.cu"
 
 using namespace minikv;
 
@@ -382,6 +383,130 @@ int minikv_qk_rope_append(const void* qkv, int64_t qkv_stride, const void* q_wei
     p.block_size = block_size; p.q_heads = (int)q_heads; p.kv_heads = (int)kv_heads; p.eps = (float)eps;
     cudaError_t err = launch_qk_rope_append(dtype, p, (int)head_dim, sm_count(), static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "minikv_qk_rope_append launch");
+    return MINIKV_OK;
+}
+
+// ------------------------------------------------------ fused projections
+int minikv_pack_linear(const void* weight, void* packed, int64_t out_features, int64_t in_features,
+                       int64_t pair_offset, int dtype, void* stream) {
+    MINIKV_REQUIRE(dtype == MINIKV_F16 || dtype == MINIKV_BF16, MINIKV_EUNSUPPORTED, "FP16/BF16 required");
+    MINIKV_REQUIRE(in_features > 0 && in_features % 64 == 0 && out_features > 0 && out_features % 128 == 0 &&
+                       out_features * in_features < (1ll << 40),
+                   MINIKV_EINVAL, "packing needs out_features % 128 == 0 and in_features % 64 == 0");
+    MINIKV_REQUIRE(pair_offset == 0 || (pair_offset % 64 == 0 && 2 * pair_offset == out_features), MINIKV_EINVAL,
+                   "a paired (gate|up) weight has 2 * pair_offset rows, pair_offset a multiple of 64");
+    MINIKV_REQUIRE(weight && packed && aligned16(weight) && aligned16(packed), MINIKV_EINVAL,
+                   "weights must be 16-byte aligned");
+    cudaError_t err = launch_pack_linear(dtype, weight, packed, out_features, in_features, pair_offset, sm_count(),
+                                         static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_pack_linear launch");
+    return MINIKV_OK;
+}
+
+int minikv_linear(const void* x, int64_t x_stride, const float* ss_in, const void* norm_weight, double eps,
+                  const void* packed_weight, void* out, int64_t tokens, int64_t in_features, int64_t out_features,
+                  int dtype, void* stream) {
+    ProjParams p;
+    int rc = proj_setup(x, x_stride, packed_weight, tokens, in_features, out_features, ss_in, norm_weight, dtype, &p);
+    if (rc != MINIKV_OK) return rc;
+    MINIKV_REQUIRE(out_features % 128 == 0, MINIKV_EINVAL, "out_features must be a multiple of 128");
+    MINIKV_REQUIRE(out && aligned16(out), MINIKV_EINVAL, "out must be 16-byte aligned");
+    if (tokens == 0) return MINIKV_OK;
+    p.out_features = (int)out_features;
+    p.eps = (float)eps;
+    p.out = out;
+    p.out_stride = out_features;
+    cudaError_t err = launch_proj<kEpiStore>(dtype, ss_in != nullptr, p, out_features / 128,
+                                             static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_linear launch");
+    return MINIKV_OK;
+}
+
+int minikv_linear_residual(const void* x, int64_t x_stride, const void* packed_weight, const void* residual,
+                           void* out, float* ss_out, int64_t tokens, int64_t in_features, int64_t out_features, int dtype,
+                           void* stream) {
+    ProjParams p;
+    int rc = proj_setup(x, x_stride, packed_weight, tokens, in_features, out_features, nullptr, nullptr, dtype, &p);
+    if (rc != MINIKV_OK) return rc;
+    MINIKV_REQUIRE(out_features % 128 == 0, MINIKV_EINVAL, "out_features must be a multiple of 128");
+    MINIKV_REQUIRE(residual && out && aligned16(residual) && aligned16(out), MINIKV_EINVAL,
+                   "residual and out must be 16-byte aligned");
+    if (tokens == 0) return MINIKV_OK;
+    p.out_features = (int)out_features;
+    p.out = out;
+    p.out_stride = out_features;
+    p.residual = residual;
+    p.residual_stride = out_features;
+    p.ss_out = ss_out;
+    cudaError_t err = launch_proj<kEpiResidual>(dtype, false, p, out_features / 128,
+                                                static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_linear_residual launch");
+    return MINIKV_OK;
+}
+
+int minikv_linear_silu_mul(const void* x, int64_t x_stride, const float* ss_in, const void* norm_weight, double eps,
+                           const void* packed_gate_up, void* out, int64_t tokens, int64_t in_features,
+                           int64_t intermediate, int dtype, void* stream) {
+    ProjParams p;
+    MINIKV_REQUIRE(intermediate > 0 && intermediate % 64 == 0 && intermediate < (1ll << 30), MINIKV_EINVAL,
+                   "intermediate size must be a positive multiple of 64");
+    int rc = proj_setup(x, x_stride, packed_gate_up, tokens, in_features, 2 * intermediate, ss_in, norm_weight,
+                        dtype, &p);
+    if (rc != MINIKV_OK) return rc;
+    MINIKV_REQUIRE(out && aligned16(out), MINIKV_EINVAL, "out must be 16-byte aligned");
+    if (tokens == 0) return MINIKV_OK;
+    p.out_features = (int)intermediate;
+    p.gate_offset = (int)intermediate;
+    p.eps = (float)eps;
+    p.out = out;
+    p.out_stride = intermediate;
+    cudaError_t err = launch_proj<kEpiSiluMul>(dtype, ss_in != nullptr, p, intermediate / 64,
+                                               static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_linear_silu_mul launch");
+    return MINIKV_OK;
+}
+
+int minikv_linear_qk_rope_append(const void* x, int64_t x_stride, const float* ss_in, const void* norm_weight,
+                                 double eps, const void* packed_qkv, const void* q_weight, const void* k_weight,
+                                 const void* cos, const void* sin, void* q_out, void* key_cache, void* value_cache,
+                                 const int64_t* block_tables, const int64_t* positions, int64_t tokens,
+                                 int64_t in_features, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                 int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype,
+                                 void* stream) {
+    MINIKV_REQUIRE(head_dim == 128, MINIKV_EUNSUPPORTED, "the fused q|k|v projection needs head_dim 128");
+    MINIKV_REQUIRE(q_heads > 0 && kv_heads > 0 && q_heads % kv_heads == 0 && q_heads + 2 * kv_heads < 65536 &&
+                       num_blocks > 0 && block_size > 0 && table_width > 0,
+                   MINIKV_EINVAL, "query heads must be divisible by KV heads");
+    const int64_t rows = (q_heads + 2 * kv_heads) * head_dim;
+    ProjParams p;
+    int rc = proj_setup(x, x_stride, packed_qkv, tokens, in_features, rows, ss_in, norm_weight, dtype, &p);
+    if (rc != MINIKV_OK) return rc;
+    MINIKV_REQUIRE(q_weight && k_weight && cos && sin && q_out && key_cache && value_cache && block_tables &&
+                       positions,
+                   MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(q_weight) && aligned16(k_weight) && aligned16(cos) && aligned16(sin) &&
+                       aligned16(q_out) && aligned16(key_cache) && aligned16(value_cache),
+                   MINIKV_EINVAL, "tensors must be 16-byte aligned");
+    if (tokens == 0) return MINIKV_OK;
+    p.out_features = (int)rows;
+    p.eps = (float)eps;
+    p.out = q_out;
+    p.q_weight = q_weight;
+    p.k_weight = k_weight;
+    p.cos = cos;
+    p.sin = sin;
+    p.key_cache = key_cache;
+    p.value_cache = value_cache;
+    p.tables = block_tables;
+    p.positions = positions;
+    p.width = table_width;
+    p.num_blocks = num_blocks;
+    p.block_size = block_size;
+    p.q_heads = (int)q_heads;
+    p.kv_heads = (int)kv_heads;
+    cudaError_t err = launch_proj<kEpiQkRope>(dtype, ss_in != nullptr, p, q_heads + 2 * kv_heads,
+                                              static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_linear_qk_rope_append launch");
     return MINIKV_OK;
 }
 

@@ -397,6 +397,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
     // page-table reads below overlap the previous kernel (the KV append of the
     // same step), and the wait comes just before the first KV copy / q read.
     if (!p.early_prologue) griddep_wait();
+    // The next chained kernel (a projection) may start on SMs that CTAs of this
+    // one leave and stream its weights; it waits for this grid before reading
+    // what the grid writes.
+    griddep_launch_dependents();
     tile_prefix(p.lens, B, cap, TT, prefix, lens_s, warp_sums);
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {

@@ -4,20 +4,35 @@ The caller of the paged-KV path in the reference engine is
 ``NativeQwen3.forward_decode_batch`` (``mini_engine/model/native_qwen3.py:423-456``):
 per layer it runs RMSNorm, the q|k|v projection, q/k RMSNorm + RoPE, the
 decode KV append, paged decode attention, the output projection and the MLP.
-This module runs the same step on B200 with the sm_100a kernels of libminikv
-for everything except the dense projections, which are plain cuBLAS GEMMs
-through ``torch.mm`` (the reference's ``FusedLinear`` torch path,
-``kernels/linear.py:116-130``):
+This module runs the same step on B200 with the sm_100a kernels of libminikv.
+By default (``fused_projections``, head_dim 128) a batch of at most
+``FUSED_MAX_BATCH`` requests runs every projection on the tcgen05 projection
+kernels (packed weights) with the element-wise steps fused into them:
+
+    per layer (5 launches):  q|k|v projection [RMSNorm prologue; q/k RMSNorm +
+                             RoPE + KV append epilogue] | paged decode |
+                             o projection [+ residual] | gate|up projection
+                             [RMSNorm prologue; SiLU * up] | down projection
+                             [+ residual]
+
+where each residual epilogue hands the next RMSNorm its per-row sums of
+squares, and each projection streams its weights while the previous kernel
+finishes (chained launches).  Larger batches, and ``fused_projections=False``,
+run the projections as plain cuBLAS GEMMs through ``torch.mm`` (the reference's
+``FusedLinear`` torch path, ``kernels/linear.py:116-130``) around the fused
+element-wise kernels:
 
     per layer (9 launches):  RMSNorm | mm(q|k|v) | qk-norm + RoPE + KV append |
                              paged decode | mm(o) | residual + RMSNorm |
                              mm(gate|up) | SiLU * up | mm(down)
 
-and the residual add of the MLP is fused into the next layer's RMSNorm.
-Rounding follows the eager reference (every intermediate in the model dtype),
-so the step's greedy tokens match the reference model's on the same weights
-and KV state.  The step never synchronises with the host, so it can be
-captured in a CUDA graph (:class:`DecodeGraph`).
+with the residual add of the MLP fused into the next layer's RMSNorm; that
+composition reproduces the reference's rounding bit for bit except inside
+the decode attention.  Either way rounding follows the eager reference
+(every intermediate in the model dtype), so the step's greedy tokens match
+the reference model's on the same weights and KV state.  The step never
+synchronises with the host, so it can be captured in a CUDA graph
+(:class:`DecodeGraph`).
 
 Weights use the fused layouts of ``enable_projection_fusion``
 (native_qwen3.py:362-376): ``qkv = cat(Wq, Wk, Wv)`` and ``gate_up = cat(Wg, Wu)``,
@@ -129,6 +144,24 @@ def _check(status, what):
     _lib.check(status, what)
 
 
+def pack_linear(weight: torch.Tensor, *, pair_offset: int = 0) -> torch.Tensor:
+    """A packed copy of an ``[out_features, in_features]`` weight for the fused projections.
+
+    The layout is the one ``minikv_pack_linear`` documents (``include/minikv.h``):
+    blocks of 128 rows x 64 in-features, each stored as the tensor core reads it
+    from shared memory.  ``pair_offset`` (the intermediate size) packs a fused
+    gate|up weight so that each block row holds matching gate and up rows.
+    """
+    if weight.ndim != 2 or not weight.is_contiguous() or not weight.is_cuda:
+        raise ValueError("pack_linear expects a contiguous 2D CUDA weight")
+    packed = torch.empty_like(weight)
+    with _lib.on_device(weight.device):
+        _check(_lib.load().minikv_pack_linear(weight.data_ptr(), packed.data_ptr(), weight.shape[0], weight.shape[1],
+                                              pair_offset, _lib.dtype_code(weight.dtype),
+                                              torch.cuda.current_stream(weight.device).cuda_stream), "pack_linear")
+    return packed
+
+
 class Qwen3DecodeStep:
     """One decode token per request through all layers, reading and appending the paged pool.
 
@@ -139,7 +172,11 @@ class Qwen3DecodeStep:
     ``positions[b]`` through ``block_tables[b]``.
     """
 
-    def __init__(self, config: Qwen3Config, weights: Qwen3Weights, pool: KVCachePool):
+    #: batches up to this size take the fused tcgen05 projections; larger ones cuBLAS
+    FUSED_MAX_BATCH = 32
+
+    def __init__(self, config: Qwen3Config, weights: Qwen3Weights, pool: KVCachePool, *,
+                 fused_projections: bool | None = None):
         shape = pool.shape
         if (shape.num_layers, shape.num_kv_heads, shape.head_dim) != (
                 config.num_hidden_layers, config.num_key_value_heads, config.head_dim):
@@ -153,6 +190,25 @@ class Qwen3DecodeStep:
         self.config, self.weights, self.pool = config, weights, pool
         self.code = _lib.dtype_code(weights.embed.dtype)
         self.lib = _lib.load()
+        fusable = self.fusable(config)
+        if fused_projections and not fusable:
+            raise ValueError("fused projections need head_dim 128, hidden and q-head sizes that are multiples "
+                             "of 128 and an intermediate size that is a multiple of 64")
+        self.fused_projections = fusable if fused_projections is None else bool(fused_projections)
+        self._packed = []
+        if self.fused_projections:
+            # the fused projections read packed weights (copies made once, here)
+            inter = config.intermediate_size
+            self._packed = [(pack_linear(layer.qkv), pack_linear(layer.o),
+                             pack_linear(layer.gate_up, pair_offset=inter), pack_linear(layer.down))
+                            for layer in weights.layers]
+
+    @staticmethod
+    def fusable(config: Qwen3Config) -> bool:
+        """Shapes the fused tcgen05 projections take (Qwen3 models use head_dim 128)."""
+        return (config.head_dim == 128 and config.hidden_size % 128 == 0
+                and (config.num_attention_heads * config.head_dim) % 128 == 0
+                and config.intermediate_size % 64 == 0)
 
     # ------------------------------------------------------------ fused ops
     def _rms(self, x, residual, weight, out, sum_out, stream):
@@ -183,6 +239,8 @@ class Qwen3DecodeStep:
         hq, hkv, dim = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         shape = pool.shape
         stream = torch.cuda.current_stream(device).cuda_stream
+        if self.fused_projections and batch <= self.FUSED_MAX_BATCH:
+            return self._forward_fused(input_ids, block_tables, positions, stream)
         x = F.embedding(input_ids, w.embed)
         inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim))
         angles = positions.to(dtype=torch.float32)[:, None] * inv_freq[None, :]
@@ -213,6 +271,54 @@ class Qwen3DecodeStep:
             following = w.layers[index + 1].input_norm if index + 1 < len(w.layers) else w.norm
             residual, h = torch.empty_like(x), torch.empty_like(x)
             self._rms(down, summed, following, h, residual, stream)
+        return torch.mm(h, w.lm_head.t())
+
+    def _forward_fused(self, input_ids, block_tables, positions, stream):
+        """The step on the fused tcgen05 projections (five launches per layer)."""
+        cfg, pool, w, lib, code = self.config, self.pool, self.weights, self.lib, self.code
+        batch, device = input_ids.shape[0], input_ids.device
+        hq, hkv, dim = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        hidden, inter, eps = cfg.hidden_size, cfg.intermediate_size, cfg.rms_norm_eps
+        shape = pool.shape
+        x = F.embedding(input_ids, w.embed)
+        inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim))
+        angles = positions.to(dtype=torch.float32)[:, None] * inv_freq[None, :]
+        cos, sin = angles.cos().to(x.dtype), angles.sin().to(x.dtype)
+        lengths = positions + 1
+        h = torch.empty_like(x)
+        self._rms(x, None, w.layers[0].input_norm, h, None, stream)
+        residual, sums = x, None  # sums: per-row partial sums of squares of `residual`
+        for index, layer in enumerate(w.layers):
+            qkv_w, o_w, gate_up_w, down_w = self._packed[index]
+            q = torch.empty((batch, hq, dim), dtype=x.dtype, device=device)
+            if sums is None:  # first layer: RMSNorm already applied
+                source, ss_in, norm = h, None, None
+            else:
+                source, ss_in, norm = residual, sums.data_ptr(), layer.input_norm.data_ptr()
+            _check(lib.minikv_linear_qk_rope_append(
+                source.data_ptr(), source.stride(0), ss_in, norm, eps, qkv_w.data_ptr(),
+                layer.q_norm.data_ptr(), layer.k_norm.data_ptr(), cos.data_ptr(), sin.data_ptr(), q.data_ptr(),
+                pool.key[index].data_ptr(), pool.value[index].data_ptr(), block_tables.data_ptr(),
+                positions.data_ptr(), batch, hidden, hq, hkv, dim, shape.num_blocks, shape.block_size,
+                block_tables.shape[1], code, stream), "linear_qk_rope_append")
+            attention = paged_attention(q, pool.key[index], pool.value[index], block_tables, lengths,
+                                        shape.block_size, validate=False, chained=True)
+            summed = torch.empty_like(x)
+            summed_sums = torch.empty((hidden // 128, batch), dtype=torch.float32, device=device)
+            _check(lib.minikv_linear_residual(
+                attention.data_ptr(), hq * dim, o_w.data_ptr(), residual.data_ptr(), summed.data_ptr(),
+                summed_sums.data_ptr(), batch, hq * dim, hidden, code, stream), "linear_residual(o)")
+            act = torch.empty((batch, inter), dtype=x.dtype, device=device)
+            _check(lib.minikv_linear_silu_mul(
+                summed.data_ptr(), hidden, summed_sums.data_ptr(), layer.post_norm.data_ptr(), eps,
+                gate_up_w.data_ptr(), act.data_ptr(), batch, hidden, inter, code, stream), "linear_silu_mul")
+            residual = torch.empty_like(x)
+            sums = torch.empty((hidden // 128, batch), dtype=torch.float32, device=device)
+            _check(lib.minikv_linear_residual(
+                act.data_ptr(), inter, down_w.data_ptr(), summed.data_ptr(), residual.data_ptr(),
+                sums.data_ptr(), batch, inter, hidden, code, stream), "linear_residual(down)")
+        h = torch.empty_like(x)
+        self._rms(residual, None, w.norm, h, None, stream)
         return torch.mm(h, w.lm_head.t())
 
     def greedy(self, input_ids, block_tables, positions):

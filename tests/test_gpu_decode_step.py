@@ -5,7 +5,8 @@ with every backend "torch", pinned bit-exact to the reference on the CPU
 (test_oracle_golden.py) -- run on the same GPU with the same weights and KV
 state, which is how the reference validates its own model paths.  The decode
 step under test runs the sm_100a kernels (fused q/k-norm + RoPE + KV append,
-paged decode, RMSNorm, SiLU*up) and cuBLAS projections.
+paged decode, RMSNorm, SiLU*up) and either the fused tcgen05 projections (the
+default) or cuBLAS projections (``fused_projections=False``).
 
 Bars:
   * each fused kernel against the reference's op chain on identical inputs:
@@ -13,12 +14,13 @@ Bars:
     fp32 reductions run in their own order, and a one-ulp change of the
     rounded normalised value can grow to two through the weight product),
     the appended V rows bit-exact;
-  * the whole 28-layer step with the reference's decode attention in place of
-    the paged decode kernel is bit-identical to the reference model: every
-    other kernel of the step (and the cuBLAS projections) reproduces the
+  * the whole 28-layer step on cuBLAS projections with the reference's decode
+    attention in place of the paged decode kernel is bit-identical to the
+    reference model: every other kernel of the step reproduces the
     reference's rounding exactly;
-  * with the paged decode kernel, whose fp32 sums run in another order than
-    torch's, the step differs from the reference only by that rounding,
+  * with the paged decode kernel (and the fused projections), whose fp32 sums
+    run in another order than torch's, the step differs from the reference
+    only by that rounding,
     amplified through 28 random-weight layers (about one bf16 ulp of a logit
     after one layer, ~0.13 after 28): logits within atol=0.25, rtol=0.01
     (twice the largest difference seen; the reference's own model check
@@ -155,13 +157,17 @@ def appended(pool_tensor, tables, positions, block_size):
     return pages, positions % block_size, pool_tensor[:, pages, positions % block_size]
 
 
-def test_decode_step_matches_reference_model_over_greedy_steps(cuda_device):
-    # 48 requests: block boundaries, short and long contexts, and enough requests
-    # that some are decided beyond the near-tie margin at every step
+@pytest.mark.parametrize("fused", [True, False], ids=["fused-projections", "cublas-projections"])
+def test_decode_step_matches_reference_model_over_greedy_steps(cuda_device, fused):
+    # block boundaries, short and long contexts, and enough requests that some are decided beyond the
+    # near-tie margin at every step: 48 on the cuBLAS projections, the fused path's largest batch on it
     contexts = (1, 17, 255, 256, 700, 1031, 1500, 2047) + tuple(int(x) for x in cases.rng(34).integers(1, 2048, 40))
+    if fused:
+        contexts = contexts[:Qwen3DecodeStep.FUSED_MAX_BATCH]
     cfg, weights, pool, tables, ids, positions = model_case(contexts, seed=31)
     ref_key, ref_value = pool.key.clone(), pool.value.clone()
-    step = Qwen3DecodeStep(cfg, weights, pool)
+    step = Qwen3DecodeStep(cfg, weights, pool, fused_projections=fused)
+    assert step.fused_projections == fused
     ours_ids, ref_ids = ids, ids.clone()
     bs = pool.shape.block_size
     for i in range(3):
@@ -201,7 +207,8 @@ def test_decode_step_is_bit_exact_with_the_reference_attention(cuda_device, monk
     ref_key, ref_value = pool.key.clone(), pool.value.clone()
     monkeypatch.setattr(engine_qwen3, "paged_attention",
                         lambda q, kc, vc, t, lens, bs, **_: paged_decode.paged_attention(q, kc, vc, t, lens, bs))
-    logits = Qwen3DecodeStep(cfg, weights, pool).forward_decode_batch(ids, tables, positions)
+    step = Qwen3DecodeStep(cfg, weights, pool, fused_projections=False)
+    logits = step.forward_decode_batch(ids, tables, positions)
     expected = ref.decode_step(cfg, weights, ids, ref_key, ref_value, tables, positions)
     assert torch.equal(logits, expected)
     assert torch.equal(pool.key, ref_key) and torch.equal(pool.value, ref_value)
