@@ -95,7 +95,17 @@ def on_device(device):
     return torch.cuda.device(device)
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(device) -> int:
+    """Handle of ``device``'s current CUDA stream (``torch.cuda.current_stream(device).cuda_stream``).
+
+    Read without building a Stream object, which costs microseconds of host
+    time on every kernel call.
+    """
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(device.index if device.index is not None else torch.cuda.current_device())
     return torch.cuda.current_stream(device).cuda_stream
 
 

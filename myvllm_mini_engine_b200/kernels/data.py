@@ -27,6 +27,13 @@ def _require(condition, message):
         raise RuntimeError(message)
 
 
+def _as_long(tensor, device):
+    """``tensor`` as a contiguous int64 tensor on ``device`` (itself when it already is one)."""
+    if tensor.dtype == torch.long and tensor.device == device and tensor.is_contiguous():
+        return tensor
+    return tensor.to(device=device, dtype=torch.long).contiguous()
+
+
 def _row_stride(tensor):
     """Token stride (elements) of a [tokens, Hkv, D] tensor whose rows are contiguous, else None."""
     if tensor.dim() != 3:
@@ -92,8 +99,8 @@ def write_kv_cache_batch(key_cache, value_cache, block_tables, token_offsets, ke
     if (block_tables.ndim != 2 or token_offsets.ndim != 1 or block_tables.shape[0] != key.shape[0]
             or token_offsets.shape[0] != key.shape[0]):
         raise ValueError("batch block table or offset shape mismatch")
-    tables = block_tables.to(device=key_cache.device, dtype=torch.long).contiguous()
-    offsets = token_offsets.to(device=key_cache.device, dtype=torch.long).contiguous()
+    tables = _as_long(block_tables, key_cache.device)
+    offsets = _as_long(token_offsets, key_cache.device)
     for t in (key_cache, value_cache, tables, offsets, key, value):  # bindings.cpp:131-142
         _require(t.is_cuda and t.is_contiguous(), "batch KV write inputs must be contiguous CUDA tensors")
         _require(t.device == key_cache.device, "batch KV write inputs must share a device")

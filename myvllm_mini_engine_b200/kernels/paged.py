@@ -89,7 +89,7 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
             _lib.check(_lib.EINVAL, "paged_attention")
         _WS_BYTES[key] = need
     with _lib.on_device(query.device):
-        stream = torch.cuda.current_stream(query.device)
+        stream = _lib.stream_of(query.device)
         if workspace is None:
             workspace = _workspace(query.device, stream, need)
         elif workspace.numel() < need:
@@ -99,7 +99,7 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
         status = entry(
             query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
             context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
-            batch, heads, kv_heads, dim, num_blocks, block_size, width, code, stream.cuda_stream)
+            batch, heads, kv_heads, dim, num_blocks, block_size, width, code, stream)
     _lib.check(status, "paged_attention")
     return out
 
@@ -110,14 +110,14 @@ _RETIRED: list = []
 
 
 def _workspace(device, stream, need):
-    """Zero-filled scratch reused by every decode call on ``stream``.
+    """Zero-filled scratch reused by every decode call on ``stream`` (a raw stream handle).
 
     The kernel keeps per-request ticket counters in it and leaves them at zero,
     so it is zeroed once, when allocated.  Calls on one stream never overlap;
     each stream gets its own buffer.  Buffers are never freed while the process
     runs, because a captured CUDA graph may still refer to one.
     """
-    key = (device.index, stream.cuda_stream)
+    key = (device.index, stream)
     buf = _WORKSPACES.get(key)
     if buf is None or buf.numel() < need:
         if buf is not None:
