@@ -130,3 +130,62 @@ def test_tensor_core_route_selection(cuda_device, dtype, dim, heads, kv_heads, e
     assert used_tc == expect_tc, names
     if not expect_tc:
         assert any("paged_decode_kernel" in n for n in names), names
+
+
+def sub_batch(args, r):
+    """Request r of a packed prefill batch as a batch of its own (same caches)."""
+    q, kc, vc, cu, starts, tables, lens = args
+    lo, hi = int(cu[r]), int(cu[r + 1])
+    return (q[lo:hi].contiguous(), kc, vc, torch.tensor([0, hi - lo], dtype=torch.int64, device=q.device),
+            starts[r:r + 1].contiguous(), tables[r:r + 1].contiguous(), lens[r:r + 1].contiguous())
+
+
+@pytest.mark.parametrize("dtype,dim", [(torch.bfloat16, 128), (torch.float16, 64)])
+def test_prefill_output_of_a_request_does_not_depend_on_the_batch(cuda_device, dtype, dim):
+    # Tensor-core route: every (query tile, kv head) item of a request is computed by
+    # one CTA over the request's own keys in a fixed order (query tiles never mix
+    # requests), so the rows of a request alone and inside a batch are bit-identical.
+    # (The CUDA-core route runs the split-KV decode over the batch's tokens, whose
+    # split points depend on the whole batch: equal within tolerance, not in bits.)
+    c = cases.ragged_prefill_case(dtype, head_dim=dim)
+    args = [c[k].cuda() for k in NAMES]
+    batched = paged_prefill_attention(*args, c["block_size"])
+    cu = c["cu_seqlens_q"]
+    for r in range(len(cu) - 1):
+        alone = paged_prefill_attention(*sub_batch(args, r), c["block_size"])
+        assert torch.equal(alone, batched[int(cu[r]):int(cu[r + 1])]), f"request {r}"
+
+
+@pytest.mark.parametrize("dtype,dim", [(torch.bfloat16, 128), (torch.float32, 64)])
+def test_prefill_replays_in_a_cuda_graph(cuda_device, dtype, dim):
+    # The ragged prefill is captured once with static metadata and query buffers;
+    # replays with new contents of the same shapes match eager calls on them.
+    c = cases.ragged_prefill_case(dtype, head_dim=dim)
+    static = [c[k].cuda() for k in NAMES]
+    bs = c["block_size"]
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        paged_prefill_attention(*static, bs, validate=False)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        out = paged_prefill_attention(*static, bs, validate=False)
+    q, _, _, cu, starts, tables, lens = static
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    for step in range(2):
+        # new queries and a shifted split of the same token count between the requests
+        q.copy_(torch.randn(q.shape, device="cuda", generator=gen).to(dtype))
+        counts = (cu[1:] - cu[:-1]).tolist()
+        if step == 1:
+            counts[0], counts[2] = counts[0] - 20, counts[2] + 20
+        new_cu = torch.tensor([0] + list(np.cumsum(counts)), dtype=torch.int64, device="cuda")
+        new_starts = starts.clone()
+        new_starts[2] = max(0, int(starts[2]) - 20)  # request 2 keeps within its pages
+        cu.copy_(new_cu)
+        starts.copy_(new_starts)
+        lens.copy_(starts + (cu[1:] - cu[:-1]))
+        graph.replay()
+        expected = paged_prefill_attention(*static, bs)
+        torch.cuda.synchronize()
+        assert torch.equal(out, expected), f"replay {step}"
