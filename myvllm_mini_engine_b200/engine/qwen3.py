@@ -334,33 +334,114 @@ class DecodeGraph:
     does (``mini_engine/engine/cuda_graph.py:196-275``); the output is
     ``next_ids``.  The decode workspace of the capture stream is created by a
     warm-up step on that stream before capture.
+
+    Two ways to fill the inputs:
+
+    * :meth:`load` copies ready ``[batch]`` / ``[batch, table_width]`` tensors
+      (host or device) into the static buffers;
+    * with ``padding_pages`` (one private scratch page per batch row), the
+      graph is a bucket that serves up to ``batch`` requests: :meth:`stage`
+      packs one step's tokens, positions and per-request page lists into one
+      pinned host buffer and makes one host-to-device copy, and the graph's
+      first kernel (``minikv_build_decode_tables``) builds the fixed-shape
+      inputs on the device -- the staging of cuda_graph.py:149-181 -- with the
+      rows past the active requests decoding position 0 on their scratch page
+      (cuda_graph.py:66-86).
     """
 
-    def __init__(self, step: Qwen3DecodeStep, batch: int, table_width: int, *, warmup_tables=None):
+    def __init__(self, step: Qwen3DecodeStep, batch: int, table_width: int, *, warmup_tables=None,
+                 padding_pages=None):
         device = step.weights.embed.device
         self.step = step
         self.device = device
+        self.batch, self.table_width = batch, table_width
         self.input_ids = torch.zeros(batch, dtype=torch.long, device=device)
         self.positions = torch.zeros(batch, dtype=torch.long, device=device)
         self.block_tables = torch.full((batch, table_width), -1, dtype=torch.long, device=device)
         if warmup_tables is not None:
             self.block_tables.copy_(warmup_tables)
+        self.staged = padding_pages is not None
+        if self.staged:
+            self._init_staging(padding_pages)
         self.stream = torch.cuda.Stream(device)
         self.graph = torch.cuda.CUDAGraph()
         self.stream.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(self.stream):
             # warm-up: allocates the stream's decode workspace and cuBLAS state outside the graph
+            if self.staged:
+                self._build_tables()
             step.greedy(self.input_ids, self.block_tables, self.positions)
         self.stream.synchronize()
         with torch.cuda.graph(self.graph, stream=self.stream):
+            if self.staged:
+                self._build_tables()
             self.next_ids = step.greedy(self.input_ids, self.block_tables, self.positions)
         torch.cuda.current_stream(device).wait_stream(self.stream)
 
+    def _init_staging(self, padding_pages):
+        pages = [int(p) for p in padding_pages][:self.batch]
+        num_blocks = self.step.pool.shape.num_blocks
+        if len(pages) < self.batch:
+            raise ValueError("padding_pages must cover one private page per batch slot")
+        if len(set(pages)) != self.batch or any(p < 0 or p >= num_blocks for p in pages):
+            raise ValueError("padding slots require distinct scratch pages inside the cache")
+        batch, width = self.batch, self.table_width
+        self._padding = torch.tensor(pages, dtype=torch.long, device=self.device)
+        # [active | tokens[batch] | positions[batch] | cu_blocks[batch + 1] | block ids ...]
+        self._offsets = (0, 1, 1 + batch, 1 + 2 * batch, 2 + 3 * batch)
+        size = 2 + 3 * batch + batch * width
+        self._host = torch.zeros(size, dtype=torch.long, pin_memory=True)
+        self._dev = torch.zeros(size, dtype=torch.long, device=self.device)
+        self._host_np = self._host.numpy()
+        self._copied = torch.cuda.Event()
+        self._copy_pending = False
+
+    def _build_tables(self):
+        o, d = self._offsets, self._dev
+        stream = _lib.stream_of(self.device)
+        _check(self.step.lib.minikv_build_decode_tables(
+            d[o[0]:].data_ptr(), d[o[1]:].data_ptr(), d[o[2]:].data_ptr(), d[o[3]:].data_ptr(), d[o[4]:].data_ptr(),
+            self._padding.data_ptr(), self.batch, self.table_width, self.input_ids.data_ptr(),
+            self.positions.data_ptr(), self.block_tables.data_ptr(), stream), "build_decode_tables")
+
     def load(self, input_ids, positions, block_tables):
         """Copy one step's metadata into the static buffers (host or device tensors)."""
+        if self.staged:
+            raise ValueError("a staged decode graph takes its inputs through stage()")
         self.input_ids.copy_(input_ids, non_blocking=True)
         self.positions.copy_(positions, non_blocking=True)
         self.block_tables.copy_(block_tables, non_blocking=True)
+
+    def stage(self, tokens, positions, block_lists):
+        """Stage one step of up to ``batch`` requests with one host-to-device copy.
+
+        ``tokens`` and ``positions`` hold one int per request; ``block_lists``
+        one sequence of physical page ids per request (1 .. table_width pages).
+        """
+        import numpy as np
+
+        active = len(tokens)
+        if active > self.batch or len(positions) != active or len(block_lists) != active:
+            raise ValueError("staged requests exceed the graph's batch or have mismatched lengths")
+        counts = [len(row) for row in block_lists]
+        if any(n < 1 or n > self.table_width for n in counts):
+            raise ValueError("each request needs 1 .. table_width pages")
+        if self._copy_pending:  # the previous copy may still read the pinned buffer
+            self._copied.synchronize()
+        o, h = self._offsets, self._host_np
+        h[0] = active
+        h[o[1]:o[1] + active] = tokens
+        h[o[2]:o[2] + active] = positions
+        cu = np.zeros(active + 1, dtype=np.int64)
+        np.cumsum(counts, out=cu[1:])
+        h[o[3]:o[3] + active + 1] = cu
+        total = int(cu[-1])
+        if total:
+            h[o[4]:o[4] + total] = np.concatenate([np.asarray(row, dtype=np.int64) for row in block_lists])
+        used = o[4] + total
+        self._dev[:used].copy_(self._host[:used], non_blocking=True)
+        self._copied.record(torch.cuda.current_stream(self.device))
+        self._copy_pending = True
 
     def replay(self):
         self.graph.replay()

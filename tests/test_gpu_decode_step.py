@@ -231,3 +231,38 @@ def test_decode_graph_replays_the_eager_step(cuda_device):
         assert torch.equal(pool.key, after[0]) and torch.equal(pool.value, after[1])
         ids, positions = replayed, positions + 1
     assert _lib.device_status() == 0
+
+
+def test_staged_decode_graph_serves_fewer_requests_than_its_batch(cuda_device):
+    """A bucket graph with on-device staging (cuda_graph.py:149-181): one packed copy per step,
+    the tables built by the graph's first kernel, rows past the active requests decoding
+    position 0 on their scratch pages; every replay equals the eager step on the same padded
+    inputs (built here by the oracle of the staging)."""
+    from oracle import metadata
+
+    contexts = (5, 63, 64, 900)
+    cfg, weights, pool, tables, ids, positions = model_case(contexts, seed=43, layers=4)
+    used = set(tables[tables >= 0].tolist())
+    batch, width = 6, tables.shape[1]
+    scratch = [b for b in range(pool.shape.num_blocks) if b not in used][:batch]
+    step = Qwen3DecodeStep(cfg, weights, pool)
+    graph = DecodeGraph(step, batch, width, padding_pages=scratch)
+    for active in (4, 2, 4):
+        rows = [tables[r][tables[r] >= 0].tolist() for r in range(active)]
+        tok, pos = ids[:active].tolist(), positions[:active].tolist()
+        before = (pool.key.clone(), pool.value.clone())
+        graph.stage(tok, pos, rows)
+        replayed = graph.replay().clone()
+        after = (pool.key.clone(), pool.value.clone())
+        pool.key.copy_(before[0])
+        pool.value.copy_(before[1])
+        meta = metadata.decode_bucket_metadata(tok, pos, rows, batch_size=batch, max_blocks=width,
+                                               padding_pages=scratch)
+        eager = step.greedy(torch.tensor(meta["input_ids"], device="cuda"),
+                            torch.tensor(meta["block_tables"], device="cuda"),
+                            torch.tensor(meta["positions"], device="cuda"))
+        assert torch.equal(replayed, eager), f"{active} active requests"
+        assert torch.equal(pool.key, after[0]) and torch.equal(pool.value, after[1])
+    with pytest.raises(ValueError):
+        graph.load(ids, positions, tables)
+    assert _lib.device_status() == 0
