@@ -284,17 +284,22 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                 for (int kb = 0; kb < L::KB; ++kb)
                     tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, w.h * G, (int)(w.q0 + w.t_lo), q_full);
             }
-            auto box_page = [&](int j) -> int64_t {  // physical page of this lane's box of tile j, or -1
+            // Page-table entry of this lane's box of tile j (-1: no box).  The entry of
+            // tile j + 2 is loaded while tile j is issued and checked an iteration
+            // later, so the table load never stalls the issue of a tile.
+            auto raw_page = [&](int j) -> int64_t {
                 const int64_t k0 = (int64_t)j * kPfKeys + box * R;
                 if (box >= groups || j >= w.n_tiles || k0 >= w.limit) return -1;
-                const int64_t page = w.table[k0 / p.block_size];
+                return w.table[k0 / p.block_size];
+            };
+            auto checked = [&](int64_t page) -> int64_t {
                 return (page >= 0 && page < p.num_blocks) ? page : -1;
             };
-            int64_t page = box_page(0);
+            int64_t page = checked(raw_page(0));
+            int64_t next_raw = raw_page(1);
             for (int j = 0; j < w.n_tiles; ++j, ++gt) {
                 const int slot = gt & 1;
                 const int64_t key0 = (int64_t)j * kPfKeys;
-                const int64_t next_page = box_page(j + 1);  // in flight while this tile is issued
                 const bool valid = page >= 0;
                 uint32_t words[4] = {0u, 0u, 0u, 0u};
                 if (!is_v) {
@@ -330,7 +335,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                     for (int kb = 0; kb < L::KB; ++kb)
                         tma_load_3d(dst + kb * L::BLOCK_BYTES, map, kb * 64, w.h, z, &full[slot]);
                 }
-                page = next_page;
+                page = checked(next_raw);
+                next_raw = raw_page(j + 2);
             }
             ++active;
         }
