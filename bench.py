@@ -62,6 +62,9 @@ def parse_args(argv=None):
                         help="qwen3: tcgen05 projections with the element-wise steps fused in for per-GPU batches "
                              "up to Qwen3DecodeStep.FUSED_MAX_BATCH (default), or cuBLAS projections around the "
                              "element-wise kernels")
+    parser.add_argument("--kv-dtype", choices=("bf16", "fp8"), default="bf16",
+                        help="decode: the KV pool format; fp8 = E4M3 pool with per-pool scales (quantising "
+                             "slot scatter + fp8 paged attention), device-timed only")
     args = parser.parse_args(argv)
     if args.batch is None:
         args.batch = 32 if args.workload == "decode" else 256
@@ -462,6 +465,112 @@ def run_ours(args, world, rank, local):
     if world == 1:
         line["cpu_baseline"] = cpu_baseline(args.context, args.cpu_seconds)
     return line
+
+
+def run_fp8(args, world, rank, local):
+    """Decode step over an FP8 (E4M3) pool: quantising scatter of the new token + fp8 paged attention.
+
+    The bf16 pools of the decode workload are quantised once (untimed) with the
+    same scatter; the step is captured as a graph.  Bytes per step count the KV
+    pool at one byte per element, q and the output at two.
+    """
+    from myvllm_mini_engine_b200 import _lib
+    from myvllm_mini_engine_b200.kernels import paged_attention_fp8, write_kv_cache_slots_fp8
+
+    device = torch.device("cuda", local)
+    x = make_inputs(args.batch, args.context, device, seed=1234 + rank)
+    k_scale, v_scale = 4.5 / 448, 4.5 / 448
+    pool_rows = x["key_cache"].shape[0] * BS
+    kq = torch.empty(x["key_cache"].shape, dtype=torch.uint8, device=device)
+    vq = torch.empty_like(kq)
+    write_kv_cache_slots_fp8(kq, vq, torch.arange(pool_rows, device=device), x["key_cache"].view(-1, HKV, D),
+                             x["value_cache"].view(-1, HKV, D), k_scale, v_scale, validate=False)
+    del x["key_cache"], x["value_cache"]
+    last = x["context_lens"] - 1
+    slots = (x["block_tables"].gather(1, (last // BS).view(-1, 1)).view(-1) * BS + last % BS).contiguous()
+    lengths = [args.context] * args.batch
+    step_bytes = kv_bytes(lengths, 1) + 2 * args.batch * HQ * D * 2 + 8 * sum(math.ceil(n / BS) for n in lengths)
+    stream = torch.cuda.current_stream(device)
+
+    def attend():
+        return paged_attention_fp8(x["query"], kq, vq, x["block_tables"], x["context_lens"], BS, k_scale, v_scale,
+                                   validate=False)
+
+    def step():
+        write_kv_cache_slots_fp8(kq, vq, slots, x["key"], x["value"], k_scale, v_scale, validate=False)
+        return attend()
+
+    capture_stream = torch.cuda.Stream(device)
+    capture_stream.wait_stream(stream)
+    with torch.cuda.stream(capture_stream):
+        for _ in range(3):
+            step()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=capture_stream):
+        step()
+    ev_a = torch.cuda.Event(enable_timing=True, external=True)
+    ev_b = torch.cuda.Event(enable_timing=True, external=True)
+    probe = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(probe, stream=capture_stream):
+        write_kv_cache_slots_fp8(kq, vq, slots, x["key"], x["value"], k_scale, v_scale, validate=False)
+        ev_a.record()
+        attend()
+        ev_b.record()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(device)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kernel_ms = []
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        end.record(stream)
+        barrier()
+        for _ in range(min(args.steps, 50)):
+            probe.replay()
+            ev_b.synchronize()
+            kernel_ms.append(ev_a.elapsed_time(ev_b))
+    elapsed_ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_per_step = elapsed_ms / args.steps
+    kernel_avg_ms = statistics.mean(kernel_ms)
+    peak, peak_kind = measured_peaks()
+    achieved = step_bytes / (kernel_avg_ms * 1e-3) / 1e9
+    status = _lib.device_status(device)
+    if status:
+        raise RuntimeError(f"device status bits set during the benchmark: {status}")
+    del graph, probe
+    if rank != 0:
+        return None
+    return {
+        "metric": "fp8 paged-decode KV-read GB/s (E4M3 pool)", "value": world * step_bytes / (ms_per_step * 1e-3) / 1e9,
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 KV, bf16 q/out",
+        "data": "synthetic",
+        "config": {"workload": f"decode step (quantising KV scatter + fp8 paged attention) of {args.batch} "
+                               f"requests x {args.context} tokens per GPU, Hq16/Hkv8/D128, block 16",
+                   "global_batch": args.batch * world, "seq_len": args.context,
+                   "parallelism": f"request-sharded x{world} (independent KV pools)",
+                   "l2": f"inputs {2 * kq.numel() / 1e6:.0f} MB per GPU > 126 MB L2"},
+        "decode_tok_s": world * args.batch / (ms_per_step * 1e-3),
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_source": peak_kind, "traffic": None,
+                     "kernel": "fp8 paged decode, timed alone between events", "bytes_per_launch": step_bytes,
+                     "launch_ms": kernel_avg_ms},
+        "e2e": None, "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
+    }
 
 
 # ------------------------------------------------- config 5: Qwen3 decode step
@@ -904,7 +1013,12 @@ def main(argv=None):
             line = run_prefill_reference(args, world, rank) if args.impl == "reference" else \
                 run_prefill(args, world, rank, local)
         else:
-            line = run_reference(args, world, rank) if args.impl == "reference" else run_ours(args, world, rank, local)
+            if args.impl == "reference":
+                line = run_reference(args, world, rank)
+            elif args.kv_dtype == "fp8":
+                line = run_fp8(args, world, rank, local)
+            else:
+                line = run_ours(args, world, rank, local)
         if line is not None and rank == 0:
             print(json.dumps(line), flush=True)
     finally:

@@ -124,6 +124,39 @@ int minikv_kv_scatter_slots(void* key_cache, void* value_cache, const int64_t* s
                             int64_t key_token_stride, int64_t value_token_stride,
                             int dtype, void* stream);
 
+/* ------------------------------------------------------------ FP8 KV pool ---
+ * No counterpart in the reference, which lists an FP8 KV pool as future work
+ * (VALIDATION_AND_BENCHMARKS.md:375).  The pool has the 16-bit pool's shape,
+ * [num_blocks, block_size, kv_heads, head_dim], one OCP E4M3 byte per element
+ * (largest finite 448, no infinities), with one fp32 scale for keys and one
+ * for values: stored = e4m3(x * (1/scale)), the product rounded to fp32, then
+ * to nearest-even E4M3, saturated to +-448 (NaN -> 0x7F); read as
+ * stored * scale.
+ *
+ * Quantising slot scatter: as minikv_kv_scatter_slots (slots outside the
+ * capacity are skipped), from fp32/fp16/bf16 rows (`dtype`) into the byte
+ * pools.  kv_heads*head_dim must be a multiple of 16. */
+int minikv_kv_scatter_slots_fp8(void* key_cache, void* value_cache, const int64_t* slot_mapping,
+                                const void* key, const void* value, int64_t tokens,
+                                int64_t num_blocks, int64_t block_size, int64_t kv_heads, int64_t head_dim,
+                                int64_t key_token_stride, int64_t value_token_stride,
+                                float k_scale, float v_scale, int dtype, void* stream);
+
+/* Decode attention over an FP8 pool: minikv_paged_decode's contract and
+ * guards, with an fp16/bf16 query and output (`dtype`) and K/V read as
+ * code * scale.  The products run on fp16 tensor cores: Q is rounded to fp16
+ * (saturated at +-65504).  head_dim in {32, 64, 96, 128, 192, 256}.  The
+ * workspace (zero-filled before its first use, left zero by every call) has
+ * its own size query. */
+int64_t minikv_paged_decode_fp8_workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                                int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                                int64_t table_width, int dtype);
+int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void* value_cache,
+                            const int64_t* block_tables, const int64_t* context_lens, void* out,
+                            void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
+                            int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                            int64_t table_width, float k_scale, float v_scale, int dtype, void* stream);
+
 /* Decode append: request r writes its token at logical position
  * token_offsets[r] through block_tables[r]; rows whose page index or physical
  * page is out of range are skipped.  Replaces write_kv_cache_batch_cuda

@@ -57,6 +57,7 @@ int sm_count() {
 
 #include "kv_write.cu"
 #include "decode.cu"
+#include "decode_fp8.cu"
 #include "metadata.cu"
 #include "prefill.cu"
 #include "decode_step.cu"
@@ -178,6 +179,92 @@ int minikv_kv_scatter_slots(void* key_cache, void* value_cache, const int64_t* s
                                         SlotRows{slot_mapping, num_blocks * block_size},
                                         static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return cuda_fail(err, "minikv_kv_scatter_slots launch");
+    return MINIKV_OK;
+}
+
+// ----------------------------------------------------------- FP8 KV pool
+static bool valid_scale(float s) { return std::isfinite(s) && s > 0.f; }
+
+static int check_fp8_decode(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
+                            int64_t block_size, int64_t table_width, int dtype) {
+    MINIKV_REQUIRE(dtype == MINIKV_F16 || dtype == MINIKV_BF16, MINIKV_EINVAL,
+                   "an fp8 KV pool needs an FP16/BF16 query");
+    MINIKV_REQUIRE(fp8_head_dim(head_dim), MINIKV_EINVAL, "fp8 KV pool: supported head_dim: 32,64,96,128,192,256");
+    return check_decode_shapes(batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype);
+}
+
+int64_t minikv_paged_decode_fp8_workspace_bytes(int64_t batch, int64_t q_heads, int64_t kv_heads,
+                                                int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                                int64_t table_width, int dtype) {
+    if (check_fp8_decode(batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype)) return -1;
+    DecodePlan plan;
+    if (!make_decode_plan(batch, q_heads, kv_heads, head_dim, block_size, table_width, dtype, sm_count(), &plan, true))
+        return -1;
+    return plan.ws_bytes;
+}
+
+int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void* value_cache,
+                            const int64_t* block_tables, const int64_t* context_lens, void* out,
+                            void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
+                            int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                            int64_t table_width, float k_scale, float v_scale, int dtype, void* stream) {
+    int rc = check_fp8_decode(batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype);
+    if (rc) return rc;
+    MINIKV_REQUIRE(valid_scale(k_scale) && valid_scale(v_scale), MINIKV_EINVAL,
+                   "fp8 KV scales must be finite and positive");
+    MINIKV_REQUIRE(query && key_cache && value_cache && block_tables && context_lens && out, MINIKV_EINVAL,
+                   "null pointer argument");
+    MINIKV_REQUIRE(aligned16(query) && aligned16(key_cache) && aligned16(value_cache) && aligned16(out),
+                   MINIKV_EINVAL, "query, caches and output must be 16-byte aligned");
+    DecodePlan plan;
+    if (!make_decode_plan(batch, q_heads, kv_heads, head_dim, block_size, table_width, dtype, sm_count(), &plan, true))
+        return fail(MINIKV_EUNSUPPORTED, "decode shape does not fit shared memory (batch too large?)");
+    MINIKV_REQUIRE(workspace != nullptr && workspace_bytes >= plan.ws_bytes && aligned16(workspace),
+                   MINIKV_EINVAL, "decode workspace too small or misaligned");
+    DecodeParams p = decode_params(query, key_cache, value_cache, block_tables, context_lens, nullptr, out,
+                                   static_cast<unsigned char*>(workspace), batch, q_heads, kv_heads, head_dim,
+                                   num_blocks, block_size, table_width, plan);
+    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim) * (double)k_scale);
+    p.out_scale = v_scale;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const cudaError_t err = dtype == MINIKV_F16 ? launch_decode_fp8_dim<__half>((int)head_dim, p, plan, s)
+                                                : launch_decode_fp8_dim<__nv_bfloat16>((int)head_dim, p, plan, s);
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_decode_fp8 launch");
+    return MINIKV_OK;
+}
+
+int minikv_kv_scatter_slots_fp8(void* key_cache, void* value_cache, const int64_t* slot_mapping, const void* key,
+                                const void* value, int64_t tokens, int64_t num_blocks, int64_t block_size,
+                                int64_t kv_heads, int64_t head_dim, int64_t key_token_stride,
+                                int64_t value_token_stride, float k_scale, float v_scale, int dtype, void* stream) {
+    MINIKV_REQUIRE(tokens >= 0, MINIKV_EINVAL, "packed KV slots must be int64 [tokens]");
+    MINIKV_REQUIRE(num_blocks > 0 && block_size > 0, MINIKV_EINVAL, "packed KV cache must be nonempty");
+    MINIKV_REQUIRE(valid_dtype(dtype), MINIKV_EINVAL, "packed KV requires FP32/FP16/BF16");
+    MINIKV_REQUIRE(valid_scale(k_scale) && valid_scale(v_scale), MINIKV_EINVAL,
+                   "fp8 KV scales must be finite and positive");
+    MINIKV_REQUIRE(kv_heads > 0 && head_dim > 0, MINIKV_EINVAL, "K/V head shape mismatch");
+    const int64_t row_elems = kv_heads * head_dim;
+    MINIKV_REQUIRE(row_elems % 16 == 0, MINIKV_EINVAL, "fp8 KV row (kv_heads*head_dim) must be a multiple of 16");
+    MINIKV_REQUIRE(key_token_stride >= row_elems && value_token_stride >= row_elems, MINIKV_EINVAL,
+                   "K/V token stride smaller than a row");
+    if (tokens == 0) return MINIKV_OK;
+    MINIKV_REQUIRE(key_cache && value_cache && key && value && slot_mapping, MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(key_cache) && aligned16(value_cache), MINIKV_EINVAL, "KV caches must be 16-byte aligned");
+    const float k_inv = 1.0f / k_scale, v_inv = 1.0f / v_scale;
+    const int64_t capacity = num_blocks * block_size;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err;
+    if (dtype == MINIKV_F32)
+        err = launch_quantize_slots<float>(key_cache, value_cache, key, value, slot_mapping, tokens, capacity,
+                                           row_elems, key_token_stride, value_token_stride, k_inv, v_inv, s);
+    else if (dtype == MINIKV_F16)
+        err = launch_quantize_slots<__half>(key_cache, value_cache, key, value, slot_mapping, tokens, capacity,
+                                            row_elems, key_token_stride, value_token_stride, k_inv, v_inv, s);
+    else
+        err = launch_quantize_slots<__nv_bfloat16>(key_cache, value_cache, key, value, slot_mapping, tokens,
+                                                   capacity, row_elems, key_token_stride, value_token_stride, k_inv,
+                                                   v_inv, s);
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_kv_scatter_slots_fp8 launch");
     return MINIKV_OK;
 }
 

@@ -67,7 +67,8 @@ struct DecodeParams {
     int stages;
     int row_stride;       // shared-memory stride of one token row (padded)
     int early_prologue;   // 1: lens/tables predate the previous kernel; read them before griddep_wait
-    float scale_log2;     // log2(e) / sqrt(D)
+    float scale_log2;     // log2(e) / sqrt(D) (times the key scale for an fp8 pool)
+    float out_scale;      // fp8 pool: the value scale, applied to the output (unused otherwise)
 };
 
 // CTA c of G owns tiles [c*total/G, (c+1)*total/G); cta_of_tile(t) inverts it.
@@ -227,6 +228,7 @@ template <typename T, int D>
 struct CoreConsumer {
     using S = CoreShape<T, D>;
     static constexpr int kSubTokens = S::SC;
+    static constexpr int kKvBytes = (int)sizeof(T);  // bytes per cached element
     float qf[kCoreHeads][S::VPL][S::E];
     float acc[kCoreHeads][S::VPL][S::E];
     float m[kCoreHeads], l[kCoreHeads];
@@ -442,7 +444,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
         chunk = warp % cph;
         active = warp < nh * cph;
     }
-    constexpr int esize = (int)sizeof(T);
+    constexpr int esize = Consumer::kKvBytes;  // bytes per cached element
     const int copy_row = nh * D * esize;              // bytes per token and K|V
     const int cache_row = p.kv_heads * D * esize;     // global row stride
 
@@ -601,9 +603,11 @@ static int64_t align256(int64_t x) { return (x + 255) / 256 * 256; }
 
 // Everything here depends on shapes and the device only (graph-static).
 static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t block_size,
-                             int64_t table_width, int dtype, int sm_count, DecodePlan* plan) {
-    const int es = esize_of(dtype);
-    const bool mma = dtype != 0;
+                             int64_t table_width, int dtype, int sm_count, DecodePlan* plan,
+                             bool kv_fp8 = false) {
+    // kv_fp8: one-byte (e4m3) pool read by the fp8 tensor-core consumer (decode_fp8.cu)
+    const int es = kv_fp8 ? 1 : esize_of(dtype);
+    const bool mma = kv_fp8 || dtype != 0;
     const int sc = mma ? 16 : kTokensPerGroup * (32 / lanes_per_token((int)D, es));
     const int heads_per_item = mma ? kMmaHeads : kCoreHeads;
     const int64_t group = Hq / Hkv;
@@ -626,7 +630,7 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
     const int stage = 2 * tt * stride;
     const int fixed = kWindowTiles * tt * 4 + (int)(2 * B + 1) * 4 + 128;
     const int max_smem = 232448 - 1024;  // opt-in limit per block, minus static shared memory
-    int stages = std::min(4, (196608 + 8192) / stage);
+    int stages = std::min(kv_fp8 ? 6 : 4, (196608 + 8192) / stage);
     while (stages > 1 && stages * (stage + 24) + fixed > max_smem) --stages;
     if (stages < 1 || stages * (stage + 24) + fixed > max_smem) return false;
     const int smem = stages * (stage + 24) + fixed;

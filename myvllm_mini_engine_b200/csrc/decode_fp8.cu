@@ -1,0 +1,304 @@
+// FP8 (e4m3) KV pool: the quantising slot scatter and the tensor-core
+// consumer of the split-KV decode kernel for one-byte K/V rows.
+//
+// Format.  The pool has the 16-bit pool's shape, [num_blocks, block_size,
+// kv_heads, head_dim], one OCP E4M3 byte per element, with one fp32 scale for
+// keys and one for values: stored = e4m3_rn_satfinite(x * (1 / scale)), read
+// back as stored * scale.  It halves the bytes a decode step streams.  The
+// reference has no FP8 pool (it is listed there as future work); the write
+// follows its slot-scatter contract (mini_engine/kernels/csrc/data.cu:196-206:
+// a slot outside the capacity writes nothing).
+//
+// Decode.  The producer warp and the ticketed merge of decode.cu are reused
+// unchanged (rows are simply one byte per element).  The consumer converts
+// K and V to fp16 in registers (two e4m3 bytes -> one f16x2 per cvt, exact:
+// every e4m3 value is an fp16 normal or zero) and runs the same transposed
+// mma.sync scheme as decode_mma.cu in fp16:
+//   S^T = K Q^T    with Q rounded to fp16 (saturated at +-65504) once per segment;
+//   O^T += V^T P^T with P split into fp16 hi + lo terms.
+// The key scale is folded into the softmax scale and the value scale into the
+// final normalisation.  A dot product does not depend on the order of its
+// terms, so the head dims inside each 16-dim k-step are permuted to make a
+// lane's K bytes one 32-bit word (dims 16kk + 4q4 .. +3), and Q is permuted
+// the same way.  For V^T (the A operand, dims as rows), a lane loads one word
+// (4 dims) from each of its 4 tokens and assembles the token pairs with byte
+// permutes; each 32-dim group of O^T is two m-tiles whose rows are dims
+// 32u + 4g + {0, 1} and {2, 3}.  With the row stride = 16 mod 64 bytes, both
+// load patterns are free of bank conflicts.
+#include <cuda_fp8.h>
+
+#include "common.cuh"
+
+namespace minikv {
+
+// Two e4m3 values (low byte first) as an f16x2 (low half first).
+__device__ __forceinline__ uint32_t e4m3x2_to_h2(uint32_t pair) {
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(pair & 0xffffu), __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+}
+
+__device__ __forceinline__ uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+// fp16 pair of two floats, saturated to the finite fp16 range.
+__device__ __forceinline__ uint32_t h2_sat(float a, float b) {
+    a = fminf(fmaxf(a, -65504.f), 65504.f);
+    b = fminf(fmaxf(b, -65504.f), 65504.f);
+    return Elem<__half>::pack(a, b);
+}
+
+template <typename T, int D>
+struct Fp8MmaConsumer {
+    static_assert(D % 32 == 0, "the fp8 pool needs head_dim % 32 == 0");
+    static constexpr int KSTEPS = D / 16;  // k-steps of S^T = K Q^T
+    static constexpr int GROUPS = D / 32;  // 32-dim groups of O^T (two m-tiles each)
+    static constexpr int kKvBytes = 1;     // bytes per cached element
+    using Mma = MmaType<__half>;
+
+    uint32_t qb[KSTEPS][2];  // Q^T (fp16): head g, dims 16kk + 4q4 + {0,1} and + {2,3}
+    float o[2 * GROUPS][4];  // O^T: m-tile 2u + i, row g -> dim 32u + 4g + 2i, row g + 8 -> + 1
+    float m[2], l[2];
+    int g, q4;
+
+    __device__ void setup(int lane) {
+        g = lane >> 2;
+        q4 = lane & 3;
+    }
+
+    __device__ void begin(const T* qrows, int item_heads) {
+        const bool valid = g < item_heads;
+#pragma unroll
+        for (int kk = 0; kk < KSTEPS; ++kk) {
+            float f[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) f[i] = valid ? Elem<T>::to_float(qrows[g * D + 16 * kk + 4 * q4 + i]) : 0.f;
+            qb[kk][0] = h2_sat(f[0], f[1]);
+            qb[kk][1] = h2_sat(f[2], f[3]);
+        }
+#pragma unroll
+        for (int mt = 0; mt < 2 * GROUPS; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[mt][e] = 0.f;
+        m[0] = m[1] = -INFINITY;
+        l[0] = l[1] = 0.f;
+    }
+
+    __device__ void tile(const unsigned char* kptr, const unsigned char* vptr, int stride, int TT, int n,
+                         uint64_t mask, float scale_log2) {
+        for (int sub = 0; sub < TT; sub += 16) {
+            // ---- S^T = K Q^T: lane (g, q4) reads dims 16kk + 4q4 .. +3 of tokens g and g + 8
+            float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+            const unsigned char* k0 = kptr + (sub + g) * stride + 4 * q4;
+            const unsigned char* k1 = k0 + 8 * stride;
+#pragma unroll
+            for (int kk = 0; kk < KSTEPS; ++kk) {
+                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(k0 + 16 * kk);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(k1 + 16 * kk);
+                uint32_t a[4];
+                a[0] = e4m3x2_to_h2(w0);
+                a[1] = e4m3x2_to_h2(w1);
+                a[2] = e4m3x2_to_h2(w0 >> 16);
+                a[3] = e4m3x2_to_h2(w1 >> 16);
+                Mma::mma((kk & 1) ? s2 : s, a, qb[kk][0], qb[kk][1]);
+            }
+            // ---- mask and scale (as decode_mma.cu; the key scale is in scale_log2)
+            const int j0 = sub + g, j1 = j0 + 8;
+            const bool ok0 = j0 < n && ((mask >> j0) & 1ull), ok1 = j1 < n && ((mask >> j1) & 1ull);
+            s[0] = ok0 ? (s[0] + s2[0]) * scale_log2 : -INFINITY;
+            s[1] = ok0 ? (s[1] + s2[1]) * scale_log2 : -INFINITY;
+            s[2] = ok1 ? (s[2] + s2[2]) * scale_log2 : -INFINITY;
+            s[3] = ok1 ? (s[3] + s2[3]) * scale_log2 : -INFINITY;
+            float alpha[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float mx = fmaxf(s[h], s[h + 2]);
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                const float mn = fmaxf(m[h], mx);
+                alpha[h] = (mn == -INFINITY) ? 1.f : exp2f(m[h] - mn);
+                m[h] = mn;
+            }
+            float pv[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) pv[e] = (m[e & 1] == -INFINITY) ? 0.f : exp2f(s[e] - m[e & 1]);
+            l[0] = l[0] * alpha[0] + pv[0] + pv[2];
+            l[1] = l[1] * alpha[1] + pv[1] + pv[3];
+            if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+                for (int mt = 0; mt < 2 * GROUPS; ++mt) {
+                    o[mt][0] *= alpha[0];
+                    o[mt][1] *= alpha[1];
+                    o[mt][2] *= alpha[0];
+                    o[mt][3] *= alpha[1];
+                }
+            }
+            // ---- P = P_hi + P_lo in fp16, moved into the B layout (as decode_mma.cu)
+            const uint32_t h01 = Elem<__half>::pack(pv[0], pv[1]);
+            const uint32_t h23 = Elem<__half>::pack(pv[2], pv[3]);
+            float rest[4];
+            {
+                float back[4];
+                Elem<__half>::unpack(h01, back);
+                Elem<__half>::unpack(h23, back + 2);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) rest[e] = pv[e] - back[e];
+            }
+            const uint32_t l01 = Elem<__half>::pack(rest[0], rest[1]);
+            const uint32_t l23 = Elem<__half>::pack(rest[2], rest[3]);
+            const int src0 = (2 * q4) * 4 + (g >> 1), src1 = src0 + 4;
+            const bool odd = g & 1;
+            const uint32_t b0 = pick_halves(__shfl_sync(0xffffffffu, h01, src0), __shfl_sync(0xffffffffu, h01, src1), odd);
+            const uint32_t b1 = pick_halves(__shfl_sync(0xffffffffu, h23, src0), __shfl_sync(0xffffffffu, h23, src1), odd);
+            const uint32_t c0 = pick_halves(__shfl_sync(0xffffffffu, l01, src0), __shfl_sync(0xffffffffu, l01, src1), odd);
+            const uint32_t c1 = pick_halves(__shfl_sync(0xffffffffu, l23, src0), __shfl_sync(0xffffffffu, l23, src1), odd);
+            // ---- O^T += V^T P^T: lane (g, q4) reads dims 32u + 4g .. +3 of tokens 2q4, 2q4+1, 2q4+8, 2q4+9
+            const unsigned char* v0 = vptr + (sub + 2 * q4) * stride + 4 * g;
+#pragma unroll
+            for (int u = 0; u < GROUPS; ++u) {
+                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(v0 + 32 * u);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(v0 + stride + 32 * u);
+                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(v0 + 8 * stride + 32 * u);
+                const uint32_t w3 = *reinterpret_cast<const uint32_t*>(v0 + 9 * stride + 32 * u);
+                // byte i of a word is dim 32u + 4g + i; pair the two tokens of each k slot
+                const uint32_t x01 = byte_perm(w0, w1, 0x5140u), x23 = byte_perm(w2, w3, 0x5140u);  // dims +0, +1
+                const uint32_t y01 = byte_perm(w0, w1, 0x7362u), y23 = byte_perm(w2, w3, 0x7362u);  // dims +2, +3
+                uint32_t a[4];
+                a[0] = e4m3x2_to_h2(x01);
+                a[1] = e4m3x2_to_h2(x01 >> 16);
+                a[2] = e4m3x2_to_h2(x23);
+                a[3] = e4m3x2_to_h2(x23 >> 16);
+                Mma::mma(o[2 * u], a, c0, c1);
+                Mma::mma(o[2 * u], a, b0, b1);
+                a[0] = e4m3x2_to_h2(y01);
+                a[1] = e4m3x2_to_h2(y01 >> 16);
+                a[2] = e4m3x2_to_h2(y23);
+                a[3] = e4m3x2_to_h2(y23 >> 16);
+                Mma::mma(o[2 * u + 1], a, c0, c1);
+                Mma::mma(o[2 * u + 1], a, b0, b1);
+            }
+        }
+    }
+
+    __device__ void finish(const DecodeParams& p, int b, int qh0, int item_heads, bool final_row, int64_t record) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float L = l[h];
+            L += __shfl_xor_sync(0xffffffffu, L, 4);
+            L += __shfl_xor_sync(0xffffffffu, L, 8);
+            L += __shfl_xor_sync(0xffffffffu, L, 16);
+            const int head = 2 * q4 + h;
+            if (head >= item_heads) continue;
+            const int qh = qh0 + head;
+            const float inv = (L > 0.f) ? p.out_scale / L : 0.f;  // the value scale folded in
+            if (final_row) {
+                T* orow = static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh) * D;
+#pragma unroll
+                for (int u = 0; u < GROUPS; ++u) {
+                    T* dst = orow + 32 * u + 4 * g;
+                    dst[0] = Elem<T>::from_float(o[2 * u][h] * inv);
+                    dst[1] = Elem<T>::from_float(o[2 * u][h + 2] * inv);
+                    dst[2] = Elem<T>::from_float(o[2 * u + 1][h] * inv);
+                    dst[3] = Elem<T>::from_float(o[2 * u + 1][h + 2] * inv);
+                }
+            } else {
+                float* prow = p.partial + (record * p.q_heads + qh) * D;
+#pragma unroll
+                for (int u = 0; u < GROUPS; ++u)
+                    *reinterpret_cast<float4*>(prow + 32 * u + 4 * g) =
+                        make_float4(o[2 * u][h] * inv, o[2 * u][h + 2] * inv, o[2 * u + 1][h] * inv,
+                                    o[2 * u + 1][h + 2] * inv);
+                if (g == 0) p.lse[record * p.q_heads + qh] = (L > 0.f) ? m[h] + log2f(L) : -INFINITY;
+            }
+        }
+    }
+};
+
+// ------------------------------------------------------ quantising scatter
+// One warp per token: K and V rows of `row_elems` elements, 16 per lane step,
+// each rounded as e4m3(x * inv_scale) (fp32 product, then nearest-even E4M3,
+// saturating) into 16 bytes of the pool row.
+template <typename T>
+__global__ void __launch_bounds__(256) quantize_slots_kernel(
+    unsigned char* __restrict__ kc, unsigned char* __restrict__ vc, const T* __restrict__ k,
+    const T* __restrict__ v, const int64_t* __restrict__ slots, int64_t tokens, int64_t capacity,
+    int64_t row_elems, int64_t k_stride, int64_t v_stride, float k_inv, float v_inv) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens; t += warps) {
+        const int64_t slot = slots[t];
+        if (slot < 0 || slot >= capacity) continue;  // data.cu:196-206
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+            const T* src = which ? v + t * v_stride : k + t * k_stride;
+            unsigned char* dst = (which ? vc : kc) + slot * row_elems;
+            const float inv = which ? v_inv : k_inv;
+            for (int64_t c = (int64_t)lane * 16; c < row_elems; c += 32 * 16) {
+                uint32_t word[4];
+#pragma unroll
+                for (int w = 0; w < 4; ++w) {
+                    uint32_t packed = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float x = __fmul_rn(Elem<T>::to_float(src[c + 4 * w + i]), inv);
+                        packed |= (uint32_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3) << (8 * i);
+                    }
+                    word[w] = packed;
+                }
+                *reinterpret_cast<uint4*>(dst + c) = make_uint4(word[0], word[1], word[2], word[3]);
+            }
+        }
+    }
+}
+
+template <typename T>
+static cudaError_t launch_quantize_slots(void* kc, void* vc, const void* k, const void* v, const int64_t* slots,
+                                         int64_t tokens, int64_t capacity, int64_t row_elems, int64_t k_stride,
+                                         int64_t v_stride, float k_inv, float v_inv, cudaStream_t stream) {
+    if (tokens <= 0) return cudaSuccess;
+    int64_t blocks = (tokens + 7) / 8;
+    const int64_t cap = (int64_t)sm_count_for_current_device() * 8;
+    if (blocks > cap) blocks = cap;
+    return launch_chained(quantize_slots_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, stream,
+                          static_cast<unsigned char*>(kc), static_cast<unsigned char*>(vc),
+                          static_cast<const T*>(k), static_cast<const T*>(v), slots, tokens, capacity, row_elems,
+                          k_stride, v_stride, k_inv, v_inv);
+}
+
+// ------------------------------------------------------------ decode host side
+template <typename T, int D>
+static cudaError_t launch_decode_fp8_typed(const DecodeParams& p, const DecodePlan& plan, cudaStream_t stream) {
+    auto kernel = paged_decode_kernel<T, D, Fp8MmaConsumer<T, D>>;
+    static int configured[64] = {0};  // opt-in shared-memory size set per device
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return err;
+    if (device < 0 || device >= 64 || configured[device] < plan.smem_bytes) {
+        err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.smem_bytes);
+        if (err != cudaSuccess) return err;
+        if (device >= 0 && device < 64) configured[device] = plan.smem_bytes;
+    }
+    return launch_chained(kernel, dim3(plan.grid, plan.head_groups), dim3(kDecodeThreads), plan.smem_bytes, stream, p);
+}
+
+template <typename T>
+static cudaError_t launch_decode_fp8_dim(int D, const DecodeParams& p, const DecodePlan& plan, cudaStream_t stream) {
+    switch (D) {
+        case 32: return launch_decode_fp8_typed<T, 32>(p, plan, stream);
+        case 64: return launch_decode_fp8_typed<T, 64>(p, plan, stream);
+        case 96: return launch_decode_fp8_typed<T, 96>(p, plan, stream);
+        case 128: return launch_decode_fp8_typed<T, 128>(p, plan, stream);
+        case 192: return launch_decode_fp8_typed<T, 192>(p, plan, stream);
+        case 256: return launch_decode_fp8_typed<T, 256>(p, plan, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+static bool fp8_head_dim(int64_t d) { return d == 32 || d == 64 || d == 96 || d == 128 || d == 192 || d == 256; }
+
+}  // namespace minikv

@@ -62,6 +62,7 @@ struct MmaConsumer {
     static constexpr int KSTEPS = D / 16;  // k-steps of S^T = K Q^T
     static constexpr int MTILES = D / 16;  // m-tiles (16 dims) of O^T
     static constexpr int esize = 2;
+    static constexpr int kKvBytes = 2;  // bytes per cached element
     using Mma = MmaType<T>;
 
     uint32_t qb[KSTEPS][2];  // Q^T as the B operand: head g, dims 16kk + 2*q4 (+1) and +8

@@ -1,0 +1,152 @@
+"""FP8 (E4M3) KV pool: quantising slot scatter and decode attention.
+
+The reference has no FP8 KV pool (``VALIDATION_AND_BENCHMARKS.md:375`` lists it
+as future work), so these two operators extend its API in its own style: the
+scatter mirrors ``write_kv_cache_slots`` (``mini_engine/kernels/data.py:84-130``)
+and the decode mirrors ``paged_attention`` (``kernels/paged.py:8-22``), each
+with a key and a value scale.
+
+A pool is a uint8 (or ``torch.float8_e4m3fn``) tensor of the 16-bit pool's
+shape ``[num_blocks, block_size, kv_heads, head_dim]``; element ``x`` is stored
+as ``e4m3(x * (1/scale))`` (fp32 product, nearest-even, saturated to +-448) and
+read as ``code * scale``.  A decode step streams half the bytes of a bf16 pool.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+from .data import _backend, _rows
+from .paged import _require, _workspace, check_backend
+
+FP8_HEAD_DIMS = (32, 64, 96, 128, 192, 256)
+_POOL_DTYPES = (torch.uint8, getattr(torch, "float8_e4m3fn", torch.uint8))
+
+
+def _scale(value, name):
+    value = float(value)
+    if not (value > 0.0 and value < float("inf")):
+        raise ValueError(f"{name} must be finite and positive")
+    return value
+
+
+def write_kv_cache_slots_fp8(key_cache, value_cache, slot_mapping, key, value, k_scale, v_scale, *,
+                             backend="cuda", validate=True):
+    """Quantise packed K/V rows into FP8 pools at ``slot_mapping`` (slots outside the capacity are skipped).
+
+    ``key``/``value`` ``[tokens, kv_heads, head_dim]`` fp32/fp16/bf16 (token-strided
+    views are read in place); pools ``[num_blocks, block_size, kv_heads, head_dim]``
+    uint8 or float8_e4m3fn.  ``validate`` adds the host-synchronising slot checks
+    of ``write_kv_cache_slots`` (data.py:109-119).
+    """
+    _backend(backend)
+    k_scale, v_scale = _scale(k_scale, "k_scale"), _scale(v_scale, "v_scale")
+    if (key_cache.ndim != 4 or value_cache.shape != key_cache.shape
+            or any(size <= 0 for size in key_cache.shape)
+            or not key_cache.is_contiguous() or not value_cache.is_contiguous()):
+        raise ValueError("KV caches must be contiguous [pages, block_size, kv_heads, head_dim]")
+    if key_cache.dtype not in _POOL_DTYPES or value_cache.dtype != key_cache.dtype:
+        raise ValueError("an fp8 KV pool must be uint8 or float8_e4m3fn")
+    if key.ndim != 3 or key.shape != value.shape or key.shape[1:] != key_cache.shape[2:]:
+        raise ValueError("packed key/value must be [tokens, kv_heads, head_dim] matching the cache")
+    if key.dtype not in _lib.DTYPE_CODES or value.dtype != key.dtype:
+        raise ValueError("packed KV requires FP32/FP16/BF16")
+    if (slot_mapping.ndim != 1 or slot_mapping.numel() != key.shape[0]
+            or slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous()):
+        raise ValueError("slot_mapping must be contiguous int64 [tokens]")
+    for tensor in (value_cache, slot_mapping, key, value):
+        if tensor.device != key_cache.device:
+            raise ValueError("packed KV tensors and slots must share the cache device")
+    if (key_cache.shape[2] * key_cache.shape[3]) % 16:
+        raise ValueError("fp8 KV row (kv_heads*head_dim) must be a multiple of 16")
+    if validate:
+        slots = slot_mapping.tolist()
+        capacity = key_cache.shape[0] * key_cache.shape[1]
+        if any(slot < 0 or slot >= capacity for slot in slots):
+            raise ValueError("KV slot is outside cache capacity")
+        if len(set(slots)) != len(slots):
+            raise ValueError("duplicate KV slots would race during scatter")
+    if key_cache.device.type != "cuda":
+        raise ValueError("CUDA packed KV writes require CUDA tensors")
+    tokens = key.shape[0]
+    if tokens == 0:
+        return
+    # the kernel reads element by element: only the token stride must be uniform
+    key, key_stride = _rows(key)
+    value, value_stride = _rows(value)
+    lib = _lib.load()
+    with _lib.on_device(key_cache.device):
+        status = lib.minikv_kv_scatter_slots_fp8(
+            key_cache.data_ptr(), value_cache.data_ptr(), slot_mapping.data_ptr(), key.data_ptr(),
+            value.data_ptr(), tokens, key_cache.shape[0], key_cache.shape[1], key_cache.shape[2],
+            key_cache.shape[3], key_stride, value_stride, k_scale, v_scale, _lib.dtype_code(key.dtype),
+            _lib.stream_of(key_cache.device))
+    _lib.check(status, "write_kv_cache_slots_fp8")
+
+
+_WS_BYTES: dict = {}
+
+
+def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_lens, block_size, k_scale, v_scale,
+                        *, backend="cuda", validate=True, workspace=None):
+    """Decode attention over FP8 pools: ``softmax(q . (K*k_scale)^T / sqrt(D)) (V*v_scale)``.
+
+    Arguments and guards as :func:`paged_attention` (``query [B, Hq, D]`` fp16 or
+    bf16, ``block_tables [B, W]`` and ``context_lens [B]`` int64); the pools are
+    uint8 / float8_e4m3fn.  Q.K and P.V run on fp16 tensor cores, so Q is
+    rounded to fp16 (saturated at +-65504).  Returns ``[B, Hq, D]`` in the query dtype.
+    """
+    check_backend(backend)
+    k_scale, v_scale = _scale(k_scale, "k_scale"), _scale(v_scale, "v_scale")
+    _require(query.is_cuda, "query must be CUDA")
+    for t in (key_cache, value_cache, block_tables, context_lens):
+        _require(t.device == query.device, "all inputs must be on the same CUDA device")
+        _require(t.is_contiguous(), "inputs must be contiguous")
+    _require(query.is_contiguous(), "query must be contiguous")
+    _require(query.dim() == 3 and key_cache.dim() == 4 and value_cache.shape == key_cache.shape,
+             "invalid query/cache shapes")
+    _require(query.dtype in (torch.float16, torch.bfloat16), "an fp8 KV pool needs an FP16/BF16 query")
+    _require(key_cache.dtype in _POOL_DTYPES and value_cache.dtype == key_cache.dtype,
+             "an fp8 KV pool must be uint8 or float8_e4m3fn")
+    _require(block_tables.dtype == torch.int64 and context_lens.dtype == torch.int64, "metadata must be int64")
+    batch, heads, dim = query.shape
+    num_blocks, bs, kv_heads, _ = key_cache.shape
+    _require(batch > 0 and heads > 0 and num_blocks > 0 and kv_heads > 0, "empty batch/heads/cache")
+    _require(block_size > 0 and bs == block_size, "block size mismatch")
+    _require(dim == key_cache.shape[3] and heads % kv_heads == 0, "head dimension or GQA mismatch")
+    _require(dim in FP8_HEAD_DIMS, "fp8 KV pool: supported head_dim: 32,64,96,128,192,256")
+    _require(block_tables.dim() == 2 and block_tables.shape[0] == batch and block_tables.shape[1] > 0,
+             "invalid block table")
+    _require(context_lens.dim() == 1 and context_lens.shape[0] == batch, "invalid context lengths")
+    width = block_tables.shape[1]
+    _require(width * block_size <= 1048576, "maximum table capacity is 1M tokens")
+    if validate:
+        _require(not bool(((context_lens <= 0) | (context_lens > width * block_size)).any()),
+                 "invalid context length")
+        positions = torch.arange(width, device=query.device, dtype=torch.int64) * block_size
+        active = positions.unsqueeze(0) < context_lens.unsqueeze(1)
+        _require(not bool((((block_tables < 0) | (block_tables >= num_blocks)) & active).any()),
+                 "physical block id out of range")
+    lib = _lib.load()
+    code = _lib.dtype_code(query.dtype)
+    key = (batch, heads, kv_heads, dim, num_blocks, block_size, width, code)
+    need = _WS_BYTES.get(key)
+    if need is None:
+        need = lib.minikv_paged_decode_fp8_workspace_bytes(*key)
+        if need < 0:
+            _lib.check(_lib.EINVAL, "paged_attention_fp8")
+        _WS_BYTES[key] = need
+    with _lib.on_device(query.device):
+        stream = _lib.stream_of(query.device)
+        if workspace is None:
+            workspace = _workspace(query.device, stream, need)
+        elif workspace.numel() < need:
+            raise RuntimeError("decode workspace too small")
+        out = torch.empty_like(query)
+        status = lib.minikv_paged_decode_fp8(
+            query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
+            context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
+            batch, heads, kv_heads, dim, num_blocks, block_size, width, k_scale, v_scale, code, stream)
+    _lib.check(status, "paged_attention_fp8")
+    return out

@@ -1,0 +1,63 @@
+"""FP8 KV pool: the oracle pinned against torch's float8_e4m3fn, and the C-ABI argument checks (no GPU)."""
+
+import numpy as np
+import torch
+
+from myvllm_mini_engine_b200 import _lib
+from oracle import fp8_kv
+
+
+def torch_e4m3(values):
+    clipped = np.clip(values, -fp8_kv.E4M3_MAX, fp8_kv.E4M3_MAX)
+    return torch.from_numpy(clipped).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+
+
+def test_encoder_matches_torch_on_every_bf16_value():
+    x = (np.arange(65536, dtype=np.uint32) << 16).view(np.float32)
+    finite = np.isfinite(x)
+    assert np.array_equal(fp8_kv.encode_e4m3(x)[finite], torch_e4m3(x[finite]))
+
+
+def test_encoder_matches_torch_on_random_fp32_and_edges():
+    gen = np.random.default_rng(11)
+    x = (gen.standard_normal(500_000) * gen.choice([1e-4, 0.01, 1.0, 50.0, 400.0], 500_000)).astype(np.float32)
+    assert np.array_equal(fp8_kv.encode_e4m3(x), torch_e4m3(x))
+    edges = np.array([np.inf, -np.inf, np.nan, -0.0, 2 ** -10, 3 * 2 ** -10, 464.0, 1e30], dtype=np.float32)
+    assert fp8_kv.encode_e4m3(edges).tolist() == [0x7E, 0xFE, 0x7F, 0x80, 0x00, 0x02, 0x7E, 0x7E]
+
+
+def test_decode_table_matches_torch():
+    codes = np.arange(256, dtype=np.uint8)
+    want = torch.from_numpy(codes).view(torch.float8_e4m3fn).float().numpy()
+    got = fp8_kv.decode_e4m3(codes)
+    nan = np.isnan(want)
+    assert np.array_equal(nan, np.isnan(got)) and np.array_equal(got[~nan], want[~nan])
+    # every finite code survives encode(decode(code)) unchanged
+    assert np.array_equal(fp8_kv.encode_e4m3(got[~nan]), codes[~nan])
+
+
+def test_scatter_oracle_skips_slots_outside_the_capacity():
+    kc = torch.zeros(2, 4, 1, 16, dtype=torch.uint8)
+    vc = torch.zeros_like(kc)
+    key = torch.ones(3, 1, 16)
+    slots = torch.tensor([1, -1, 8])
+    fp8_kv.scatter_slots_fp8(kc, vc, slots, key, -key, 0.5, 0.25)
+    assert kc.view(-1, 16)[1].tolist() == [fp8_kv.encode_e4m3(np.float32(2.0)).item()] * 16
+    assert vc.view(-1, 16)[1].tolist() == [fp8_kv.encode_e4m3(np.float32(-4.0)).item()] * 16
+    assert int(kc.sum()) == 16 * int(kc.view(-1, 16)[1, 0])
+
+
+def test_abi_rejects_bad_fp8_arguments_without_a_gpu():
+    lib = _lib.load()
+    p = 16  # never dereferenced: every call below fails its checks first
+    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 80, 10, 16, 4, 0.1, 0.1, _lib.BF16, None)
+    assert rc == _lib.EINVAL and "head_dim" in lib.minikv_last_error().decode()
+    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 128, 10, 16, 4, 0.1, 0.1, _lib.F32, None)
+    assert rc == _lib.EINVAL and "FP16/BF16" in lib.minikv_last_error().decode()
+    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 128, 10, 16, 4, 0.0, 0.1, _lib.BF16, None)
+    assert rc == _lib.EINVAL and "scales" in lib.minikv_last_error().decode()
+    assert lib.minikv_paged_decode_fp8_workspace_bytes(2, 8, 4, 80, 10, 16, 4, _lib.BF16) == -1
+    rc = lib.minikv_kv_scatter_slots_fp8(p, p, p, p, p, 4, 8, 4, 3, 5, 15, 15, 0.1, 0.1, _lib.F16, None)
+    assert rc == _lib.EINVAL and "multiple of 16" in lib.minikv_last_error().decode()
+    rc = lib.minikv_kv_scatter_slots_fp8(p, p, p, p, p, 4, 8, 4, 2, 64, 128, 128, float("inf"), 0.1, _lib.F16, None)
+    assert rc == _lib.EINVAL and "scales" in lib.minikv_last_error().decode()

@@ -1,0 +1,175 @@
+"""FP8 (E4M3) KV pool on the GPU against the CPU oracle (oracle/fp8_kv.py).
+
+The quantising scatter must match the oracle byte for byte.  Decode attention
+over an FP8 pool is compared with the fp32 oracle run on the dequantised pool
+(``code * scale``), at the decode tolerances: fp16 atol=rtol=2e-3, bf16
+atol=rtol=1e-2.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+from myvllm_mini_engine_b200 import _lib
+from myvllm_mini_engine_b200.kernels import paged_attention, paged_attention_fp8, write_kv_cache_slots_fp8
+from oracle import fp8_kv
+
+pytestmark = pytest.mark.gpu
+TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
+K_SCALE, V_SCALE = 0.0125, 0.0095  # N(0,1) data spans about +-400 codes' worth of range
+
+
+def fp8_pools(c, k_scale=K_SCALE, v_scale=V_SCALE):
+    """The case's 16-bit pools quantised by the oracle (uint8, CPU)."""
+    k = torch.from_numpy(fp8_kv.quantize(c["key_cache"], k_scale))
+    v = torch.from_numpy(fp8_kv.quantize(c["value_cache"], v_scale))
+    return k, v
+
+
+def run_both(c, dtype, k_scale=K_SCALE, v_scale=V_SCALE, validate=True, tables=None, lens=None):
+    kq, vq = fp8_pools(c, k_scale, v_scale)
+    tables = c["block_tables"] if tables is None else tables
+    lens = c["context_lens"] if lens is None else lens
+    expected = fp8_kv.paged_attention_fp8_fp32(c["query"], kq, vq, tables, lens, c["block_size"], k_scale, v_scale)
+    actual = paged_attention_fp8(c["query"].cuda(), kq.cuda(), vq.cuda(), tables.cuda(), lens.cuda(),
+                                 c["block_size"], k_scale, v_scale, validate=validate)
+    return actual, expected
+
+
+def assert_close(actual, expected_fp32, dtype):
+    tol = TOL[dtype]
+    torch.testing.assert_close(actual.float().cpu(), expected_fp32, atol=tol, rtol=tol)
+
+
+@pytest.mark.parametrize("src", [torch.float32, torch.float16, torch.bfloat16])
+def test_quantising_scatter_is_bit_exact(cuda_device, src):
+    gen = np.random.default_rng(5)
+    blocks, bs, hkv, dim, tokens = 12, 16, 4, 64, 150
+    mags = gen.choice([1e-6, 1e-3, 0.05, 1.0, 3.0, 6.0], size=(2, tokens + 8, hkv, dim))
+    data = torch.from_numpy((gen.standard_normal((2, tokens + 8, hkv, dim)) * mags).astype(np.float32)).to(src)
+    # edge values: saturation (+-inf and beyond 448*scale), signed zero, ties, the subnormal range
+    edge = torch.tensor([float("inf"), -float("inf"), -0.0, 0.0, 1e9, -1e9, 448 * K_SCALE, 2 ** -10 * K_SCALE,
+                         -(2 ** -10) * K_SCALE, 2 ** -9 * K_SCALE, 1.0625 * K_SCALE, 1.1875 * K_SCALE],
+                        dtype=torch.float32).to(src)
+    data[0, 0, 0, :edge.numel()] = edge
+    data[1, 2, 1, :edge.numel()] = edge / K_SCALE * V_SCALE
+    # token-strided views (every other token of a larger buffer)
+    key, value = data[0, ::2], data[1, ::2]
+    n = key.shape[0]
+    slots = torch.from_numpy(gen.permutation(blocks * bs)[:n].astype(np.int64))
+    slots[3] = -1
+    slots[7] = blocks * bs + 5  # outside the capacity: skipped
+    init = torch.from_numpy(gen.integers(0, 256, size=(2, blocks, bs, hkv, dim), dtype=np.uint8))
+    kc, vc = init[0].clone(), init[1].clone()
+    fp8_kv.scatter_slots_fp8(kc, vc, slots, key.contiguous(), value.contiguous(), K_SCALE, V_SCALE)
+    gk, gv = init[0].cuda(), init[1].cuda()
+    write_kv_cache_slots_fp8(gk, gv, slots.cuda(), key.cuda(), value.cuda(), K_SCALE, V_SCALE, validate=False)
+    torch.cuda.synchronize()
+    assert torch.equal(gk.cpu(), kc) and torch.equal(gv.cpu(), vc)
+    # the float8 dtype view reads back the same values the oracle decodes
+    got = gk.view(torch.float8_e4m3fn).float().cpu().numpy()
+    want = fp8_kv.decode_e4m3(kc.numpy())
+    assert np.array_equal(np.isnan(got), np.isnan(want)) and np.array_equal(got[~np.isnan(got)], want[~np.isnan(want)])
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+@pytest.mark.parametrize("dim", [32, 64, 96, 128, 192, 256])
+def test_decode_matches_oracle_on_dequantised_pool(cuda_device, dtype, dim):
+    c = cases.decode_case(dtype, head_dim=dim)
+    actual, expected = run_both(c, dtype)
+    assert actual.dtype == dtype and actual.shape == c["query"].shape
+    assert_close(actual, expected, dtype)
+
+
+@pytest.mark.parametrize("block_size,lengths,heads,kv_heads", [
+    (16, (256, 255), 8, 1), (32, (257, 1025, 9), 16, 8), (16, (4097,), 16, 8), (256, (513, 1, 300), 16, 8),
+    (1, (7, 33), 16, 8), (24, (100, 47), 32, 4), (16, (65,), 16, 16), (16, (700, 3000), 32, 2),
+])
+def test_block_partition_and_group_boundaries(cuda_device, block_size, lengths, heads, kv_heads):
+    c = cases.decode_case(torch.bfloat16, block_size=block_size, lengths=lengths, heads=heads, kv_heads=kv_heads)
+    actual, expected = run_both(c, torch.bfloat16)
+    assert_close(actual, expected, torch.bfloat16)
+
+
+def test_scales_apply_and_equal_the_16bit_decode_of_the_dequantised_pool(cuda_device):
+    c = cases.decode_case(torch.float16, lengths=(33, 600, 129))
+    for k_scale, v_scale in ((K_SCALE, V_SCALE), (0.5, 2.0), (1.0, 1.0)):
+        kq, vq = fp8_pools(c, k_scale, v_scale)
+        fp8 = paged_attention_fp8(c["query"].cuda(), kq.cuda(), vq.cuda(), c["block_tables"].cuda(),
+                                  c["context_lens"].cuda(), 16, k_scale, v_scale)
+        # the 16-bit decode of the dequantised pool (rounded to fp16; exact for power-of-two scales)
+        kd = fp8_kv.dequantize(kq, k_scale).to(torch.float16).cuda()
+        vd = fp8_kv.dequantize(vq, v_scale).to(torch.float16).cuda()
+        ref = paged_attention(c["query"].cuda(), kd, vd, c["block_tables"].cuda(), c["context_lens"].cuda(), 16)
+        assert_close(fp8, ref.float().cpu(), torch.float16)
+
+
+def test_trusted_mode_invalid_pages_and_lengths(cuda_device):
+    c = cases.decode_case(torch.bfloat16, lengths=(65, 300, 17))
+    tables = c["block_tables"].clone()
+    tables[0].fill_(-1)
+    tables[1, 3] = 1 << 40
+    lens = c["context_lens"].clone()
+    lens[2] = 10_000
+    actual, expected = run_both(c, torch.bfloat16, validate=False, tables=tables, lens=lens)
+    assert torch.isfinite(actual).all() and not actual[0].any() and not actual[2].any()
+    assert_close(actual, expected, torch.bfloat16)
+    assert _lib.device_status() == 0
+
+
+def test_rejects_unsupported_arguments(cuda_device):
+    c = cases.decode_case(torch.bfloat16, head_dim=80, lengths=(5,))
+    kq, vq = fp8_pools(c)
+    args = [c["query"].cuda(), kq.cuda(), vq.cuda(), c["block_tables"].cuda(), c["context_lens"].cuda(), 16]
+    with pytest.raises(RuntimeError, match="head_dim"):
+        paged_attention_fp8(*args, K_SCALE, V_SCALE)
+    c = cases.decode_case(torch.float32, head_dim=64, lengths=(5,))
+    kq, vq = fp8_pools(c)
+    with pytest.raises(RuntimeError, match="FP16/BF16"):
+        paged_attention_fp8(c["query"].cuda(), kq.cuda(), vq.cuda(), c["block_tables"].cuda(),
+                            c["context_lens"].cuda(), 16, K_SCALE, V_SCALE)
+    with pytest.raises(ValueError, match="finite and positive"):
+        paged_attention_fp8(c["query"].cuda().half(), kq.cuda(), vq.cuda(), c["block_tables"].cuda(),
+                            c["context_lens"].cuda(), 16, 0.0, V_SCALE)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_scatter_then_decode_replays_in_a_cuda_graph(cuda_device, dtype):
+    """One captured step: quantise the new tokens into the pool, then decode; replays see new inputs."""
+    c = cases.decode_case(dtype, lengths=(40, 255, 517, 3))
+    kq, vq = fp8_pools(c)
+    gk, gv = kq.cuda(), vq.cuda()
+    tables, lens = c["block_tables"].cuda(), c["context_lens"].cuda()
+    batch, _, dim = c["query"].shape
+    hkv = c["key_cache"].shape[2]
+    gen = torch.Generator().manual_seed(3)
+    new_k = torch.randn(batch, hkv, dim, generator=gen).to(dtype).cuda()
+    new_v = torch.randn(batch, hkv, dim, generator=gen).to(dtype).cuda()
+    # slot of each request's last token
+    last = (lens - 1).cpu()
+    slots = torch.tensor([int(c["block_tables"][b, int(last[b]) // 16]) * 16 + int(last[b]) % 16
+                          for b in range(batch)], dtype=torch.int64).cuda()
+    query = c["query"].cuda()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        paged_attention_fp8(query, gk, gv, tables, lens, 16, K_SCALE, V_SCALE, validate=False)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        write_kv_cache_slots_fp8(gk, gv, slots, new_k, new_v, K_SCALE, V_SCALE, validate=False)
+        out = paged_attention_fp8(query, gk, gv, tables, lens, 16, K_SCALE, V_SCALE, validate=False)
+    for step in range(2):
+        new_k.normal_()
+        new_v.normal_()
+        query.mul_(0.9)
+        graph.replay()
+        torch.cuda.synchronize()
+        kc, vc = kq.clone(), vq.clone()
+        fp8_kv.scatter_slots_fp8(kc, vc, slots.cpu(), new_k.cpu(), new_v.cpu(), K_SCALE, V_SCALE)
+        assert torch.equal(gk.cpu(), kc) and torch.equal(gv.cpu(), vc)
+        expected = fp8_kv.paged_attention_fp8_fp32(query.cpu(), kc, vc, c["block_tables"], c["context_lens"], 16,
+                                                   K_SCALE, V_SCALE)
+        assert_close(out, expected, dtype)
+    assert _lib.device_status() == 0
