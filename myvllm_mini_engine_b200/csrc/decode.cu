@@ -67,6 +67,8 @@ struct DecodeParams {
     int stages;
     int row_stride;       // shared-memory stride of one token row (padded)
     int early_prologue;   // 1: lens/tables predate the previous kernel; read them before griddep_wait
+    int coalesce;         // 1: rows unpadded and the CTA holds every kv head: one bulk copy per run of
+                          //    consecutive physical rows (fp8 pool only)
     float scale_log2;     // log2(e) / sqrt(D) (times the key scale for an fp8 pool)
     float out_scale;      // fp8 pool: the value scale, applied to the output (unused otherwise)
 };
@@ -513,13 +515,39 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                     mbar_arrive_expect_tx(&full[slot], (uint32_t)(__popcll(mask) * copy_row * 2));
                 }
                 __syncwarp();
+                if (p.coalesce) {
+                    // A run = consecutive tokens whose physical rows are consecutive: one
+                    // copy of len rows (stride == copy_row == cache_row here).
+                    const int prev0 = __shfl_up_sync(0xffffffffu, row[0], 1);
+                    const int last0 = __shfl_sync(0xffffffffu, row[0], 31);
+                    const int prev1 = __shfl_up_sync(0xffffffffu, row[1], 1);
+                    const bool head0 = ok[0] && (lane == 0 || prev0 < 0 || prev0 != row[0] - 1);
+                    const bool head1 = ok[1] && (lane == 0 ? (last0 < 0 || last0 != row[1] - 1)
+                                                           : (prev1 < 0 || prev1 != row[1] - 1));
+                    const uint64_t heads = (uint64_t)__ballot_sync(0xffffffffu, head0) |
+                                           ((uint64_t)__ballot_sync(0xffffffffu, head1) << 32);
+                    const uint64_t stops = heads | ~mask;  // bits >= TT are never in mask
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    if (!ok[h]) continue;
-                    const int j = lane + 32 * h;
-                    const int64_t r = row[h];
-                    bulk_load(kdst + j * stride, kbase + r * cache_row, copy_row, &full[slot], policy);
-                    bulk_load(vdst + j * stride, vbase + r * cache_row, copy_row, &full[slot], policy);
+                    for (int h = 0; h < 2; ++h) {
+                        if (!(h ? head1 : head0)) continue;
+                        const int j = lane + 32 * h;
+                        const uint64_t rest = j < 63 ? (stops >> (j + 1)) : 0ull;
+                        const int len = rest ? __ffsll((long long)rest) : 64 - j;
+                        const int64_t r = row[h];
+                        bulk_load(kdst + j * stride, kbase + r * cache_row, (uint32_t)(len * copy_row), &full[slot],
+                                  policy);
+                        bulk_load(vdst + j * stride, vbase + r * cache_row, (uint32_t)(len * copy_row), &full[slot],
+                                  policy);
+                    }
+                } else {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        if (!ok[h]) continue;
+                        const int j = lane + 32 * h;
+                        const int64_t r = row[h];
+                        bulk_load(kdst + j * stride, kbase + r * cache_row, copy_row, &full[slot], policy);
+                        bulk_load(vdst + j * stride, vbase + r * cache_row, copy_row, &full[slot], policy);
+                    }
                 }
             }
             __syncwarp();
@@ -585,7 +613,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
 
 // ------------------------------------------------------------------ host side
 struct DecodePlan {
-    bool mma;
+    bool mma, coalesce;
     int tile_tokens, stages, row_stride, heads_per_item, heads_per_cta, chunks_per_head, chunk_groups,
         head_groups;
     int grid, smem_bytes;
@@ -624,7 +652,11 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
         z = (int)((Hkv + hpc - 1) / hpc);
     }
     // Padding by 16 bytes makes (stride / 16) odd: ldmatrix rows hit distinct banks.
-    const int stride = hpc * (int)D * es + 16;
+    // fp8 pool with every kv head in one CTA: token rows are contiguous in the
+    // pool, so they are staged unpadded and copied in runs (the fp8 consumer's
+    // loads are built for that layout).
+    const bool coalesce = kv_fp8 && hpc == Hkv;
+    const int stride = hpc * (int)D * es + (coalesce ? 0 : 16);
     int tt = (32768 / stride) / sc * sc;
     tt = std::max(sc, std::min(64, tt));
     const int stage = 2 * tt * stride;
@@ -642,6 +674,7 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
     plan->tile_tokens = tt;
     plan->stages = stages;
     plan->row_stride = stride;
+    plan->coalesce = coalesce;
     plan->heads_per_item = heads_per_item;
     plan->heads_per_cta = hpc;
     plan->chunks_per_head = cph;
@@ -728,6 +761,7 @@ static DecodeParams decode_params(const void* query, const void* key_cache, cons
     p.tile_tokens = plan.tile_tokens;
     p.stages = plan.stages;
     p.row_stride = plan.row_stride;
+    p.coalesce = plan.coalesce ? 1 : 0;
     p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
     return p;
 }

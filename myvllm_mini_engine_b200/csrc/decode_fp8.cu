@@ -9,8 +9,13 @@
 // follows its slot-scatter contract (mini_engine/kernels/csrc/data.cu:196-206:
 // a slot outside the capacity writes nothing).
 //
-// Decode.  The producer warp and the ticketed merge of decode.cu are reused
-// unchanged (rows are simply one byte per element).  The consumer converts
+// Decode.  The producer warp and the ticketed merge of decode.cu are reused.
+// When one CTA holds every kv head (the usual case: a token's row is then
+// hpc * D bytes and consecutive rows of a page are contiguous), rows are
+// staged unpadded and the producer issues one bulk copy per run of
+// consecutive physical rows, a page or more, instead of one per token: per
+// token copies of 1 KB rows held the loop at about half the HBM rate.  The
+// consumer converts
 // K and V to fp16 in registers (two e4m3 bytes -> one f16x2 per cvt, exact:
 // every e4m3 value is an fp16 normal or zero) and runs the same transposed
 // mma.sync scheme as decode_mma.cu in fp16:
@@ -18,13 +23,15 @@
 //   O^T += V^T P^T with P split into fp16 hi + lo terms.
 // The key scale is folded into the softmax scale and the value scale into the
 // final normalisation.  A dot product does not depend on the order of its
-// terms, so the head dims inside each 16-dim k-step are permuted to make a
-// lane's K bytes one 32-bit word (dims 16kk + 4q4 .. +3), and Q is permuted
-// the same way.  For V^T (the A operand, dims as rows), a lane loads one word
-// (4 dims) from each of its 4 tokens and assembles the token pairs with byte
-// permutes; each 32-dim group of O^T is two m-tiles whose rows are dims
-// 32u + 4g + {0, 1} and {2, 3}.  With the row stride = 16 mod 64 bytes, both
-// load patterns are free of bank conflicts.
+// terms, so the head dims of the k-steps are permuted: lane q4 of k-step kk
+// covers dims q4*D/4 + 4kk .. +3, so a lane's K bytes of a token are one
+// contiguous D/4-byte run (vector loads), and Q is permuted the same way.
+// For V^T (the A operand, dims as rows), a lane loads dims g*D/8 .. +D/8 of
+// each of its 4 tokens and pairs the tokens with byte permutes; word w of
+// that run feeds m-tiles 2w (rows g, g+8 = dims g*D/8 + 4w + 0, 1) and 2w + 1
+// (dims + 2, 3).  Rows are staged unpadded when the producer copies runs of
+// whole rows (the CTA holds every kv head); the vector loads then meet 2-way
+// (K) and 4-way (V) bank conflicts.
 #include <cuda_fp8.h>
 
 #include "common.cuh"
@@ -43,6 +50,30 @@ __device__ __forceinline__ uint32_t byte_perm(uint32_t a, uint32_t b, uint32_t s
     return r;
 }
 
+// NB bytes (a multiple of 4) at p as 32-bit words, in the widest vectors the
+// alignment (ALIGN, a power of two >= 4) allows.
+template <int NB, int ALIGN>
+__device__ __forceinline__ void load_words(const unsigned char* p, uint32_t* w) {
+    if constexpr (ALIGN >= 16 && NB % 16 == 0) {
+#pragma unroll
+        for (int i = 0; i < NB / 16; ++i) {
+            const uint4 v = *reinterpret_cast<const uint4*>(p + 16 * i);
+            w[4 * i] = v.x; w[4 * i + 1] = v.y; w[4 * i + 2] = v.z; w[4 * i + 3] = v.w;
+        }
+    } else if constexpr (ALIGN >= 8 && NB % 8 == 0) {
+#pragma unroll
+        for (int i = 0; i < NB / 8; ++i) {
+            const uint2 v = *reinterpret_cast<const uint2*>(p + 8 * i);
+            w[2 * i] = v.x; w[2 * i + 1] = v.y;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < NB / 4; ++i) w[i] = *reinterpret_cast<const uint32_t*>(p + 4 * i);
+    }
+}
+
+constexpr int pow2_align(int bytes) { return (bytes % 16 == 0) ? 16 : (bytes % 8 == 0) ? 8 : 4; }
+
 // fp16 pair of two floats, saturated to the finite fp16 range.
 __device__ __forceinline__ uint32_t h2_sat(float a, float b) {
     a = fminf(fmaxf(a, -65504.f), 65504.f);
@@ -54,12 +85,14 @@ template <typename T, int D>
 struct Fp8MmaConsumer {
     static_assert(D % 32 == 0, "the fp8 pool needs head_dim % 32 == 0");
     static constexpr int KSTEPS = D / 16;  // k-steps of S^T = K Q^T
-    static constexpr int GROUPS = D / 32;  // 32-dim groups of O^T (two m-tiles each)
+    static constexpr int GROUPS = D / 32;  // V words per token and lane (two m-tiles each)
+    static constexpr int KB = D / 4;       // K bytes of a token per lane
+    static constexpr int VB = D / 8;       // V bytes of a token per lane
     static constexpr int kKvBytes = 1;     // bytes per cached element
     using Mma = MmaType<__half>;
 
-    uint32_t qb[KSTEPS][2];  // Q^T (fp16): head g, dims 16kk + 4q4 + {0,1} and + {2,3}
-    float o[2 * GROUPS][4];  // O^T: m-tile 2u + i, row g -> dim 32u + 4g + 2i, row g + 8 -> + 1
+    uint32_t qb[KSTEPS][2];  // Q^T (fp16): head g, dims q4*D/4 + 4kk + {0,1} and + {2,3}
+    float o[2 * GROUPS][4];  // O^T: m-tile 2w + i, row g -> dim g*D/8 + 4w + 2i, row g + 8 -> + 1
     float m[2], l[2];
     int g, q4;
 
@@ -74,7 +107,7 @@ struct Fp8MmaConsumer {
         for (int kk = 0; kk < KSTEPS; ++kk) {
             float f[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) f[i] = valid ? Elem<T>::to_float(qrows[g * D + 16 * kk + 4 * q4 + i]) : 0.f;
+            for (int i = 0; i < 4; ++i) f[i] = valid ? Elem<T>::to_float(qrows[g * D + q4 * KB + 4 * kk + i]) : 0.f;
             qb[kk][0] = h2_sat(f[0], f[1]);
             qb[kk][1] = h2_sat(f[2], f[3]);
         }
@@ -89,19 +122,18 @@ struct Fp8MmaConsumer {
     __device__ void tile(const unsigned char* kptr, const unsigned char* vptr, int stride, int TT, int n,
                          uint64_t mask, float scale_log2) {
         for (int sub = 0; sub < TT; sub += 16) {
-            // ---- S^T = K Q^T: lane (g, q4) reads dims 16kk + 4q4 .. +3 of tokens g and g + 8
+            // ---- S^T = K Q^T: lane (g, q4) reads dims q4*D/4 .. +D/4 of tokens g and g + 8
             float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
-            const unsigned char* k0 = kptr + (sub + g) * stride + 4 * q4;
-            const unsigned char* k1 = k0 + 8 * stride;
+            uint32_t kw0[KSTEPS], kw1[KSTEPS];
+            load_words<KB, pow2_align(KB)>(kptr + (sub + g) * stride + q4 * KB, kw0);
+            load_words<KB, pow2_align(KB)>(kptr + (sub + g + 8) * stride + q4 * KB, kw1);
 #pragma unroll
             for (int kk = 0; kk < KSTEPS; ++kk) {
-                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(k0 + 16 * kk);
-                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(k1 + 16 * kk);
                 uint32_t a[4];
-                a[0] = e4m3x2_to_h2(w0);
-                a[1] = e4m3x2_to_h2(w1);
-                a[2] = e4m3x2_to_h2(w0 >> 16);
-                a[3] = e4m3x2_to_h2(w1 >> 16);
+                a[0] = e4m3x2_to_h2(kw0[kk]);
+                a[1] = e4m3x2_to_h2(kw1[kk]);
+                a[2] = e4m3x2_to_h2(kw0[kk] >> 16);
+                a[3] = e4m3x2_to_h2(kw1[kk] >> 16);
                 Mma::mma((kk & 1) ? s2 : s, a, qb[kk][0], qb[kk][1]);
             }
             // ---- mask and scale (as decode_mma.cu; the key scale is in scale_log2)
@@ -155,15 +187,17 @@ struct Fp8MmaConsumer {
             const uint32_t b1 = pick_halves(__shfl_sync(0xffffffffu, h23, src0), __shfl_sync(0xffffffffu, h23, src1), odd);
             const uint32_t c0 = pick_halves(__shfl_sync(0xffffffffu, l01, src0), __shfl_sync(0xffffffffu, l01, src1), odd);
             const uint32_t c1 = pick_halves(__shfl_sync(0xffffffffu, l23, src0), __shfl_sync(0xffffffffu, l23, src1), odd);
-            // ---- O^T += V^T P^T: lane (g, q4) reads dims 32u + 4g .. +3 of tokens 2q4, 2q4+1, 2q4+8, 2q4+9
-            const unsigned char* v0 = vptr + (sub + 2 * q4) * stride + 4 * g;
+            // ---- O^T += V^T P^T: lane (g, q4) reads dims g*D/8 .. +D/8 of tokens 2q4, 2q4+1, 2q4+8, 2q4+9
+            uint32_t vw[4][GROUPS];
+            const unsigned char* v0 = vptr + (sub + 2 * q4) * stride + g * VB;
+            load_words<VB, pow2_align(VB)>(v0, vw[0]);
+            load_words<VB, pow2_align(VB)>(v0 + stride, vw[1]);
+            load_words<VB, pow2_align(VB)>(v0 + 8 * stride, vw[2]);
+            load_words<VB, pow2_align(VB)>(v0 + 9 * stride, vw[3]);
 #pragma unroll
             for (int u = 0; u < GROUPS; ++u) {
-                const uint32_t w0 = *reinterpret_cast<const uint32_t*>(v0 + 32 * u);
-                const uint32_t w1 = *reinterpret_cast<const uint32_t*>(v0 + stride + 32 * u);
-                const uint32_t w2 = *reinterpret_cast<const uint32_t*>(v0 + 8 * stride + 32 * u);
-                const uint32_t w3 = *reinterpret_cast<const uint32_t*>(v0 + 9 * stride + 32 * u);
-                // byte i of a word is dim 32u + 4g + i; pair the two tokens of each k slot
+                const uint32_t w0 = vw[0][u], w1 = vw[1][u], w2 = vw[2][u], w3 = vw[3][u];
+                // byte i of word u is dim g*D/8 + 4u + i; pair the two tokens of each k slot
                 const uint32_t x01 = byte_perm(w0, w1, 0x5140u), x23 = byte_perm(w2, w3, 0x5140u);  // dims +0, +1
                 const uint32_t y01 = byte_perm(w0, w1, 0x7362u), y23 = byte_perm(w2, w3, 0x7362u);  // dims +2, +3
                 uint32_t a[4];
@@ -198,7 +232,7 @@ struct Fp8MmaConsumer {
                 T* orow = static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh) * D;
 #pragma unroll
                 for (int u = 0; u < GROUPS; ++u) {
-                    T* dst = orow + 32 * u + 4 * g;
+                    T* dst = orow + g * VB + 4 * u;
                     dst[0] = Elem<T>::from_float(o[2 * u][h] * inv);
                     dst[1] = Elem<T>::from_float(o[2 * u][h + 2] * inv);
                     dst[2] = Elem<T>::from_float(o[2 * u + 1][h] * inv);
@@ -208,7 +242,7 @@ struct Fp8MmaConsumer {
                 float* prow = p.partial + (record * p.q_heads + qh) * D;
 #pragma unroll
                 for (int u = 0; u < GROUPS; ++u)
-                    *reinterpret_cast<float4*>(prow + 32 * u + 4 * g) =
+                    *reinterpret_cast<float4*>(prow + g * VB + 4 * u) =
                         make_float4(o[2 * u][h] * inv, o[2 * u][h + 2] * inv, o[2 * u + 1][h] * inv,
                                     o[2 * u + 1][h + 2] * inv);
                 if (g == 0) p.lse[record * p.q_heads + qh] = (L > 0.f) ? m[h] + log2f(L) : -INFINITY;

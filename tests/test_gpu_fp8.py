@@ -173,3 +173,19 @@ def test_scatter_then_decode_replays_in_a_cuda_graph(cuda_device, dtype):
                                                    K_SCALE, V_SCALE)
         assert_close(out, expected, dtype)
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("block_size", [16, 32])
+def test_runs_across_contiguous_pages(cuda_device, block_size):
+    """Pages laid out back to back: one staged copy spans several pages (and whole tiles)."""
+    c = cases.decode_case(torch.bfloat16, block_size=block_size, lengths=(1000, 37, 513))
+    width = c["block_tables"].shape[1]
+    c["block_tables"] = torch.arange(3 * width, dtype=torch.int64).view(3, width)
+    actual, expected = run_both(c, torch.bfloat16)
+    assert_close(actual, expected, torch.bfloat16)
+    # mixed: contiguous pages with a few holes (-1 pages are masked in trusted mode)
+    tables = c["block_tables"].clone()
+    tables[0, 5] = -1
+    tables[2, 1] = -1
+    actual, expected = run_both(c, torch.bfloat16, validate=False, tables=tables)
+    assert_close(actual, expected, torch.bfloat16)
