@@ -62,9 +62,9 @@ def parse_args(argv=None):
                         help="qwen3: tcgen05 projections with the element-wise steps fused in for per-GPU batches "
                              "up to Qwen3DecodeStep.FUSED_MAX_BATCH (default), or cuBLAS projections around the "
                              "element-wise kernels")
-    parser.add_argument("--kv-dtype", choices=("bf16", "fp8"), default="bf16",
-                        help="decode: the KV pool format; fp8 = E4M3 pool with per-pool scales (quantising "
-                             "slot scatter + fp8 paged attention), device-timed only")
+    parser.add_argument("--kv-dtype", choices=("bf16", "fp8", "fp8_e5m2"), default="bf16",
+                        help="decode: the KV pool format; fp8 = E4M3 pool, fp8_e5m2 = E5M2 pool, with per-pool "
+                             "scales (quantising slot scatter + fp8 paged attention), device-timed only")
     args = parser.parse_args(argv)
     if args.batch is None:
         args.batch = 32 if args.workload == "decode" else 256
@@ -479,12 +479,13 @@ def run_fp8(args, world, rank, local):
 
     device = torch.device("cuda", local)
     x = make_inputs(args.batch, args.context, device, seed=1234 + rank)
+    fmt = "e5m2" if args.kv_dtype == "fp8_e5m2" else "e4m3"
     k_scale, v_scale = 4.5 / 448, 4.5 / 448
     pool_rows = x["key_cache"].shape[0] * BS
     kq = torch.empty(x["key_cache"].shape, dtype=torch.uint8, device=device)
     vq = torch.empty_like(kq)
     write_kv_cache_slots_fp8(kq, vq, torch.arange(pool_rows, device=device), x["key_cache"].view(-1, HKV, D),
-                             x["value_cache"].view(-1, HKV, D), k_scale, v_scale, validate=False)
+                             x["value_cache"].view(-1, HKV, D), k_scale, v_scale, kv_format=fmt, validate=False)
     del x["key_cache"], x["value_cache"]
     last = x["context_lens"] - 1
     slots = (x["block_tables"].gather(1, (last // BS).view(-1, 1)).view(-1) * BS + last % BS).contiguous()
@@ -494,10 +495,10 @@ def run_fp8(args, world, rank, local):
 
     def attend():
         return paged_attention_fp8(x["query"], kq, vq, x["block_tables"], x["context_lens"], BS, k_scale, v_scale,
-                                   validate=False)
+                                   kv_format=fmt, validate=False)
 
     def step():
-        write_kv_cache_slots_fp8(kq, vq, slots, x["key"], x["value"], k_scale, v_scale, validate=False)
+        write_kv_cache_slots_fp8(kq, vq, slots, x["key"], x["value"], k_scale, v_scale, kv_format=fmt, validate=False)
         return attend()
 
     capture_stream = torch.cuda.Stream(device)
@@ -513,7 +514,7 @@ def run_fp8(args, world, rank, local):
     ev_b = torch.cuda.Event(enable_timing=True, external=True)
     probe = torch.cuda.CUDAGraph()
     with torch.cuda.graph(probe, stream=capture_stream):
-        write_kv_cache_slots_fp8(kq, vq, slots, x["key"], x["value"], k_scale, v_scale, validate=False)
+        write_kv_cache_slots_fp8(kq, vq, slots, x["key"], x["value"], k_scale, v_scale, kv_format=fmt, validate=False)
         ev_a.record()
         attend()
         ev_b.record()
@@ -555,9 +556,9 @@ def run_fp8(args, world, rank, local):
     if rank != 0:
         return None
     return {
-        "metric": "fp8 paged-decode KV-read GB/s (E4M3 pool)", "value": world * step_bytes / (ms_per_step * 1e-3) / 1e9,
+        "metric": f"fp8 paged-decode KV-read GB/s ({fmt.upper()} pool)", "value": world * step_bytes / (ms_per_step * 1e-3) / 1e9,
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 KV, bf16 q/out",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": f"{fmt} KV, bf16 q/out",
         "data": "synthetic",
         "config": {"workload": f"decode step (quantising KV scatter + fp8 paged attention) of {args.batch} "
                                f"requests x {args.context} tokens per GPU, Hq16/Hkv8/D128, block 16",
@@ -1015,7 +1016,7 @@ def main(argv=None):
         else:
             if args.impl == "reference":
                 line = run_reference(args, world, rank)
-            elif args.kv_dtype == "fp8":
+            elif args.kv_dtype in ("fp8", "fp8_e5m2"):
                 line = run_fp8(args, world, rank, local)
             else:
                 line = run_ours(args, world, rank, local)

@@ -33,6 +33,8 @@ extern "C" {
 #define MINIKV_ABI_VERSION 1
 
 enum { MINIKV_F32 = 0, MINIKV_F16 = 1, MINIKV_BF16 = 2 };
+/* FP8 KV pool byte formats (OCP FP8). */
+enum { MINIKV_FP8_E4M3 = 0, MINIKV_FP8_E5M2 = 1 };
 enum { MINIKV_OK = 0, MINIKV_EINVAL = 1, MINIKV_ECUDA = 2, MINIKV_EUNSUPPORTED = 3 };
 /* bits of the device status word (minikv_device_status) */
 enum { MINIKV_STATUS_WAIT_TIMEOUT = 1 };
@@ -127,11 +129,13 @@ int minikv_kv_scatter_slots(void* key_cache, void* value_cache, const int64_t* s
 /* ------------------------------------------------------------ FP8 KV pool ---
  * No counterpart in the reference, which lists an FP8 KV pool as future work
  * (VALIDATION_AND_BENCHMARKS.md:375).  The pool has the 16-bit pool's shape,
- * [num_blocks, block_size, kv_heads, head_dim], one OCP E4M3 byte per element
- * (largest finite 448, no infinities), with one fp32 scale for keys and one
- * for values: stored = e4m3(x * (1/scale)), the product rounded to fp32, then
- * to nearest-even E4M3, saturated to +-448 (NaN -> 0x7F); read as
- * stored * scale.
+ * [num_blocks, block_size, kv_heads, head_dim], one OCP FP8 byte per element,
+ * fp8_format MINIKV_FP8_E4M3 (largest finite 448, no infinities) or
+ * MINIKV_FP8_E5M2 (largest finite 57344), with one fp32 scale for keys and one
+ * for values: stored = fp8(x * (1/scale)), the product rounded to fp32, then
+ * to the nearest-even code, saturated to the largest finite value (NaN stays
+ * NaN); read as stored * scale.  E5M2 decodes with byte moves only (an E5M2
+ * byte is the high byte of an fp16), E4M3 keeps one more mantissa bit.
  *
  * Quantising slot scatter: as minikv_kv_scatter_slots (slots outside the
  * capacity are skipped), from fp32/fp16/bf16 rows (`dtype`) into the byte
@@ -140,7 +144,7 @@ int minikv_kv_scatter_slots_fp8(void* key_cache, void* value_cache, const int64_
                                 const void* key, const void* value, int64_t tokens,
                                 int64_t num_blocks, int64_t block_size, int64_t kv_heads, int64_t head_dim,
                                 int64_t key_token_stride, int64_t value_token_stride,
-                                float k_scale, float v_scale, int dtype, void* stream);
+                                float k_scale, float v_scale, int fp8_format, int dtype, void* stream);
 
 /* Decode attention over an FP8 pool: minikv_paged_decode's contract and
  * guards, with an fp16/bf16 query and output (`dtype`) and K/V read as
@@ -155,7 +159,8 @@ int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void
                             const int64_t* block_tables, const int64_t* context_lens, void* out,
                             void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
                             int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
-                            int64_t table_width, float k_scale, float v_scale, int dtype, void* stream);
+                            int64_t table_width, float k_scale, float v_scale, int fp8_format, int dtype,
+                            void* stream);
 
 /* Decode append: request r writes its token at logical position
  * token_offsets[r] through block_tables[r]; rows whose page index or physical

@@ -207,7 +207,10 @@ int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void
                             const int64_t* block_tables, const int64_t* context_lens, void* out,
                             void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
                             int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
-                            int64_t table_width, float k_scale, float v_scale, int dtype, void* stream) {
+                            int64_t table_width, float k_scale, float v_scale, int fp8_format, int dtype,
+                            void* stream) {
+    MINIKV_REQUIRE(fp8_format == MINIKV_FP8_E4M3 || fp8_format == MINIKV_FP8_E5M2, MINIKV_EINVAL,
+                   "fp8 format must be E4M3 or E5M2");
     int rc = check_fp8_decode(batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype);
     if (rc) return rc;
     MINIKV_REQUIRE(valid_scale(k_scale) && valid_scale(v_scale), MINIKV_EINVAL,
@@ -227,8 +230,9 @@ int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void
     p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim) * (double)k_scale);
     p.out_scale = v_scale;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const cudaError_t err = dtype == MINIKV_F16 ? launch_decode_fp8_dim<__half>((int)head_dim, p, plan, s)
-                                                : launch_decode_fp8_dim<__nv_bfloat16>((int)head_dim, p, plan, s);
+    const bool e5m2 = fp8_format == MINIKV_FP8_E5M2;
+    const cudaError_t err = dtype == MINIKV_F16 ? launch_decode_fp8<__half>(e5m2, (int)head_dim, p, plan, s)
+                                                : launch_decode_fp8<__nv_bfloat16>(e5m2, (int)head_dim, p, plan, s);
     if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_decode_fp8 launch");
     return MINIKV_OK;
 }
@@ -236,7 +240,10 @@ int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void
 int minikv_kv_scatter_slots_fp8(void* key_cache, void* value_cache, const int64_t* slot_mapping, const void* key,
                                 const void* value, int64_t tokens, int64_t num_blocks, int64_t block_size,
                                 int64_t kv_heads, int64_t head_dim, int64_t key_token_stride,
-                                int64_t value_token_stride, float k_scale, float v_scale, int dtype, void* stream) {
+                                int64_t value_token_stride, float k_scale, float v_scale, int fp8_format, int dtype,
+                                void* stream) {
+    MINIKV_REQUIRE(fp8_format == MINIKV_FP8_E4M3 || fp8_format == MINIKV_FP8_E5M2, MINIKV_EINVAL,
+                   "fp8 format must be E4M3 or E5M2");
     MINIKV_REQUIRE(tokens >= 0, MINIKV_EINVAL, "packed KV slots must be int64 [tokens]");
     MINIKV_REQUIRE(num_blocks > 0 && block_size > 0, MINIKV_EINVAL, "packed KV cache must be nonempty");
     MINIKV_REQUIRE(valid_dtype(dtype), MINIKV_EINVAL, "packed KV requires FP32/FP16/BF16");
@@ -251,19 +258,20 @@ int minikv_kv_scatter_slots_fp8(void* key_cache, void* value_cache, const int64_
     MINIKV_REQUIRE(key_cache && value_cache && key && value && slot_mapping, MINIKV_EINVAL, "null pointer argument");
     MINIKV_REQUIRE(aligned16(key_cache) && aligned16(value_cache), MINIKV_EINVAL, "KV caches must be 16-byte aligned");
     const float k_inv = 1.0f / k_scale, v_inv = 1.0f / v_scale;
+    const bool e5m2 = fp8_format == MINIKV_FP8_E5M2;
     const int64_t capacity = num_blocks * block_size;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaError_t err;
     if (dtype == MINIKV_F32)
         err = launch_quantize_slots<float>(key_cache, value_cache, key, value, slot_mapping, tokens, capacity,
-                                           row_elems, key_token_stride, value_token_stride, k_inv, v_inv, s);
+                                           row_elems, key_token_stride, value_token_stride, k_inv, v_inv, e5m2, s);
     else if (dtype == MINIKV_F16)
         err = launch_quantize_slots<__half>(key_cache, value_cache, key, value, slot_mapping, tokens, capacity,
-                                            row_elems, key_token_stride, value_token_stride, k_inv, v_inv, s);
+                                            row_elems, key_token_stride, value_token_stride, k_inv, v_inv, e5m2, s);
     else
         err = launch_quantize_slots<__nv_bfloat16>(key_cache, value_cache, key, value, slot_mapping, tokens,
                                                    capacity, row_elems, key_token_stride, value_token_stride, k_inv,
-                                                   v_inv, s);
+                                                   v_inv, e5m2, s);
     if (err != cudaSuccess) return cuda_fail(err, "minikv_kv_scatter_slots_fp8 launch");
     return MINIKV_OK;
 }

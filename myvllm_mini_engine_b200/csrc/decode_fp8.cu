@@ -2,9 +2,9 @@
 // consumer of the split-KV decode kernel for one-byte K/V rows.
 //
 // Format.  The pool has the 16-bit pool's shape, [num_blocks, block_size,
-// kv_heads, head_dim], one OCP E4M3 byte per element, with one fp32 scale for
-// keys and one for values: stored = e4m3_rn_satfinite(x * (1 / scale)), read
-// back as stored * scale.  It halves the bytes a decode step streams.  The
+// kv_heads, head_dim], one OCP FP8 byte per element (E4M3, or E5M2), with one
+// fp32 scale for keys and one for values: stored = fp8_rn_satfinite(x * (1 /
+// scale)), read back as stored * scale.  It halves the bytes a decode step streams.  The
 // reference has no FP8 pool (it is listed there as future work); the write
 // follows its slot-scatter contract (mini_engine/kernels/csrc/data.cu:196-206:
 // a slot outside the capacity writes nothing).
@@ -74,6 +74,19 @@ __device__ __forceinline__ void load_words(const unsigned char* p, uint32_t* w) 
 
 constexpr int pow2_align(int bytes) { return (bytes % 16 == 0) ? 16 : (bytes % 8 == 0) ? 8 : 4; }
 
+// Pairs of fp8 codes to f16x2 for the two formats.  E4M3: the hardware
+// conversion (exact).  E5M2: an E5M2 byte is the high byte of the fp16 of the
+// same value, so a byte permute is the conversion (exact, ALU only).
+template <bool E5M2> struct Fp8Codec;
+template <> struct Fp8Codec<false> {
+    __device__ static __forceinline__ uint32_t lo(uint32_t w) { return e4m3x2_to_h2(w); }        // bytes 0, 1
+    __device__ static __forceinline__ uint32_t hi(uint32_t w) { return e4m3x2_to_h2(w >> 16); }  // bytes 2, 3
+};
+template <> struct Fp8Codec<true> {
+    __device__ static __forceinline__ uint32_t lo(uint32_t w) { return byte_perm(w, 0u, 0x1404u); }
+    __device__ static __forceinline__ uint32_t hi(uint32_t w) { return byte_perm(w, 0u, 0x3424u); }
+};
+
 // fp16 pair of two floats, saturated to the finite fp16 range.
 __device__ __forceinline__ uint32_t h2_sat(float a, float b) {
     a = fminf(fmaxf(a, -65504.f), 65504.f);
@@ -81,7 +94,7 @@ __device__ __forceinline__ uint32_t h2_sat(float a, float b) {
     return Elem<__half>::pack(a, b);
 }
 
-template <typename T, int D>
+template <typename T, int D, bool E5M2>
 struct Fp8MmaConsumer {
     static_assert(D % 32 == 0, "the fp8 pool needs head_dim % 32 == 0");
     static constexpr int KSTEPS = D / 16;  // k-steps of S^T = K Q^T
@@ -90,6 +103,7 @@ struct Fp8MmaConsumer {
     static constexpr int VB = D / 8;       // V bytes of a token per lane
     static constexpr int kKvBytes = 1;     // bytes per cached element
     using Mma = MmaType<__half>;
+    using Codec = Fp8Codec<E5M2>;
 
     uint32_t qb[KSTEPS][2];  // Q^T (fp16): head g, dims q4*D/4 + 4kk + {0,1} and + {2,3}
     float o[2 * GROUPS][4];  // O^T: m-tile 2w + i, row g -> dim g*D/8 + 4w + 2i, row g + 8 -> + 1
@@ -121,63 +135,94 @@ struct Fp8MmaConsumer {
 
     __device__ void tile(const unsigned char* kptr, const unsigned char* vptr, int stride, int TT, int n,
                          uint64_t mask, float scale_log2) {
-        for (int sub = 0; sub < TT; sub += 16) {
-            // ---- S^T = K Q^T: lane (g, q4) reads dims q4*D/4 .. +D/4 of tokens g and g + 8
-            float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
+        // Two 16-token slices per step where the tile allows: their K loads,
+        // conversions and MMAs are independent (ILP for a warp that is alone with
+        // one other on its scheduler), and the online-softmax max, rescale and
+        // exp2 of alpha are paid once per 32 tokens.
+        int sub = 0;
+        for (; sub + 32 <= TT; sub += 32) step<2>(kptr, vptr, stride, sub, n, mask, scale_log2);
+        for (; sub < TT; sub += 16) step<1>(kptr, vptr, stride, sub, n, mask, scale_log2);
+    }
+
+    template <int NS>
+    __device__ __forceinline__ void step(const unsigned char* kptr, const unsigned char* vptr, int stride, int sub,
+                                         int n, uint64_t mask, float scale_log2) {
+        // ---- S^T = K Q^T: lane (g, q4) reads dims q4*D/4 .. +D/4 of tokens g and g + 8 of each slice
+        float s[NS][4], s2[NS][4];
+#pragma unroll
+        for (int i = 0; i < NS; ++i) {
             uint32_t kw0[KSTEPS], kw1[KSTEPS];
-            load_words<KB, pow2_align(KB)>(kptr + (sub + g) * stride + q4 * KB, kw0);
-            load_words<KB, pow2_align(KB)>(kptr + (sub + g + 8) * stride + q4 * KB, kw1);
+            load_words<KB, pow2_align(KB)>(kptr + (sub + 16 * i + g) * stride + q4 * KB, kw0);
+            load_words<KB, pow2_align(KB)>(kptr + (sub + 16 * i + g + 8) * stride + q4 * KB, kw1);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) s[i][e] = s2[i][e] = 0.f;
 #pragma unroll
             for (int kk = 0; kk < KSTEPS; ++kk) {
                 uint32_t a[4];
-                a[0] = e4m3x2_to_h2(kw0[kk]);
-                a[1] = e4m3x2_to_h2(kw1[kk]);
-                a[2] = e4m3x2_to_h2(kw0[kk] >> 16);
-                a[3] = e4m3x2_to_h2(kw1[kk] >> 16);
-                Mma::mma((kk & 1) ? s2 : s, a, qb[kk][0], qb[kk][1]);
+                a[0] = Codec::lo(kw0[kk]);
+                a[1] = Codec::lo(kw1[kk]);
+                a[2] = Codec::hi(kw0[kk]);
+                a[3] = Codec::hi(kw1[kk]);
+                Mma::mma((kk & 1) ? s2[i] : s[i], a, qb[kk][0], qb[kk][1]);
             }
-            // ---- mask and scale (as decode_mma.cu; the key scale is in scale_log2)
-            const int j0 = sub + g, j1 = j0 + 8;
+        }
+        // ---- mask and scale (as decode_mma.cu; the key scale is in scale_log2)
+#pragma unroll
+        for (int i = 0; i < NS; ++i) {
+            const int j0 = sub + 16 * i + g, j1 = j0 + 8;
             const bool ok0 = j0 < n && ((mask >> j0) & 1ull), ok1 = j1 < n && ((mask >> j1) & 1ull);
-            s[0] = ok0 ? (s[0] + s2[0]) * scale_log2 : -INFINITY;
-            s[1] = ok0 ? (s[1] + s2[1]) * scale_log2 : -INFINITY;
-            s[2] = ok1 ? (s[2] + s2[2]) * scale_log2 : -INFINITY;
-            s[3] = ok1 ? (s[3] + s2[3]) * scale_log2 : -INFINITY;
-            float alpha[2];
+            s[i][0] = ok0 ? (s[i][0] + s2[i][0]) * scale_log2 : -INFINITY;
+            s[i][1] = ok0 ? (s[i][1] + s2[i][1]) * scale_log2 : -INFINITY;
+            s[i][2] = ok1 ? (s[i][2] + s2[i][2]) * scale_log2 : -INFINITY;
+            s[i][3] = ok1 ? (s[i][3] + s2[i][3]) * scale_log2 : -INFINITY;
+        }
+        float alpha[2];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                float mx = fmaxf(s[h], s[h + 2]);
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
-                const float mn = fmaxf(m[h], mx);
-                alpha[h] = (mn == -INFINITY) ? 1.f : exp2f(m[h] - mn);
-                m[h] = mn;
+        for (int h = 0; h < 2; ++h) {
+            float mx = fmaxf(s[0][h], s[0][h + 2]);
+#pragma unroll
+            for (int i = 1; i < NS; ++i) mx = fmaxf(mx, fmaxf(s[i][h], s[i][h + 2]));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+            const float mn = fmaxf(m[h], mx);
+            alpha[h] = (mn == -INFINITY) ? 1.f : exp2f(m[h] - mn);
+            m[h] = mn;
+        }
+        float pv[NS][4];
+#pragma unroll
+        for (int i = 0; i < NS; ++i)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) pv[i][e] = (m[e & 1] == -INFINITY) ? 0.f : exp2f(s[i][e] - m[e & 1]);
+        float add0 = 0.f, add1 = 0.f;
+#pragma unroll
+        for (int i = 0; i < NS; ++i) {
+            add0 += pv[i][0] + pv[i][2];
+            add1 += pv[i][1] + pv[i][3];
+        }
+        l[0] = l[0] * alpha[0] + add0;
+        l[1] = l[1] * alpha[1] + add1;
+        if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
+#pragma unroll
+            for (int mt = 0; mt < 2 * GROUPS; ++mt) {
+                o[mt][0] *= alpha[0];
+                o[mt][1] *= alpha[1];
+                o[mt][2] *= alpha[0];
+                o[mt][3] *= alpha[1];
             }
-            float pv[4];
+        }
 #pragma unroll
-            for (int e = 0; e < 4; ++e) pv[e] = (m[e & 1] == -INFINITY) ? 0.f : exp2f(s[e] - m[e & 1]);
-            l[0] = l[0] * alpha[0] + pv[0] + pv[2];
-            l[1] = l[1] * alpha[1] + pv[1] + pv[3];
-            if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {
-#pragma unroll
-                for (int mt = 0; mt < 2 * GROUPS; ++mt) {
-                    o[mt][0] *= alpha[0];
-                    o[mt][1] *= alpha[1];
-                    o[mt][2] *= alpha[0];
-                    o[mt][3] *= alpha[1];
-                }
-            }
+        for (int i = 0; i < NS; ++i) {
             // ---- P = P_hi + P_lo in fp16, moved into the B layout (as decode_mma.cu)
-            const uint32_t h01 = Elem<__half>::pack(pv[0], pv[1]);
-            const uint32_t h23 = Elem<__half>::pack(pv[2], pv[3]);
+            const uint32_t h01 = Elem<__half>::pack(pv[i][0], pv[i][1]);
+            const uint32_t h23 = Elem<__half>::pack(pv[i][2], pv[i][3]);
             float rest[4];
             {
                 float back[4];
                 Elem<__half>::unpack(h01, back);
                 Elem<__half>::unpack(h23, back + 2);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) rest[e] = pv[e] - back[e];
+                for (int e = 0; e < 4; ++e) rest[e] = pv[i][e] - back[e];
             }
             const uint32_t l01 = Elem<__half>::pack(rest[0], rest[1]);
             const uint32_t l23 = Elem<__half>::pack(rest[2], rest[3]);
@@ -189,7 +234,7 @@ struct Fp8MmaConsumer {
             const uint32_t c1 = pick_halves(__shfl_sync(0xffffffffu, l23, src0), __shfl_sync(0xffffffffu, l23, src1), odd);
             // ---- O^T += V^T P^T: lane (g, q4) reads dims g*D/8 .. +D/8 of tokens 2q4, 2q4+1, 2q4+8, 2q4+9
             uint32_t vw[4][GROUPS];
-            const unsigned char* v0 = vptr + (sub + 2 * q4) * stride + g * VB;
+            const unsigned char* v0 = vptr + (sub + 16 * i + 2 * q4) * stride + g * VB;
             load_words<VB, pow2_align(VB)>(v0, vw[0]);
             load_words<VB, pow2_align(VB)>(v0 + stride, vw[1]);
             load_words<VB, pow2_align(VB)>(v0 + 8 * stride, vw[2]);
@@ -201,16 +246,16 @@ struct Fp8MmaConsumer {
                 const uint32_t x01 = byte_perm(w0, w1, 0x5140u), x23 = byte_perm(w2, w3, 0x5140u);  // dims +0, +1
                 const uint32_t y01 = byte_perm(w0, w1, 0x7362u), y23 = byte_perm(w2, w3, 0x7362u);  // dims +2, +3
                 uint32_t a[4];
-                a[0] = e4m3x2_to_h2(x01);
-                a[1] = e4m3x2_to_h2(x01 >> 16);
-                a[2] = e4m3x2_to_h2(x23);
-                a[3] = e4m3x2_to_h2(x23 >> 16);
+                a[0] = Codec::lo(x01);
+                a[1] = Codec::hi(x01);
+                a[2] = Codec::lo(x23);
+                a[3] = Codec::hi(x23);
                 Mma::mma(o[2 * u], a, c0, c1);
                 Mma::mma(o[2 * u], a, b0, b1);
-                a[0] = e4m3x2_to_h2(y01);
-                a[1] = e4m3x2_to_h2(y01 >> 16);
-                a[2] = e4m3x2_to_h2(y23);
-                a[3] = e4m3x2_to_h2(y23 >> 16);
+                a[0] = Codec::lo(y01);
+                a[1] = Codec::hi(y01);
+                a[2] = Codec::lo(y23);
+                a[3] = Codec::hi(y23);
                 Mma::mma(o[2 * u + 1], a, c0, c1);
                 Mma::mma(o[2 * u + 1], a, b0, b1);
             }
@@ -255,7 +300,7 @@ struct Fp8MmaConsumer {
 // One warp per token: K and V rows of `row_elems` elements, 16 per lane step,
 // each rounded as e4m3(x * inv_scale) (fp32 product, then nearest-even E4M3,
 // saturating) into 16 bytes of the pool row.
-template <typename T>
+template <typename T, bool E5M2>
 __global__ void __launch_bounds__(256) quantize_slots_kernel(
     unsigned char* __restrict__ kc, unsigned char* __restrict__ vc, const T* __restrict__ k,
     const T* __restrict__ v, const int64_t* __restrict__ slots, int64_t tokens, int64_t capacity,
@@ -280,7 +325,7 @@ __global__ void __launch_bounds__(256) quantize_slots_kernel(
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
                         const float x = __fmul_rn(Elem<T>::to_float(src[c + 4 * w + i]), inv);
-                        packed |= (uint32_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3) << (8 * i);
+                        packed |= (uint32_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, E5M2 ? __NV_E5M2 : __NV_E4M3) << (8 * i);
                     }
                     word[w] = packed;
                 }
@@ -293,21 +338,22 @@ __global__ void __launch_bounds__(256) quantize_slots_kernel(
 template <typename T>
 static cudaError_t launch_quantize_slots(void* kc, void* vc, const void* k, const void* v, const int64_t* slots,
                                          int64_t tokens, int64_t capacity, int64_t row_elems, int64_t k_stride,
-                                         int64_t v_stride, float k_inv, float v_inv, cudaStream_t stream) {
+                                         int64_t v_stride, float k_inv, float v_inv, bool e5m2, cudaStream_t stream) {
     if (tokens <= 0) return cudaSuccess;
     int64_t blocks = (tokens + 7) / 8;
     const int64_t cap = (int64_t)sm_count_for_current_device() * 8;
     if (blocks > cap) blocks = cap;
-    return launch_chained(quantize_slots_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, stream,
+    return launch_chained(e5m2 ? quantize_slots_kernel<T, true> : quantize_slots_kernel<T, false>,
+                          dim3((unsigned)blocks), dim3(256), 0, stream,
                           static_cast<unsigned char*>(kc), static_cast<unsigned char*>(vc),
                           static_cast<const T*>(k), static_cast<const T*>(v), slots, tokens, capacity, row_elems,
                           k_stride, v_stride, k_inv, v_inv);
 }
 
 // ------------------------------------------------------------ decode host side
-template <typename T, int D>
+template <typename T, int D, bool E5M2>
 static cudaError_t launch_decode_fp8_typed(const DecodeParams& p, const DecodePlan& plan, cudaStream_t stream) {
-    auto kernel = paged_decode_kernel<T, D, Fp8MmaConsumer<T, D>>;
+    auto kernel = paged_decode_kernel<T, D, Fp8MmaConsumer<T, D, E5M2>>;
     static int configured[64] = {0};  // opt-in shared-memory size set per device
     int device = 0;
     cudaError_t err = cudaGetDevice(&device);
@@ -320,17 +366,23 @@ static cudaError_t launch_decode_fp8_typed(const DecodeParams& p, const DecodePl
     return launch_chained(kernel, dim3(plan.grid, plan.head_groups), dim3(kDecodeThreads), plan.smem_bytes, stream, p);
 }
 
-template <typename T>
+template <typename T, bool E5M2>
 static cudaError_t launch_decode_fp8_dim(int D, const DecodeParams& p, const DecodePlan& plan, cudaStream_t stream) {
     switch (D) {
-        case 32: return launch_decode_fp8_typed<T, 32>(p, plan, stream);
-        case 64: return launch_decode_fp8_typed<T, 64>(p, plan, stream);
-        case 96: return launch_decode_fp8_typed<T, 96>(p, plan, stream);
-        case 128: return launch_decode_fp8_typed<T, 128>(p, plan, stream);
-        case 192: return launch_decode_fp8_typed<T, 192>(p, plan, stream);
-        case 256: return launch_decode_fp8_typed<T, 256>(p, plan, stream);
+        case 32: return launch_decode_fp8_typed<T, 32, E5M2>(p, plan, stream);
+        case 64: return launch_decode_fp8_typed<T, 64, E5M2>(p, plan, stream);
+        case 96: return launch_decode_fp8_typed<T, 96, E5M2>(p, plan, stream);
+        case 128: return launch_decode_fp8_typed<T, 128, E5M2>(p, plan, stream);
+        case 192: return launch_decode_fp8_typed<T, 192, E5M2>(p, plan, stream);
+        case 256: return launch_decode_fp8_typed<T, 256, E5M2>(p, plan, stream);
         default: return cudaErrorInvalidValue;
     }
+}
+
+template <typename T>
+static cudaError_t launch_decode_fp8(bool e5m2, int D, const DecodeParams& p, const DecodePlan& plan,
+                                     cudaStream_t stream) {
+    return e5m2 ? launch_decode_fp8_dim<T, true>(D, p, plan, stream) : launch_decode_fp8_dim<T, false>(D, p, plan, stream);
 }
 
 static bool fp8_head_dim(int64_t d) { return d == 32 || d == 64 || d == 96 || d == 128 || d == 192 || d == 256; }

@@ -1,4 +1,4 @@
-"""FP8 (E4M3) KV pool: quantising slot scatter and decode attention.
+"""FP8 KV pool (E4M3 or E5M2): quantising slot scatter and decode attention.
 
 The reference has no FP8 KV pool (``VALIDATION_AND_BENCHMARKS.md:375`` lists it
 as future work), so these two operators extend its API in its own style: the
@@ -6,10 +6,13 @@ scatter mirrors ``write_kv_cache_slots`` (``mini_engine/kernels/data.py:84-130``
 and the decode mirrors ``paged_attention`` (``kernels/paged.py:8-22``), each
 with a key and a value scale.
 
-A pool is a uint8 (or ``torch.float8_e4m3fn``) tensor of the 16-bit pool's
-shape ``[num_blocks, block_size, kv_heads, head_dim]``; element ``x`` is stored
-as ``e4m3(x * (1/scale))`` (fp32 product, nearest-even, saturated to +-448) and
-read as ``code * scale``.  A decode step streams half the bytes of a bf16 pool.
+A pool is a uint8 (or ``torch.float8_e4m3fn`` / ``torch.float8_e5m2``) tensor
+of the 16-bit pool's shape ``[num_blocks, block_size, kv_heads, head_dim]``;
+element ``x`` is stored as ``fp8(x * (1/scale))`` (fp32 product, nearest-even,
+saturated to the largest finite code) and read as ``code * scale``.
+``kv_format`` picks the byte format: "e4m3" (3 mantissa bits, range 448) or
+"e5m2" (2 mantissa bits, range 57344, decoded with byte moves only, so its
+decode runs faster).  A decode step streams half the bytes of a bf16 pool.
 """
 
 from __future__ import annotations
@@ -21,7 +24,14 @@ from .data import _backend, _rows
 from .paged import _require, _workspace, check_backend
 
 FP8_HEAD_DIMS = (32, 64, 96, 128, 192, 256)
-_POOL_DTYPES = (torch.uint8, getattr(torch, "float8_e4m3fn", torch.uint8))
+_POOL_DTYPES = (torch.uint8, getattr(torch, "float8_e4m3fn", torch.uint8), getattr(torch, "float8_e5m2", torch.uint8))
+FORMATS = {"e4m3": 0, "e5m2": 1}
+
+
+def _format(kv_format):
+    if kv_format not in FORMATS:
+        raise ValueError("kv_format must be 'e4m3' or 'e5m2'")
+    return FORMATS[kv_format]
 
 
 def _scale(value, name):
@@ -32,22 +42,23 @@ def _scale(value, name):
 
 
 def write_kv_cache_slots_fp8(key_cache, value_cache, slot_mapping, key, value, k_scale, v_scale, *,
-                             backend="cuda", validate=True):
+                             kv_format="e4m3", backend="cuda", validate=True):
     """Quantise packed K/V rows into FP8 pools at ``slot_mapping`` (slots outside the capacity are skipped).
 
     ``key``/``value`` ``[tokens, kv_heads, head_dim]`` fp32/fp16/bf16 (token-strided
     views are read in place); pools ``[num_blocks, block_size, kv_heads, head_dim]``
-    uint8 or float8_e4m3fn.  ``validate`` adds the host-synchronising slot checks
+    uint8 or a float8 dtype.  ``validate`` adds the host-synchronising slot checks
     of ``write_kv_cache_slots`` (data.py:109-119).
     """
     _backend(backend)
+    fmt = _format(kv_format)
     k_scale, v_scale = _scale(k_scale, "k_scale"), _scale(v_scale, "v_scale")
     if (key_cache.ndim != 4 or value_cache.shape != key_cache.shape
             or any(size <= 0 for size in key_cache.shape)
             or not key_cache.is_contiguous() or not value_cache.is_contiguous()):
         raise ValueError("KV caches must be contiguous [pages, block_size, kv_heads, head_dim]")
     if key_cache.dtype not in _POOL_DTYPES or value_cache.dtype != key_cache.dtype:
-        raise ValueError("an fp8 KV pool must be uint8 or float8_e4m3fn")
+        raise ValueError("an fp8 KV pool must be uint8 or a float8 dtype")
     if key.ndim != 3 or key.shape != value.shape or key.shape[1:] != key_cache.shape[2:]:
         raise ValueError("packed key/value must be [tokens, kv_heads, head_dim] matching the cache")
     if key.dtype not in _lib.DTYPE_CODES or value.dtype != key.dtype:
@@ -80,7 +91,7 @@ def write_kv_cache_slots_fp8(key_cache, value_cache, slot_mapping, key, value, k
         status = lib.minikv_kv_scatter_slots_fp8(
             key_cache.data_ptr(), value_cache.data_ptr(), slot_mapping.data_ptr(), key.data_ptr(),
             value.data_ptr(), tokens, key_cache.shape[0], key_cache.shape[1], key_cache.shape[2],
-            key_cache.shape[3], key_stride, value_stride, k_scale, v_scale, _lib.dtype_code(key.dtype),
+            key_cache.shape[3], key_stride, value_stride, k_scale, v_scale, fmt, _lib.dtype_code(key.dtype),
             _lib.stream_of(key_cache.device))
     _lib.check(status, "write_kv_cache_slots_fp8")
 
@@ -89,15 +100,16 @@ _WS_BYTES: dict = {}
 
 
 def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_lens, block_size, k_scale, v_scale,
-                        *, backend="cuda", validate=True, workspace=None):
+                        *, kv_format="e4m3", backend="cuda", validate=True, workspace=None):
     """Decode attention over FP8 pools: ``softmax(q . (K*k_scale)^T / sqrt(D)) (V*v_scale)``.
 
     Arguments and guards as :func:`paged_attention` (``query [B, Hq, D]`` fp16 or
     bf16, ``block_tables [B, W]`` and ``context_lens [B]`` int64); the pools are
-    uint8 / float8_e4m3fn.  Q.K and P.V run on fp16 tensor cores, so Q is
+    uint8 or a float8 dtype holding ``kv_format`` codes.  Q.K and P.V run on fp16 tensor cores, so Q is
     rounded to fp16 (saturated at +-65504).  Returns ``[B, Hq, D]`` in the query dtype.
     """
     check_backend(backend)
+    fmt = _format(kv_format)
     k_scale, v_scale = _scale(k_scale, "k_scale"), _scale(v_scale, "v_scale")
     _require(query.is_cuda, "query must be CUDA")
     for t in (key_cache, value_cache, block_tables, context_lens):
@@ -108,7 +120,7 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_len
              "invalid query/cache shapes")
     _require(query.dtype in (torch.float16, torch.bfloat16), "an fp8 KV pool needs an FP16/BF16 query")
     _require(key_cache.dtype in _POOL_DTYPES and value_cache.dtype == key_cache.dtype,
-             "an fp8 KV pool must be uint8 or float8_e4m3fn")
+             "an fp8 KV pool must be uint8 or a float8 dtype")
     _require(block_tables.dtype == torch.int64 and context_lens.dtype == torch.int64, "metadata must be int64")
     batch, heads, dim = query.shape
     num_blocks, bs, kv_heads, _ = key_cache.shape
@@ -147,6 +159,6 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_len
         status = lib.minikv_paged_decode_fp8(
             query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
             context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
-            batch, heads, kv_heads, dim, num_blocks, block_size, width, k_scale, v_scale, code, stream)
+            batch, heads, kv_heads, dim, num_blocks, block_size, width, k_scale, v_scale, fmt, code, stream)
     _lib.check(status, "paged_attention_fp8")
     return out

@@ -1,21 +1,39 @@
 """FP8 KV pool: the oracle pinned against torch's float8_e4m3fn, and the C-ABI argument checks (no GPU)."""
 
 import numpy as np
+import pytest
 import torch
 
 from myvllm_mini_engine_b200 import _lib
 from oracle import fp8_kv
 
 
+TORCH_DTYPES = {"e4m3": torch.float8_e4m3fn, "e5m2": torch.float8_e5m2}
+
+
+def torch_fp8(values, fmt="e4m3"):
+    vmax = fp8_kv.FORMATS[fmt][3]
+    clipped = np.clip(values, -vmax, vmax)
+    return torch.from_numpy(clipped).to(TORCH_DTYPES[fmt]).view(torch.uint8).numpy()
+
+
 def torch_e4m3(values):
-    clipped = np.clip(values, -fp8_kv.E4M3_MAX, fp8_kv.E4M3_MAX)
-    return torch.from_numpy(clipped).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    return torch_fp8(values, "e4m3")
 
 
-def test_encoder_matches_torch_on_every_bf16_value():
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_encoder_matches_torch_on_every_bf16_value(fmt):
     x = (np.arange(65536, dtype=np.uint32) << 16).view(np.float32)
     finite = np.isfinite(x)
-    assert np.array_equal(fp8_kv.encode_e4m3(x)[finite], torch_e4m3(x[finite]))
+    assert np.array_equal(fp8_kv.encode_fp8(x, fmt)[finite], torch_fp8(x[finite], fmt))
+
+
+def test_e5m2_encoder_on_random_fp32_and_edges():
+    gen = np.random.default_rng(12)
+    x = (gen.standard_normal(500_000) * gen.choice([1e-6, 0.01, 1.0, 500.0, 3e4], 500_000)).astype(np.float32)
+    assert np.array_equal(fp8_kv.encode_fp8(x, "e5m2"), torch_fp8(x, "e5m2"))
+    edges = np.array([np.inf, -np.inf, -0.0, 2 ** -17, 3 * 2 ** -17, 61440.0], dtype=np.float32)
+    assert fp8_kv.encode_fp8(edges, "e5m2").tolist() == [0x7B, 0xFB, 0x80, 0x00, 0x02, 0x7B]
 
 
 def test_encoder_matches_torch_on_random_fp32_and_edges():
@@ -26,14 +44,16 @@ def test_encoder_matches_torch_on_random_fp32_and_edges():
     assert fp8_kv.encode_e4m3(edges).tolist() == [0x7E, 0xFE, 0x7F, 0x80, 0x00, 0x02, 0x7E, 0x7E]
 
 
-def test_decode_table_matches_torch():
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_decode_table_matches_torch(fmt):
     codes = np.arange(256, dtype=np.uint8)
-    want = torch.from_numpy(codes).view(torch.float8_e4m3fn).float().numpy()
-    got = fp8_kv.decode_e4m3(codes)
+    want = torch.from_numpy(codes).view(TORCH_DTYPES[fmt]).float().numpy()
+    got = fp8_kv.decode_fp8(codes, fmt)
     nan = np.isnan(want)
     assert np.array_equal(nan, np.isnan(got)) and np.array_equal(got[~nan], want[~nan])
     # every finite code survives encode(decode(code)) unchanged
-    assert np.array_equal(fp8_kv.encode_e4m3(got[~nan]), codes[~nan])
+    finite = np.isfinite(want)
+    assert np.array_equal(fp8_kv.encode_fp8(got[finite], fmt), codes[finite])
 
 
 def test_scatter_oracle_skips_slots_outside_the_capacity():
@@ -50,14 +70,18 @@ def test_scatter_oracle_skips_slots_outside_the_capacity():
 def test_abi_rejects_bad_fp8_arguments_without_a_gpu():
     lib = _lib.load()
     p = 16  # never dereferenced: every call below fails its checks first
-    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 80, 10, 16, 4, 0.1, 0.1, _lib.BF16, None)
+    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 80, 10, 16, 4, 0.1, 0.1, 0, _lib.BF16, None)
     assert rc == _lib.EINVAL and "head_dim" in lib.minikv_last_error().decode()
-    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 128, 10, 16, 4, 0.1, 0.1, _lib.F32, None)
+    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 128, 10, 16, 4, 0.1, 0.1, 0, _lib.F32, None)
     assert rc == _lib.EINVAL and "FP16/BF16" in lib.minikv_last_error().decode()
-    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 128, 10, 16, 4, 0.0, 0.1, _lib.BF16, None)
+    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 128, 10, 16, 4, 0.0, 0.1, 0, _lib.BF16, None)
     assert rc == _lib.EINVAL and "scales" in lib.minikv_last_error().decode()
     assert lib.minikv_paged_decode_fp8_workspace_bytes(2, 8, 4, 80, 10, 16, 4, _lib.BF16) == -1
-    rc = lib.minikv_kv_scatter_slots_fp8(p, p, p, p, p, 4, 8, 4, 3, 5, 15, 15, 0.1, 0.1, _lib.F16, None)
+    rc = lib.minikv_kv_scatter_slots_fp8(p, p, p, p, p, 4, 8, 4, 3, 5, 15, 15, 0.1, 0.1, 1, _lib.F16, None)
     assert rc == _lib.EINVAL and "multiple of 16" in lib.minikv_last_error().decode()
-    rc = lib.minikv_kv_scatter_slots_fp8(p, p, p, p, p, 4, 8, 4, 2, 64, 128, 128, float("inf"), 0.1, _lib.F16, None)
+    rc = lib.minikv_kv_scatter_slots_fp8(p, p, p, p, p, 4, 8, 4, 2, 64, 128, 128, float("inf"), 0.1, 0, _lib.F16, None)
     assert rc == _lib.EINVAL and "scales" in lib.minikv_last_error().decode()
+    rc = lib.minikv_kv_scatter_slots_fp8(p, p, p, p, p, 4, 8, 4, 2, 64, 128, 128, 0.1, 0.1, 2, _lib.F16, None)
+    assert rc == _lib.EINVAL and "E4M3 or E5M2" in lib.minikv_last_error().decode()
+    rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 128, 10, 16, 4, 0.1, 0.1, 5, _lib.BF16, None)
+    assert rc == _lib.EINVAL and "E4M3 or E5M2" in lib.minikv_last_error().decode()

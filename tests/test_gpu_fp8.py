@@ -1,4 +1,4 @@
-"""FP8 (E4M3) KV pool on the GPU against the CPU oracle (oracle/fp8_kv.py).
+"""FP8 (E4M3 / E5M2) KV pool on the GPU against the CPU oracle (oracle/fp8_kv.py).
 
 The quantising scatter must match the oracle byte for byte.  Decode attention
 over an FP8 pool is compared with the fp32 oracle run on the dequantised pool
@@ -20,20 +20,21 @@ TOL = {torch.float16: 2e-3, torch.bfloat16: 1e-2}
 K_SCALE, V_SCALE = 0.0125, 0.0095  # N(0,1) data spans about +-400 codes' worth of range
 
 
-def fp8_pools(c, k_scale=K_SCALE, v_scale=V_SCALE):
+def fp8_pools(c, k_scale=K_SCALE, v_scale=V_SCALE, fmt="e4m3"):
     """The case's 16-bit pools quantised by the oracle (uint8, CPU)."""
-    k = torch.from_numpy(fp8_kv.quantize(c["key_cache"], k_scale))
-    v = torch.from_numpy(fp8_kv.quantize(c["value_cache"], v_scale))
+    k = torch.from_numpy(fp8_kv.quantize(c["key_cache"], k_scale, fmt))
+    v = torch.from_numpy(fp8_kv.quantize(c["value_cache"], v_scale, fmt))
     return k, v
 
 
-def run_both(c, dtype, k_scale=K_SCALE, v_scale=V_SCALE, validate=True, tables=None, lens=None):
-    kq, vq = fp8_pools(c, k_scale, v_scale)
+def run_both(c, dtype, k_scale=K_SCALE, v_scale=V_SCALE, validate=True, tables=None, lens=None, fmt="e4m3"):
+    kq, vq = fp8_pools(c, k_scale, v_scale, fmt)
     tables = c["block_tables"] if tables is None else tables
     lens = c["context_lens"] if lens is None else lens
-    expected = fp8_kv.paged_attention_fp8_fp32(c["query"], kq, vq, tables, lens, c["block_size"], k_scale, v_scale)
+    expected = fp8_kv.paged_attention_fp8_fp32(c["query"], kq, vq, tables, lens, c["block_size"], k_scale, v_scale,
+                                               fmt)
     actual = paged_attention_fp8(c["query"].cuda(), kq.cuda(), vq.cuda(), tables.cuda(), lens.cuda(),
-                                 c["block_size"], k_scale, v_scale, validate=validate)
+                                 c["block_size"], k_scale, v_scale, kv_format=fmt, validate=validate)
     return actual, expected
 
 
@@ -42,8 +43,9 @@ def assert_close(actual, expected_fp32, dtype):
     torch.testing.assert_close(actual.float().cpu(), expected_fp32, atol=tol, rtol=tol)
 
 
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
 @pytest.mark.parametrize("src", [torch.float32, torch.float16, torch.bfloat16])
-def test_quantising_scatter_is_bit_exact(cuda_device, src):
+def test_quantising_scatter_is_bit_exact(cuda_device, src, fmt):
     gen = np.random.default_rng(5)
     blocks, bs, hkv, dim, tokens = 12, 16, 4, 64, 150
     mags = gen.choice([1e-6, 1e-3, 0.05, 1.0, 3.0, 6.0], size=(2, tokens + 8, hkv, dim))
@@ -62,22 +64,25 @@ def test_quantising_scatter_is_bit_exact(cuda_device, src):
     slots[7] = blocks * bs + 5  # outside the capacity: skipped
     init = torch.from_numpy(gen.integers(0, 256, size=(2, blocks, bs, hkv, dim), dtype=np.uint8))
     kc, vc = init[0].clone(), init[1].clone()
-    fp8_kv.scatter_slots_fp8(kc, vc, slots, key.contiguous(), value.contiguous(), K_SCALE, V_SCALE)
+    fp8_kv.scatter_slots_fp8(kc, vc, slots, key.contiguous(), value.contiguous(), K_SCALE, V_SCALE, fmt)
     gk, gv = init[0].cuda(), init[1].cuda()
-    write_kv_cache_slots_fp8(gk, gv, slots.cuda(), key.cuda(), value.cuda(), K_SCALE, V_SCALE, validate=False)
+    write_kv_cache_slots_fp8(gk, gv, slots.cuda(), key.cuda(), value.cuda(), K_SCALE, V_SCALE, kv_format=fmt,
+                             validate=False)
     torch.cuda.synchronize()
     assert torch.equal(gk.cpu(), kc) and torch.equal(gv.cpu(), vc)
     # the float8 dtype view reads back the same values the oracle decodes
-    got = gk.view(torch.float8_e4m3fn).float().cpu().numpy()
-    want = fp8_kv.decode_e4m3(kc.numpy())
+    view = torch.float8_e4m3fn if fmt == "e4m3" else torch.float8_e5m2
+    got = gk.view(view).float().cpu().numpy()
+    want = fp8_kv.decode_fp8(kc.numpy(), fmt)
     assert np.array_equal(np.isnan(got), np.isnan(want)) and np.array_equal(got[~np.isnan(got)], want[~np.isnan(want)])
 
 
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 @pytest.mark.parametrize("dim", [32, 64, 96, 128, 192, 256])
-def test_decode_matches_oracle_on_dequantised_pool(cuda_device, dtype, dim):
+def test_decode_matches_oracle_on_dequantised_pool(cuda_device, dtype, dim, fmt):
     c = cases.decode_case(dtype, head_dim=dim)
-    actual, expected = run_both(c, dtype)
+    actual, expected = run_both(c, dtype, fmt=fmt)
     assert actual.dtype == dtype and actual.shape == c["query"].shape
     assert_close(actual, expected, dtype)
 
@@ -88,8 +93,9 @@ def test_decode_matches_oracle_on_dequantised_pool(cuda_device, dtype, dim):
 ])
 def test_block_partition_and_group_boundaries(cuda_device, block_size, lengths, heads, kv_heads):
     c = cases.decode_case(torch.bfloat16, block_size=block_size, lengths=lengths, heads=heads, kv_heads=kv_heads)
-    actual, expected = run_both(c, torch.bfloat16)
-    assert_close(actual, expected, torch.bfloat16)
+    for fmt in ("e4m3", "e5m2"):
+        actual, expected = run_both(c, torch.bfloat16, fmt=fmt)
+        assert_close(actual, expected, torch.bfloat16)
 
 
 def test_scales_apply_and_equal_the_16bit_decode_of_the_dequantised_pool(cuda_device):
@@ -105,14 +111,15 @@ def test_scales_apply_and_equal_the_16bit_decode_of_the_dequantised_pool(cuda_de
         assert_close(fp8, ref.float().cpu(), torch.float16)
 
 
-def test_trusted_mode_invalid_pages_and_lengths(cuda_device):
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_trusted_mode_invalid_pages_and_lengths(cuda_device, fmt):
     c = cases.decode_case(torch.bfloat16, lengths=(65, 300, 17))
     tables = c["block_tables"].clone()
     tables[0].fill_(-1)
     tables[1, 3] = 1 << 40
     lens = c["context_lens"].clone()
     lens[2] = 10_000
-    actual, expected = run_both(c, torch.bfloat16, validate=False, tables=tables, lens=lens)
+    actual, expected = run_both(c, torch.bfloat16, validate=False, tables=tables, lens=lens, fmt=fmt)
     assert torch.isfinite(actual).all() and not actual[0].any() and not actual[2].any()
     assert_close(actual, expected, torch.bfloat16)
     assert _lib.device_status() == 0
@@ -129,16 +136,19 @@ def test_rejects_unsupported_arguments(cuda_device):
     with pytest.raises(RuntimeError, match="FP16/BF16"):
         paged_attention_fp8(c["query"].cuda(), kq.cuda(), vq.cuda(), c["block_tables"].cuda(),
                             c["context_lens"].cuda(), 16, K_SCALE, V_SCALE)
+    with pytest.raises(ValueError, match="kv_format"):
+        paged_attention_fp8(c["query"].cuda().half(), kq.cuda(), vq.cuda(), c["block_tables"].cuda(),
+                            c["context_lens"].cuda(), 16, K_SCALE, V_SCALE, kv_format="e3m4")
     with pytest.raises(ValueError, match="finite and positive"):
         paged_attention_fp8(c["query"].cuda().half(), kq.cuda(), vq.cuda(), c["block_tables"].cuda(),
                             c["context_lens"].cuda(), 16, 0.0, V_SCALE)
 
 
-@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
-def test_scatter_then_decode_replays_in_a_cuda_graph(cuda_device, dtype):
+@pytest.mark.parametrize("dtype,fmt", [(torch.float16, "e4m3"), (torch.bfloat16, "e5m2")])
+def test_scatter_then_decode_replays_in_a_cuda_graph(cuda_device, dtype, fmt):
     """One captured step: quantise the new tokens into the pool, then decode; replays see new inputs."""
     c = cases.decode_case(dtype, lengths=(40, 255, 517, 3))
-    kq, vq = fp8_pools(c)
+    kq, vq = fp8_pools(c, fmt=fmt)
     gk, gv = kq.cuda(), vq.cuda()
     tables, lens = c["block_tables"].cuda(), c["context_lens"].cuda()
     batch, _, dim = c["query"].shape
@@ -154,12 +164,12 @@ def test_scatter_then_decode_replays_in_a_cuda_graph(cuda_device, dtype):
     stream = torch.cuda.Stream()
     stream.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(stream):
-        paged_attention_fp8(query, gk, gv, tables, lens, 16, K_SCALE, V_SCALE, validate=False)
+        paged_attention_fp8(query, gk, gv, tables, lens, 16, K_SCALE, V_SCALE, kv_format=fmt, validate=False)
     stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        write_kv_cache_slots_fp8(gk, gv, slots, new_k, new_v, K_SCALE, V_SCALE, validate=False)
-        out = paged_attention_fp8(query, gk, gv, tables, lens, 16, K_SCALE, V_SCALE, validate=False)
+        write_kv_cache_slots_fp8(gk, gv, slots, new_k, new_v, K_SCALE, V_SCALE, kv_format=fmt, validate=False)
+        out = paged_attention_fp8(query, gk, gv, tables, lens, 16, K_SCALE, V_SCALE, kv_format=fmt, validate=False)
     for step in range(2):
         new_k.normal_()
         new_v.normal_()
@@ -167,10 +177,10 @@ def test_scatter_then_decode_replays_in_a_cuda_graph(cuda_device, dtype):
         graph.replay()
         torch.cuda.synchronize()
         kc, vc = kq.clone(), vq.clone()
-        fp8_kv.scatter_slots_fp8(kc, vc, slots.cpu(), new_k.cpu(), new_v.cpu(), K_SCALE, V_SCALE)
+        fp8_kv.scatter_slots_fp8(kc, vc, slots.cpu(), new_k.cpu(), new_v.cpu(), K_SCALE, V_SCALE, fmt)
         assert torch.equal(gk.cpu(), kc) and torch.equal(gv.cpu(), vc)
         expected = fp8_kv.paged_attention_fp8_fp32(query.cpu(), kc, vc, c["block_tables"], c["context_lens"], 16,
-                                                   K_SCALE, V_SCALE)
+                                                   K_SCALE, V_SCALE, fmt)
         assert_close(out, expected, dtype)
     assert _lib.device_status() == 0
 
