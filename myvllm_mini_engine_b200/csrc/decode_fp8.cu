@@ -133,6 +133,22 @@ struct Fp8MmaConsumer {
         l[0] = l[1] = 0.f;
     }
 
+    // A lane's K run of one token (KB bytes).  Runs of 32 bytes are read as two
+    // 16-byte halves, odd rows g first the upper one: rows g and g + 1 of a
+    // quarter-warp then hit different banks when rows are unpadded.
+    __device__ __forceinline__ void load_k_run(const unsigned char* p, uint32_t* w) const {
+        if constexpr (KB == 32) {
+            const int first = (g & 1) ? 16 : 0;
+            const uint4 a = *reinterpret_cast<const uint4*>(p + first);
+            const uint4 b = *reinterpret_cast<const uint4*>(p + (16 - first));
+            const uint4 lo = (g & 1) ? b : a, hi = (g & 1) ? a : b;
+            w[0] = lo.x; w[1] = lo.y; w[2] = lo.z; w[3] = lo.w;
+            w[4] = hi.x; w[5] = hi.y; w[6] = hi.z; w[7] = hi.w;
+        } else {
+            load_words<KB, pow2_align(KB)>(p, w);
+        }
+    }
+
     __device__ void tile(const unsigned char* kptr, const unsigned char* vptr, int stride, int TT, int n,
                          uint64_t mask, float scale_log2) {
         // Two 16-token slices per step where the tile allows: their K loads,
@@ -152,8 +168,8 @@ struct Fp8MmaConsumer {
 #pragma unroll
         for (int i = 0; i < NS; ++i) {
             uint32_t kw0[KSTEPS], kw1[KSTEPS];
-            load_words<KB, pow2_align(KB)>(kptr + (sub + 16 * i + g) * stride + q4 * KB, kw0);
-            load_words<KB, pow2_align(KB)>(kptr + (sub + 16 * i + g + 8) * stride + q4 * KB, kw1);
+            load_k_run(kptr + (sub + 16 * i + g) * stride + q4 * KB, kw0);
+            load_k_run(kptr + (sub + 16 * i + g + 8) * stride + q4 * KB, kw1);
 #pragma unroll
             for (int e = 0; e < 4; ++e) s[i][e] = s2[i][e] = 0.f;
 #pragma unroll
