@@ -1,4 +1,4 @@
 from .block_manager import BlockManager, BlockTable
-from .kv_cache import KVCachePool, KVCacheShape
+from .kv_cache import FP8KVCachePool, KVCachePool, KVCacheShape
 
-__all__ = ["BlockManager", "BlockTable", "KVCachePool", "KVCacheShape"]
+__all__ = ["BlockManager", "BlockTable", "FP8KVCachePool", "KVCachePool", "KVCacheShape"]

@@ -199,3 +199,35 @@ def test_runs_across_contiguous_pages(cuda_device, block_size):
     tables[2, 1] = -1
     actual, expected = run_both(c, torch.bfloat16, validate=False, tables=tables)
     assert_close(actual, expected, torch.bfloat16)
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_fp8_pool_range_write_attend_gather_and_copy_on_write(cuda_device, fmt):
+    from myvllm_mini_engine_b200.cache import FP8KVCachePool
+
+    gen = torch.Generator().manual_seed(17)
+    layers, blocks, bs, hkv, dim = 2, 24, 16, 4, 64
+    pool = FP8KVCachePool(layers, blocks, bs, hkv, dim, k_scale=K_SCALE, v_scale=V_SCALE, kv_format=fmt)
+    ids, offset, tokens = [5, 17, 2, 9], 3, 50
+    key = torch.randn(tokens, hkv, dim, generator=gen).to(torch.bfloat16)
+    value = torch.randn(tokens, hkv, dim, generator=gen).to(torch.bfloat16)
+    pool.write_cuda(1, ids, offset, key.cuda(), value.cuda())
+    positions = torch.arange(tokens) + offset
+    slots = torch.tensor(ids)[positions // bs] * bs + positions % bs
+    kc = torch.zeros(blocks, bs, hkv, dim, dtype=torch.uint8)
+    vc = torch.zeros_like(kc)
+    fp8_kv.scatter_slots_fp8(kc, vc, slots, key, value, K_SCALE, V_SCALE, fmt)
+    assert torch.equal(pool.key[1].cpu(), kc) and torch.equal(pool.value[1].cpu(), vc)
+    assert not pool.key[0].any() and not pool.value[0].any()
+    k_rows, v_rows = pool.gather(1, ids, offset + tokens)
+    assert torch.equal(k_rows[offset:].cpu(), fp8_kv.dequantize(kc.view(-1, hkv, dim)[slots], K_SCALE, fmt))
+    assert torch.equal(v_rows[offset:].cpu(), fp8_kv.dequantize(vc.view(-1, hkv, dim)[slots], V_SCALE, fmt))
+    query = torch.randn(2, 8, dim, generator=gen).to(torch.bfloat16)
+    tables = torch.tensor([ids, ids], dtype=torch.int64)
+    lens = torch.tensor([offset + tokens, 20], dtype=torch.int64)
+    out = pool.attend(1, query.cuda(), tables.cuda(), lens.cuda())
+    expected = fp8_kv.paged_attention_fp8_fp32(query, kc, vc, tables, lens, bs, K_SCALE, V_SCALE, fmt)
+    assert_close(out, expected, torch.bfloat16)
+    pool.copy_blocks([(17, 20)])
+    torch.cuda.synchronize()
+    assert torch.equal(pool.key[:, 20], pool.key[:, 17]) and torch.equal(pool.value[:, 20], pool.value[:, 17])
