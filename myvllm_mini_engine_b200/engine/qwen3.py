@@ -47,7 +47,8 @@ import torch
 from torch.nn import functional as F
 
 from .. import _lib
-from ..cache.kv_cache import KVCachePool
+from ..cache.kv_cache import FP8KVCachePool, KVCachePool
+from ..kernels.fp8 import paged_attention_fp8, write_kv_cache_slots_fp8
 from ..kernels.paged import paged_attention
 
 
@@ -166,7 +167,10 @@ class Qwen3DecodeStep:
     """One decode token per request through all layers, reading and appending the paged pool.
 
     ``pool`` is a :class:`KVCachePool` shaped for ``config`` (layers, kv heads,
-    head_dim) in the weights' dtype and device.  ``forward_decode_batch``
+    head_dim) in the weights' dtype and device, or an :class:`FP8KVCachePool`
+    (an extension: the new token's K/V are written by the same kernels into a
+    small bf16 staging buffer, then quantised into the pool by the FP8 slot
+    scatter, and the attention reads the FP8 pool).  ``forward_decode_batch``
     follows ``NativeQwen3.forward_decode_batch`` (native_qwen3.py:423-456):
     it returns the logits ``[B, vocab]`` and appends each request's new K/V at
     ``positions[b]`` through ``block_tables[b]``.
@@ -181,7 +185,8 @@ class Qwen3DecodeStep:
         if (shape.num_layers, shape.num_kv_heads, shape.head_dim) != (
                 config.num_hidden_layers, config.num_key_value_heads, config.head_dim):
             raise ValueError("KV cache architecture mismatch")
-        if pool.key.device != weights.embed.device or pool.dtype != weights.embed.dtype:
+        self.fp8 = isinstance(pool, FP8KVCachePool)
+        if pool.key.device != weights.embed.device or (not self.fp8 and pool.dtype != weights.embed.dtype):
             raise ValueError("cache must match model device and dtype")
         if weights.embed.dtype not in (torch.float16, torch.bfloat16):
             raise ValueError("the decode step runs in FP16/BF16")
@@ -239,6 +244,8 @@ class Qwen3DecodeStep:
         hq, hkv, dim = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         shape = pool.shape
         stream = torch.cuda.current_stream(device).cuda_stream
+        if self.fp8:
+            self._fp8_begin(batch, block_tables, positions)
         if self.fused_projections and batch <= self.FUSED_MAX_BATCH:
             return self._forward_fused(input_ids, block_tables, positions, stream)
         x = F.embedding(input_ids, w.embed)
@@ -252,14 +259,12 @@ class Qwen3DecodeStep:
         for index, layer in enumerate(w.layers):
             qkv = torch.mm(h, layer.qkv.t())
             q = torch.empty((batch, hq, dim), dtype=x.dtype, device=device)
+            kc, vc, tables, pos, blocks, bs, width = self._append_target(index, block_tables, positions)
             _check(self.lib.minikv_qk_rope_append(
                 qkv.data_ptr(), qkv.stride(0), layer.q_norm.data_ptr(), layer.k_norm.data_ptr(), cos.data_ptr(),
-                sin.data_ptr(), q.data_ptr(), pool.key[index].data_ptr(), pool.value[index].data_ptr(),
-                block_tables.data_ptr(), positions.data_ptr(), batch, hq, hkv, dim, shape.num_blocks,
-                shape.block_size, block_tables.shape[1], cfg.rms_norm_eps, self.code, stream), "qk_rope_append")
-            # lengths and tables predate the append kernel just launched: chained decode
-            attention = paged_attention(q, pool.key[index], pool.value[index], block_tables, lengths,
-                                        shape.block_size, validate=False, chained=True)
+                sin.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), tables.data_ptr(), pos.data_ptr(),
+                batch, hq, hkv, dim, blocks, bs, width, cfg.rms_norm_eps, self.code, stream), "qk_rope_append")
+            attention = self._attend(index, q, block_tables, lengths)
             o = torch.mm(attention.view(batch, hq * dim), layer.o.t())
             summed, normalized = torch.empty_like(x), torch.empty_like(x)
             self._rms(o, residual, layer.post_norm, normalized, summed, stream)
@@ -295,14 +300,13 @@ class Qwen3DecodeStep:
                 source, ss_in, norm = h, None, None
             else:
                 source, ss_in, norm = residual, sums.data_ptr(), layer.input_norm.data_ptr()
+            kc, vc, tables, pos, blocks, bs, width = self._append_target(index, block_tables, positions)
             _check(lib.minikv_linear_qk_rope_append(
                 source.data_ptr(), source.stride(0), ss_in, norm, eps, qkv_w.data_ptr(),
                 layer.q_norm.data_ptr(), layer.k_norm.data_ptr(), cos.data_ptr(), sin.data_ptr(), q.data_ptr(),
-                pool.key[index].data_ptr(), pool.value[index].data_ptr(), block_tables.data_ptr(),
-                positions.data_ptr(), batch, hidden, hq, hkv, dim, shape.num_blocks, shape.block_size,
-                block_tables.shape[1], code, stream), "linear_qk_rope_append")
-            attention = paged_attention(q, pool.key[index], pool.value[index], block_tables, lengths,
-                                        shape.block_size, validate=False, chained=True)
+                kc.data_ptr(), vc.data_ptr(), tables.data_ptr(), pos.data_ptr(), batch, hidden, hq, hkv, dim,
+                blocks, bs, width, code, stream), "linear_qk_rope_append")
+            attention = self._attend(index, q, block_tables, lengths)
             summed = torch.empty_like(x)
             summed_sums = torch.empty((hidden // 128, batch), dtype=torch.float32, device=device)
             _check(lib.minikv_linear_residual(
@@ -320,6 +324,43 @@ class Qwen3DecodeStep:
         h = torch.empty_like(x)
         self._rms(residual, None, w.norm, h, None, stream)
         return torch.mm(h, w.lm_head.t())
+
+    # ------------------------------------------------------ KV pool access
+    def _fp8_begin(self, batch, block_tables, positions):
+        """Per-step state of the FP8 pool: the staging rows and each request's slot (device ops only)."""
+        cfg, bs = self.config, self.pool.shape.block_size
+        device = positions.device
+        shape = (batch, 1, cfg.num_key_value_heads, cfg.head_dim)
+        self._stage_k = torch.empty(shape, dtype=self.weights.embed.dtype, device=device)
+        self._stage_v = torch.empty_like(self._stage_k)
+        self._stage_tables = torch.arange(batch, dtype=torch.long, device=device).view(batch, 1)
+        self._stage_pos = torch.zeros(batch, dtype=torch.long, device=device)
+        page = block_tables.gather(1, (positions // bs).view(-1, 1)).view(-1)
+        self._slots = (page * bs + positions % bs).contiguous()
+
+    def _append_target(self, index, block_tables, positions):
+        """Where the append kernels write the new token's K/V: the pool, or the FP8 path's staging rows."""
+        shape = self.pool.shape
+        if not self.fp8:
+            return (self.pool.key[index], self.pool.value[index], block_tables, positions, shape.num_blocks,
+                    shape.block_size, block_tables.shape[1])
+        # staging "pool": one 1-token page per request (page b, offset 0)
+        return (self._stage_k, self._stage_v, self._stage_tables, self._stage_pos, self._stage_k.shape[0], 1, 1)
+
+    def _attend(self, index, q, block_tables, lengths):
+        pool = self.pool
+        if not self.fp8:
+            # lengths and tables predate the append kernel just launched: chained decode
+            return paged_attention(q, pool.key[index], pool.value[index], block_tables, lengths,
+                                   pool.shape.block_size, validate=False, chained=True)
+        batch = q.shape[0]
+        rows = (batch, self.config.num_key_value_heads, self.config.head_dim)
+        write_kv_cache_slots_fp8(pool.key[index], pool.value[index], self._slots, self._stage_k.view(rows),
+                                 self._stage_v.view(rows), pool.k_scale, pool.v_scale, kv_format=pool.kv_format,
+                                 validate=False)
+        return paged_attention_fp8(q, pool.key[index], pool.value[index], block_tables, lengths,
+                                   pool.shape.block_size, pool.k_scale, pool.v_scale, kv_format=pool.kv_format,
+                                   validate=False)
 
     def greedy(self, input_ids, block_tables, positions):
         """Greedy next token of every request (argmax of the step's logits)."""
