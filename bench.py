@@ -668,10 +668,12 @@ def run_qwen3_reference(args, world, rank):
 
 def run_qwen3(args, world, rank, local):
     from myvllm_mini_engine_b200 import _lib
-    from myvllm_mini_engine_b200.cache.kv_cache import KVCachePool
+    from myvllm_mini_engine_b200.cache.kv_cache import FP8KVCachePool, KVCachePool
     from myvllm_mini_engine_b200.engine.qwen3 import DecodeGraph, Qwen3DecodeStep, Qwen3Weights
-    from myvllm_mini_engine_b200.kernels import paged_attention
+    from myvllm_mini_engine_b200.kernels import paged_attention, paged_attention_fp8
 
+    fmt = {"fp8": "e4m3", "fp8_e5m2": "e5m2"}.get(args.kv_dtype)  # None: bf16 pool
+    kv_es = 1 if fmt else 2
     if args.batch % world:
         raise SystemExit(f"--batch {args.batch} does not split over {world} GPUs")
     device = torch.device("cuda", local)
@@ -679,18 +681,29 @@ def run_qwen3(args, world, rank, local):
     batch = args.batch // world
     pages = math.ceil((args.context + 1) / BS)
     blocks = batch * pages
-    pool_bytes = 2 * cfg.num_hidden_layers * blocks * BS * cfg.num_key_value_heads * cfg.head_dim * 2
+    pool_bytes = 2 * cfg.num_hidden_layers * blocks * BS * cfg.num_key_value_heads * cfg.head_dim * kv_es
     free, _ = torch.cuda.mem_get_info(device)
     if pool_bytes + (4 << 30) > free:
         raise SystemExit(f"KV pool of {pool_bytes / 1e9:.1f} GB does not fit the {free / 1e9:.1f} GB free on "
                          f"GPU {local}")
     weights = Qwen3Weights.random(cfg, dtype=torch.bfloat16, device=device, seed=QWEN3_SEED)
-    pool = KVCachePool(cfg.num_hidden_layers, blocks, BS, cfg.num_key_value_heads, cfg.head_dim,
-                       dtype=torch.bfloat16, device=device)
     gen = torch.Generator(device=device).manual_seed(QWEN3_SEED + 1 + rank)
-    for layer in range(cfg.num_hidden_layers):
-        pool.key[layer].normal_(generator=gen)
-        pool.value[layer].normal_(generator=gen)
+    if fmt:
+        # FP8 pool: N(0,1) history quantised by the pool's own scatter (scale 1/32: |x| < 14 fits E4M3)
+        pool = FP8KVCachePool(cfg.num_hidden_layers, blocks, BS, cfg.num_key_value_heads, cfg.head_dim,
+                              k_scale=1 / 32, v_scale=1 / 32, kv_format=fmt, device=device)
+        rows = torch.empty(blocks * BS, cfg.num_key_value_heads, cfg.head_dim, dtype=torch.bfloat16, device=device)
+        slots = torch.arange(blocks * BS, device=device)
+        for layer in range(cfg.num_hidden_layers):
+            rows.normal_(generator=gen)
+            pool.write_slots(layer, slots, rows, rows.flip(0), validate=False)
+        del rows, slots
+    else:
+        pool = KVCachePool(cfg.num_hidden_layers, blocks, BS, cfg.num_key_value_heads, cfg.head_dim,
+                           dtype=torch.bfloat16, device=device)
+        for layer in range(cfg.num_hidden_layers):
+            pool.key[layer].normal_(generator=gen)
+            pool.value[layer].normal_(generator=gen)
     tables = qwen3_tables(batch, pages, device, QWEN3_SEED + 100 + rank)
     ids = torch.randint(0, cfg.vocab_size, (batch,), device=device, generator=gen)
     positions = torch.full((batch,), args.context, dtype=torch.int64, device=device)
@@ -727,18 +740,24 @@ def run_qwen3(args, world, rank, local):
 
     # the dominant kernel alone: paged decode over this rank's batch, one launch per layer, graph-replayed
     lengths = [args.context + 1] * batch
-    launch_bytes = decode_bytes(lengths, batch)
+    launch_bytes = kv_bytes(lengths, kv_es) + 2 * batch * HQ * D * 2 + 8 * sum(math.ceil(n / BS) for n in lengths)
     q = torch.randn(batch, HQ, D, device=device, dtype=torch.bfloat16, generator=gen)
     lens = positions + 1
+
+    def attend(layer):
+        if fmt:
+            return pool.attend(layer, q, tables, lens, validate=False)
+        return paged_attention(q, pool.key[layer], pool.value[layer], tables, lens, BS, validate=False)
+
     side = torch.cuda.Stream(device)
     side.wait_stream(stream)
     with torch.cuda.stream(side):
-        paged_attention(q, pool.key[0], pool.value[0], tables, lens, BS, validate=False)
+        attend(0)
     side.synchronize()
     decode_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(decode_graph, stream=side):
         for layer in range(cfg.num_hidden_layers):
-            paged_attention(q, pool.key[layer], pool.value[layer], tables, lens, BS, validate=False)
+            attend(layer)
     decode_graph.replay()
     torch.cuda.synchronize(device)
     d_start, d_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -778,9 +797,12 @@ def run_qwen3(args, world, rank, local):
     del graph, decode_graph
     if rank != 0:
         return None
-    step_bytes = cfg.num_hidden_layers * (launch_bytes + 2 * batch * HKV * D * 2) + qwen3_weight_bytes(cfg)
+    step_bytes = cfg.num_hidden_layers * (launch_bytes + 2 * batch * HKV * D * kv_es) + qwen3_weight_bytes(cfg)
     line = qwen3_line_base(args, world, f"request-sharded x{world} ({batch} requests and an independent KV "
                                         f"pool per GPU, weights replicated, no collective)")
+    line["config"]["kv_pool"] = fmt or "bf16"
+    if fmt:
+        line["dtype"] = f"bf16 compute, {fmt} KV pool (scales 1/32)"
     line.update({
         "value": args.batch / (ms_per_step * 1e-3), "ms_per_step": ms_per_step,
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
