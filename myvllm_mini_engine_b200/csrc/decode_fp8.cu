@@ -182,6 +182,17 @@ struct Fp8MmaConsumer {
                 Mma::mma((kk & 1) ? s2[i] : s[i], a, qb[kk][0], qb[kk][1]);
             }
         }
+        // V words of every slice, loaded before the softmax so their latency overlaps it:
+        // lane (g, q4) reads dims g*D/8 .. +D/8 of tokens 2q4, 2q4+1, 2q4+8, 2q4+9
+        uint32_t vw[NS][4][GROUPS];
+#pragma unroll
+        for (int i = 0; i < NS; ++i) {
+            const unsigned char* v0 = vptr + (sub + 16 * i + 2 * q4) * stride + g * VB;
+            load_words<VB, pow2_align(VB)>(v0, vw[i][0]);
+            load_words<VB, pow2_align(VB)>(v0 + stride, vw[i][1]);
+            load_words<VB, pow2_align(VB)>(v0 + 8 * stride, vw[i][2]);
+            load_words<VB, pow2_align(VB)>(v0 + 9 * stride, vw[i][3]);
+        }
         // ---- mask and scale (as decode_mma.cu; the key scale is in scale_log2)
 #pragma unroll
         for (int i = 0; i < NS; ++i) {
@@ -248,16 +259,10 @@ struct Fp8MmaConsumer {
             const uint32_t b1 = pick_halves(__shfl_sync(0xffffffffu, h23, src0), __shfl_sync(0xffffffffu, h23, src1), odd);
             const uint32_t c0 = pick_halves(__shfl_sync(0xffffffffu, l01, src0), __shfl_sync(0xffffffffu, l01, src1), odd);
             const uint32_t c1 = pick_halves(__shfl_sync(0xffffffffu, l23, src0), __shfl_sync(0xffffffffu, l23, src1), odd);
-            // ---- O^T += V^T P^T: lane (g, q4) reads dims g*D/8 .. +D/8 of tokens 2q4, 2q4+1, 2q4+8, 2q4+9
-            uint32_t vw[4][GROUPS];
-            const unsigned char* v0 = vptr + (sub + 16 * i + 2 * q4) * stride + g * VB;
-            load_words<VB, pow2_align(VB)>(v0, vw[0]);
-            load_words<VB, pow2_align(VB)>(v0 + stride, vw[1]);
-            load_words<VB, pow2_align(VB)>(v0 + 8 * stride, vw[2]);
-            load_words<VB, pow2_align(VB)>(v0 + 9 * stride, vw[3]);
+            // ---- O^T += V^T P^T
 #pragma unroll
             for (int u = 0; u < GROUPS; ++u) {
-                const uint32_t w0 = vw[0][u], w1 = vw[1][u], w2 = vw[2][u], w3 = vw[3][u];
+                const uint32_t w0 = vw[i][0][u], w1 = vw[i][1][u], w2 = vw[i][2][u], w3 = vw[i][3][u];
                 // byte i of word u is dim g*D/8 + 4u + i; pair the two tokens of each k slot
                 const uint32_t x01 = byte_perm(w0, w1, 0x5140u), x23 = byte_perm(w2, w3, 0x5140u);  // dims +0, +1
                 const uint32_t y01 = byte_perm(w0, w1, 0x7362u), y23 = byte_perm(w2, w3, 0x7362u);  // dims +2, +3
