@@ -1,13 +1,14 @@
-// FP8 (e4m3) KV pool: the quantising slot scatter and the tensor-core
-// consumer of the split-KV decode kernel for one-byte K/V rows.
+// FP8 KV pool (E4M3 or E5M2): the quantising slot scatter and the
+// tensor-core consumer of the split-KV decode kernel for one-byte K/V rows.
 //
 // Format.  The pool has the 16-bit pool's shape, [num_blocks, block_size,
-// kv_heads, head_dim], one OCP FP8 byte per element (E4M3, or E5M2), with one
+// kv_heads, head_dim], one OCP FP8 byte per element (E4M3 or E5M2), with one
 // fp32 scale for keys and one for values: stored = fp8_rn_satfinite(x * (1 /
-// scale)), read back as stored * scale.  It halves the bytes a decode step streams.  The
-// reference has no FP8 pool (it is listed there as future work); the write
-// follows its slot-scatter contract (mini_engine/kernels/csrc/data.cu:196-206:
-// a slot outside the capacity writes nothing).
+// scale)), read back as stored * scale.  It halves the bytes a decode step
+// streams.  The reference has no FP8 pool (it is listed there as future
+// work); the write follows its slot-scatter contract
+// (mini_engine/kernels/csrc/data.cu:196-206: a slot outside the capacity
+// writes nothing).
 //
 // Decode.  The producer warp and the ticketed merge of decode.cu are reused.
 // When one CTA holds every kv head (the usual case: a token's row is then
@@ -15,10 +16,10 @@
 // staged unpadded and the producer issues one bulk copy per run of
 // consecutive physical rows, a page or more, instead of one per token: per
 // token copies of 1 KB rows held the loop at about half the HBM rate.  The
-// consumer converts
-// K and V to fp16 in registers (two e4m3 bytes -> one f16x2 per cvt, exact:
-// every e4m3 value is an fp16 normal or zero) and runs the same transposed
-// mma.sync scheme as decode_mma.cu in fp16:
+// consumer converts K and V to fp16 in registers, exactly: an E4M3 pair with
+// one cvt (every E4M3 value is an fp16 normal or zero), an E5M2 pair with one
+// byte permute (an E5M2 byte is the high byte of the fp16 of its value).  It
+// then runs the transposed mma.sync scheme of decode_mma.cu in fp16:
 //   S^T = K Q^T    with Q rounded to fp16 (saturated at +-65504) once per segment;
 //   O^T += V^T P^T with P split into fp16 hi + lo terms.
 // The key scale is folded into the softmax scale and the value scale into the
@@ -29,9 +30,9 @@
 // For V^T (the A operand, dims as rows), a lane loads dims g*D/8 .. +D/8 of
 // each of its 4 tokens and pairs the tokens with byte permutes; word w of
 // that run feeds m-tiles 2w (rows g, g+8 = dims g*D/8 + 4w + 0, 1) and 2w + 1
-// (dims + 2, 3).  Rows are staged unpadded when the producer copies runs of
-// whole rows (the CTA holds every kv head); the vector loads then meet 2-way
-// (K) and 4-way (V) bank conflicts.
+// (dims + 2, 3).  On unpadded rows, K reads are conflict-free (odd rows read
+// their two 16-byte halves in swapped order) and V reads meet 4-way bank
+// conflicts.
 #include <cuda_fp8.h>
 
 #include "common.cuh"
