@@ -85,3 +85,34 @@ def test_abi_rejects_bad_fp8_arguments_without_a_gpu():
     assert rc == _lib.EINVAL and "E4M3 or E5M2" in lib.minikv_last_error().decode()
     rc = lib.minikv_paged_decode_fp8(p, p, p, p, p, p, p, 1 << 20, 2, 8, 4, 128, 10, 16, 4, 0.1, 0.1, 5, _lib.BF16, None)
     assert rc == _lib.EINVAL and "E4M3 or E5M2" in lib.minikv_last_error().decode()
+
+
+def test_fp8_pool_and_wrappers_validate_arguments_on_the_host():
+    from myvllm_mini_engine_b200.cache import FP8KVCachePool
+    from myvllm_mini_engine_b200.kernels import paged_attention_fp8, write_kv_cache_slots_fp8
+
+    with pytest.raises(ValueError, match="kv_format"):
+        FP8KVCachePool(1, 4, 16, 2, 64, k_scale=0.1, v_scale=0.1, kv_format="e3m4", device="cpu")
+    with pytest.raises(ValueError, match="finite and positive"):
+        FP8KVCachePool(1, 4, 16, 2, 64, k_scale=0.0, v_scale=0.1, device="cpu")
+    with pytest.raises(ValueError, match="even head_dim"):
+        FP8KVCachePool(1, 4, 16, 2, 63, k_scale=0.1, v_scale=0.1, device="cpu")
+    pool = FP8KVCachePool(2, 4, 16, 2, 64, k_scale=0.1, v_scale=0.1, kv_format="e5m2", device="cpu")
+    assert pool.memory_bytes == 2 * 2 * 4 * 16 * 2 * 64 and pool.key.dtype == torch.uint8
+    rows = torch.zeros(3, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(IndexError, match="layer"):
+        pool.write_cuda(2, [0], 0, rows, rows)
+    with pytest.raises(IndexError, match="block id"):
+        pool.write_cuda(0, [7], 0, rows, rows)
+    with pytest.raises(ValueError, match="capacity"):
+        pool.write_cuda(0, [0], 15, rows, rows)
+    with pytest.raises(ValueError, match="CUDA"):  # no CPU path
+        pool.write_slots(0, torch.arange(3), rows, rows)
+    kc = torch.zeros(4, 16, 2, 64, dtype=torch.uint8)
+    with pytest.raises(ValueError, match="uint8 or a float8"):
+        write_kv_cache_slots_fp8(kc.float(), kc.float(), torch.arange(3), rows, rows, 0.1, 0.1)
+    with pytest.raises(ValueError, match="FP32/FP16/BF16"):
+        write_kv_cache_slots_fp8(kc, kc.clone(), torch.arange(3), rows.to(torch.int32), rows.to(torch.int32), 0.1, 0.1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        paged_attention_fp8(torch.zeros(1, 4, 64, dtype=torch.bfloat16), kc, kc, torch.zeros(1, 1, dtype=torch.int64),
+                            torch.ones(1, dtype=torch.int64), 16, 0.1, 0.1)
