@@ -16,9 +16,10 @@
 // staged unpadded and the producer issues one bulk copy per run of
 // consecutive physical rows, a page or more, instead of one per token: per
 // token copies of 1 KB rows held the loop at about half the HBM rate.  The
-// consumer converts K and V to fp16 in registers, exactly: an E4M3 pair with
-// one cvt (every E4M3 value is an fp16 normal or zero), an E5M2 pair with one
-// byte permute (an E5M2 byte is the high byte of the fp16 of its value).  It
+// consumer converts K and V to fp16 in registers, exactly: an E4M3 K pair with
+// one cvt (every E4M3 value is an fp16 normal or zero), an E4M3 V pair with
+// integer ops (see Fp8Codec), an E5M2 pair with one byte permute (an E5M2
+// byte is the high byte of the fp16 of its value).  It
 // then runs the transposed mma.sync scheme of decode_mma.cu in fp16:
 //   S^T = K Q^T    with Q rounded to fp16 (saturated at +-65504) once per segment;
 //   O^T += V^T P^T with P split into fp16 hi + lo terms.
@@ -78,14 +79,33 @@ constexpr int pow2_align(int bytes) { return (bytes % 16 == 0) ? 16 : (bytes % 8
 // Pairs of fp8 codes to f16x2 for the two formats.  E4M3: the hardware
 // conversion (exact).  E5M2: an E5M2 byte is the high byte of the fp16 of the
 // same value, so a byte permute is the conversion (exact, ALU only).
+//
+// For V, E4M3 uses integer ops instead, so that K's conversions and V's run on
+// two pipes (XU and ALU): a code s.eeee.mmm placed as fp16 bits
+// s.0eeee.mmm0000000 is the fp16 of its value times 2^-8, for normals and
+// subnormals alike (fp16 has 8 more exponent bias and room for every E4M3
+// subnormal).  vlo/vhi return that; kVScale is the factor the output is
+// multiplied back by.
+__device__ __forceinline__ uint32_t e4m3x2_to_h2_scaled(uint32_t spread) {
+    // spread = code0 << 8 | code1 << 24: shift the magnitudes into place, then move
+    // the sign from bit 14 (30) to 15 (31) by adding the bit to itself
+    const uint32_t t = spread >> 1;
+    return t + (t & 0x40004000u);
+}
 template <bool E5M2> struct Fp8Codec;
 template <> struct Fp8Codec<false> {
     __device__ static __forceinline__ uint32_t lo(uint32_t w) { return e4m3x2_to_h2(w); }        // bytes 0, 1
     __device__ static __forceinline__ uint32_t hi(uint32_t w) { return e4m3x2_to_h2(w >> 16); }  // bytes 2, 3
+    __device__ static __forceinline__ uint32_t vlo(uint32_t w) { return e4m3x2_to_h2_scaled(byte_perm(w, 0u, 0x1404u)); }
+    __device__ static __forceinline__ uint32_t vhi(uint32_t w) { return e4m3x2_to_h2_scaled(byte_perm(w, 0u, 0x3424u)); }
+    static constexpr float kVScale = 256.f;
 };
 template <> struct Fp8Codec<true> {
     __device__ static __forceinline__ uint32_t lo(uint32_t w) { return byte_perm(w, 0u, 0x1404u); }
     __device__ static __forceinline__ uint32_t hi(uint32_t w) { return byte_perm(w, 0u, 0x3424u); }
+    __device__ static __forceinline__ uint32_t vlo(uint32_t w) { return lo(w); }
+    __device__ static __forceinline__ uint32_t vhi(uint32_t w) { return hi(w); }
+    static constexpr float kVScale = 1.f;
 };
 
 // fp16 pair of two floats, saturated to the finite fp16 range.
@@ -268,16 +288,16 @@ struct Fp8MmaConsumer {
                 const uint32_t x01 = byte_perm(w0, w1, 0x5140u), x23 = byte_perm(w2, w3, 0x5140u);  // dims +0, +1
                 const uint32_t y01 = byte_perm(w0, w1, 0x7362u), y23 = byte_perm(w2, w3, 0x7362u);  // dims +2, +3
                 uint32_t a[4];
-                a[0] = Codec::lo(x01);
-                a[1] = Codec::hi(x01);
-                a[2] = Codec::lo(x23);
-                a[3] = Codec::hi(x23);
+                a[0] = Codec::vlo(x01);
+                a[1] = Codec::vhi(x01);
+                a[2] = Codec::vlo(x23);
+                a[3] = Codec::vhi(x23);
                 Mma::mma(o[2 * u], a, c0, c1);
                 Mma::mma(o[2 * u], a, b0, b1);
-                a[0] = Codec::lo(y01);
-                a[1] = Codec::hi(y01);
-                a[2] = Codec::lo(y23);
-                a[3] = Codec::hi(y23);
+                a[0] = Codec::vlo(y01);
+                a[1] = Codec::vhi(y01);
+                a[2] = Codec::vlo(y23);
+                a[3] = Codec::vhi(y23);
                 Mma::mma(o[2 * u + 1], a, c0, c1);
                 Mma::mma(o[2 * u + 1], a, b0, b1);
             }
@@ -294,7 +314,7 @@ struct Fp8MmaConsumer {
             const int head = 2 * q4 + h;
             if (head >= item_heads) continue;
             const int qh = qh0 + head;
-            const float inv = (L > 0.f) ? p.out_scale / L : 0.f;  // the value scale folded in
+            const float inv = (L > 0.f) ? p.out_scale * Codec::kVScale / L : 0.f;  // the value scale folded in
             if (final_row) {
                 T* orow = static_cast<T*>(p.out) + ((int64_t)b * p.q_heads + qh) * D;
 #pragma unroll
