@@ -162,6 +162,22 @@ int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void
                             int64_t table_width, float k_scale, float v_scale, int fp8_format, int dtype,
                             void* stream);
 
+/* Ragged causal paged prefill over an FP8 pool: minikv_paged_prefill's
+ * contract (arguments, guards, packed [tokens, q_heads, head_dim] query and
+ * output) with fp16/bf16 query/output (`dtype`), K/V read as code * scale.
+ * Runs the CUDA-core route (one decode row per query token, fp8 consumer).
+ * The workspace has its own size query (no zero fill needed). */
+int64_t minikv_paged_prefill_fp8_workspace_bytes(int64_t tokens, int64_t requests, int64_t q_heads,
+                                                 int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
+                                                 int64_t block_size, int64_t table_width, int64_t max_query_len,
+                                                 int dtype);
+int minikv_paged_prefill_fp8(const void* q, const void* key_cache, const void* value_cache,
+                             const int64_t* cu_seqlens_q, const int64_t* query_starts, const int64_t* block_tables,
+                             const int64_t* context_lens, void* out, void* workspace, int64_t workspace_bytes,
+                             int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                             int64_t num_blocks, int64_t block_size, int64_t table_width, int64_t max_query_len,
+                             float k_scale, float v_scale, int fp8_format, int dtype, void* stream);
+
 /* Decode append: request r writes its token at logical position
  * token_offsets[r] through block_tables[r]; rows whose page index or physical
  * page is out of range are skipped.  Replaces write_kv_cache_batch_cuda

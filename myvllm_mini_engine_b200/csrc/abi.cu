@@ -385,6 +385,53 @@ int minikv_paged_prefill(const void* q, const void* key_cache, const void* value
                        max_query_len, dtype, static_cast<cudaStream_t>(stream));
 }
 
+int64_t minikv_paged_prefill_fp8_workspace_bytes(int64_t tokens, int64_t requests, int64_t q_heads,
+                                                 int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
+                                                 int64_t block_size, int64_t table_width, int64_t max_query_len,
+                                                 int dtype) {
+    (void)max_query_len;
+    if (check_prefill(tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype))
+        return -1;
+    if ((dtype != MINIKV_F16 && dtype != MINIKV_BF16) || !fp8_head_dim(head_dim)) return -1;
+    return prefill_fp8_workspace_bytes(tokens, q_heads, kv_heads, head_dim, block_size, table_width, dtype,
+                                       sm_count());
+}
+
+int minikv_paged_prefill_fp8(const void* q, const void* key_cache, const void* value_cache,
+                             const int64_t* cu_seqlens_q, const int64_t* query_starts, const int64_t* block_tables,
+                             const int64_t* context_lens, void* out, void* workspace, int64_t workspace_bytes,
+                             int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                             int64_t num_blocks, int64_t block_size, int64_t table_width, int64_t max_query_len,
+                             float k_scale, float v_scale, int fp8_format, int dtype, void* stream) {
+    (void)max_query_len;
+    MINIKV_REQUIRE(fp8_format == MINIKV_FP8_E4M3 || fp8_format == MINIKV_FP8_E5M2, MINIKV_EINVAL,
+                   "fp8 format must be E4M3 or E5M2");
+    int rc = check_prefill(tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width,
+                           dtype);
+    if (rc) return rc;
+    MINIKV_REQUIRE(dtype == MINIKV_F16 || dtype == MINIKV_BF16, MINIKV_EINVAL,
+                   "an fp8 KV pool needs an FP16/BF16 query");
+    MINIKV_REQUIRE(fp8_head_dim(head_dim), MINIKV_EINVAL, "fp8 KV pool: supported head_dim: 32,64,96,128,192,256");
+    MINIKV_REQUIRE(valid_scale(k_scale) && valid_scale(v_scale), MINIKV_EINVAL,
+                   "fp8 KV scales must be finite and positive");
+    if (tokens == 0) return MINIKV_OK;
+    MINIKV_REQUIRE(requests > 0 && table_width > 0, MINIKV_EINVAL, "paged prefill metadata shape mismatch");
+    MINIKV_REQUIRE(q && key_cache && value_cache && cu_seqlens_q && query_starts && block_tables && context_lens &&
+                       out,
+                   MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(q) && aligned16(key_cache) && aligned16(value_cache) && aligned16(out), MINIKV_EINVAL,
+                   "paged prefill tensors must be 16-byte aligned");
+    const int64_t need = prefill_fp8_workspace_bytes(tokens, q_heads, kv_heads, head_dim, block_size, table_width,
+                                                     dtype, sm_count());
+    MINIKV_REQUIRE(need >= 0, MINIKV_EUNSUPPORTED, "paged prefill shape does not fit shared memory");
+    MINIKV_REQUIRE(workspace_bytes >= need && workspace && aligned16(workspace), MINIKV_EINVAL,
+                   "paged prefill workspace too small or misaligned");
+    return run_prefill_fp8(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens, out,
+                           workspace, tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size,
+                           table_width, k_scale, v_scale, fp8_format == MINIKV_FP8_E5M2, dtype,
+                           static_cast<cudaStream_t>(stream));
+}
+
 // ----------------------------------------------------------------- metadata
 int minikv_build_prefill_metadata(const int64_t* query_starts, const int64_t* cu_seqlens_q, const int64_t* cu_blocks,
                                   const int64_t* block_ids, const int64_t* token_ids, int64_t requests,

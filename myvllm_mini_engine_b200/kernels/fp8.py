@@ -22,6 +22,7 @@ import torch
 from .. import _lib
 from .data import _backend, _rows
 from .paged import _require, _workspace, check_backend
+from .prefill import check_arguments
 
 FP8_HEAD_DIMS = (32, 64, 96, 128, 192, 256)
 _POOL_DTYPES = (torch.uint8, getattr(torch, "float8_e4m3fn", torch.uint8), getattr(torch, "float8_e5m2", torch.uint8))
@@ -162,3 +163,52 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_len
             batch, heads, kv_heads, dim, num_blocks, block_size, width, k_scale, v_scale, fmt, code, stream)
     _lib.check(status, "paged_attention_fp8")
     return out
+
+
+def paged_prefill_attention_fp8(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens,
+                                block_size, k_scale, v_scale, *, kv_format="e4m3", backend="cuda", validate=True,
+                                max_query_len=None):
+    """Ragged causal prefill over FP8 pools: :func:`paged_prefill_attention` with K/V read as ``code * scale``.
+
+    Arguments, checks and messages as ``paged_prefill_attention``
+    (``mini_engine/kernels/prefill.py:61-131``), plus the pools' scales and
+    format.  ``q`` is fp16 or bf16 ``[tokens, q_heads, head_dim]``.  Each query
+    token runs as one row of the fp8 split-KV decode kernel (the CUDA-core
+    route); Q is rounded to fp16 for the products.
+    """
+    if backend != "cuda":
+        raise ValueError("paged prefill backend must be cuda (this package has no torch/CPU path)")
+    fmt = _format(kv_format)
+    k_scale, v_scale = _scale(k_scale, "k_scale"), _scale(v_scale, "v_scale")
+    check_arguments(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens, block_size,
+                    validate, cache_dtypes=_POOL_DTYPES)
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("an fp8 KV pool needs an FP16/BF16 query")
+    if q.device.type != "cuda":
+        raise ValueError("CUDA paged prefill requires CUDA tensors")
+    if q.shape[2] not in FP8_HEAD_DIMS:
+        raise ValueError("fp8 KV pool: supported head_dim: 32,64,96,128,192,256")
+    q = q.contiguous()
+    output = torch.empty_like(q)
+    tokens = q.shape[0]
+    if tokens == 0:
+        return output
+    requests = block_tables.shape[0]
+    num_blocks, _, kv_heads, dim = key_cache.shape
+    width = block_tables.shape[1]
+    bound = tokens if max_query_len is None else int(max_query_len)
+    lib = _lib.load()
+    code = _lib.dtype_code(q.dtype)
+    need = lib.minikv_paged_prefill_fp8_workspace_bytes(tokens, requests, q.shape[1], kv_heads, dim, num_blocks,
+                                                        block_size, width, bound, code)
+    if need < 0:
+        _lib.check(_lib.EINVAL, "paged_prefill_attention_fp8")
+    workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    with _lib.on_device(q.device):
+        status = lib.minikv_paged_prefill_fp8(
+            q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), cu_seqlens_q.data_ptr(),
+            query_starts.data_ptr(), block_tables.data_ptr(), context_lens.data_ptr(), output.data_ptr(),
+            workspace.data_ptr(), workspace.numel(), tokens, requests, q.shape[1], kv_heads, dim, num_blocks,
+            block_size, width, bound, k_scale, v_scale, fmt, code, _lib.stream_of(q.device))
+    _lib.check(status, "paged_prefill_attention_fp8")
+    return output

@@ -17,8 +17,8 @@ HEAD_DIMS = (16, 32, 64, 80, 96, 128, 192, 256)
 
 
 def check_arguments(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables,
-                    context_lens, block_size, validate):
-    """prefill.py:70-104."""
+                    context_lens, block_size, validate, cache_dtypes=None):
+    """prefill.py:70-104.  ``cache_dtypes``: the caches' allowed dtypes when they differ from Q's (FP8 pools)."""
     if (type(block_size) is not int or block_size <= 0 or key_cache.ndim != 4
             or value_cache.shape != key_cache.shape or key_cache.shape[1] != block_size
             or any(size <= 0 for size in key_cache.shape)
@@ -29,8 +29,10 @@ def check_arguments(q, key_cache, value_cache, cu_seqlens_q, query_starts, block
         raise ValueError("paged prefill Q must be [tokens, heads, head_dim] with divisible GQA heads")
     if q.dtype not in (torch.float32, torch.float16, torch.bfloat16):
         raise ValueError("paged prefill requires FP32/FP16/BF16")
-    if key_cache.dtype != q.dtype or value_cache.dtype != q.dtype:
+    if cache_dtypes is None and (key_cache.dtype != q.dtype or value_cache.dtype != q.dtype):
         raise ValueError("paged prefill Q/K/V must share dtype")
+    if cache_dtypes is not None and (key_cache.dtype not in cache_dtypes or value_cache.dtype != key_cache.dtype):
+        raise ValueError("an fp8 KV pool must be uint8 or a float8 dtype")
     metadata = (cu_seqlens_q, query_starts, block_tables, context_lens)
     if (cu_seqlens_q.ndim != 1 or query_starts.ndim != 1 or context_lens.ndim != 1
             or block_tables.ndim != 2 or query_starts.numel() != block_tables.shape[0]

@@ -231,3 +231,26 @@ def test_fp8_pool_range_write_attend_gather_and_copy_on_write(cuda_device, fmt):
     pool.copy_blocks([(17, 20)])
     torch.cuda.synchronize()
     assert torch.equal(pool.key[:, 20], pool.key[:, 17]) and torch.equal(pool.value[:, 20], pool.value[:, 17])
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_ragged_prefill_over_fp8_pool_matches_oracle(cuda_device, fmt):
+    """BASELINE config 4's ragged batch (16 x 128-token chunks over prefixes up to 1024) on an FP8 pool."""
+    from myvllm_mini_engine_b200.engine import PrefillBatch
+    from myvllm_mini_engine_b200.kernels import paged_prefill_attention_fp8
+    from oracle import prefill as prefill_oracle
+
+    c = cases.config4()
+    bs = c["block_size"]
+    batch = PrefillBatch.from_sequences(c["tokens"], c["cow_tables"], c["starts"], block_size=bs,
+                                        num_blocks=c["num_blocks"], device="cuda")
+    kq = torch.from_numpy(fp8_kv.quantize(c["key_cache"], K_SCALE, fmt))
+    vq = torch.from_numpy(fp8_kv.quantize(c["value_cache"], V_SCALE, fmt))
+    meta = (batch.cu_seqlens_q, batch.query_starts, batch.block_tables, batch.context_lens)
+    out = paged_prefill_attention_fp8(c["q"].cuda(), kq.cuda(), vq.cuda(), *meta, bs, K_SCALE, V_SCALE,
+                                      kv_format=fmt)
+    expected = prefill_oracle.paged_prefill_fp32(c["q"].float(), fp8_kv.dequantize(kq, K_SCALE, fmt),
+                                                 fp8_kv.dequantize(vq, V_SCALE, fmt), *(t.cpu() for t in meta), bs)
+    assert out.dtype == c["q"].dtype and out.shape == c["q"].shape
+    assert_close(out, expected, c["q"].dtype)
+    assert _lib.device_status() == 0
