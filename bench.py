@@ -668,7 +668,7 @@ def run_qwen3_reference(args, world, rank):
 
 def run_qwen3(args, world, rank, local):
     from myvllm_mini_engine_b200 import _lib
-    from myvllm_mini_engine_b200.cache.kv_cache import FP8KVCachePool, KVCachePool
+    from myvllm_mini_engine_b200.cache.kv_cache import FP8KVCachePool, PagedKVPool
     from myvllm_mini_engine_b200.engine.qwen3 import DecodeGraph, Qwen3DecodeStep, Qwen3Weights
     from myvllm_mini_engine_b200.kernels import paged_attention, paged_attention_fp8
 
@@ -699,7 +699,7 @@ def run_qwen3(args, world, rank, local):
             pool.write_slots(layer, slots, rows, rows.flip(0), validate=False)
         del rows, slots
     else:
-        pool = KVCachePool(cfg.num_hidden_layers, blocks, BS, cfg.num_key_value_heads, cfg.head_dim,
+        pool = PagedKVPool(cfg.num_hidden_layers, blocks, BS, cfg.num_key_value_heads, cfg.head_dim,
                            dtype=torch.bfloat16, device=device)
         for layer in range(cfg.num_hidden_layers):
             pool.key[layer].normal_(generator=gen)

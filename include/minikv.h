@@ -41,6 +41,11 @@ enum { MINIKV_STATUS_WAIT_TIMEOUT = 1 };
 
 int minikv_abi_version(void);
 
+/* SHA-256 (hex) of the sources the library was built from (csrc/*.cu, *.cuh and
+ * this header), so a loader can refuse a library older than its sources.  New;
+ * the reference JIT-builds its extension on import and has no such check. */
+const char* minikv_source_hash(void);
+
 /* Message of the last failed call on this thread ("" if none). */
 const char* minikv_last_error(void);
 
@@ -102,7 +107,9 @@ int minikv_paged_decode_chained(const void* query, const void* key_cache, const 
  * built-in 16 MiB device array that every GPU loading the library keeps until
  * exit; shapes needing more scratch than that fail with MINIKV_EINVAL.  The
  * first call on each device looks the array up (cudaGetSymbolAddress) and
- * should come before any stream capture.  All calls share the array: calls
+ * should come before any stream capture; the address it keeps is valid for
+ * the life of the device's primary context (not across cudaDeviceReset).
+ * All calls share the array: calls
  * that overlap on the GPU race and must be serialised by the caller.  Nothing
  * is allocated or freed. */
 int minikv_paged_decode_noalloc(const void* query, const void* key_cache, const void* value_cache,

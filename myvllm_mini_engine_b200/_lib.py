@@ -3,7 +3,8 @@
 The shared library is built in-tree (``python -m myvllm_mini_engine_b200.build``
 or ``__graft_entry__.build()``) and loaded from this package directory.  There
 is no CPU fallback: if the library is missing or fails to load, every op
-raises RuntimeError.
+raises RuntimeError.  A library built from other sources than the ones next
+to it (its compiled-in ``minikv_source_hash`` differs) is refused the same way.
 """
 
 from __future__ import annotations
@@ -27,6 +28,7 @@ _p, _i64, _int, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_f
 # name -> (restype, argtypes); must match include/minikv.h
 SIGNATURES = {
     "minikv_abi_version": (_int, []),
+    "minikv_source_hash": (ctypes.c_char_p, []),
     "minikv_last_error": (ctypes.c_char_p, []),
     "minikv_device_status": (_int, [ctypes.POINTER(ctypes.c_uint), _int, _p]),
     "minikv_paged_decode_workspace_bytes": (_i64, [_i64] * 7 + [_int]),
@@ -79,6 +81,13 @@ def load():
         fn.argtypes = argtypes
     if lib.minikv_abi_version() != 1:
         raise RuntimeError("libminikv ABI version mismatch; rebuild the library")
+    from . import build
+
+    if build.CSRC.is_dir():  # an installed copy without its sources cannot be checked
+        expected, found = build.source_hash(), lib.minikv_source_hash().decode()
+        if found != expected:
+            raise RuntimeError(f"{path} was built from other sources (hash {found[:12]}, sources "
+                               f"{expected[:12]}): rebuild it with `python -m myvllm_mini_engine_b200.build`")
     _LIB = lib
     return lib
 

@@ -5,12 +5,17 @@
 One translation unit (csrc/abi.cu includes the kernel files), compiled with
 ``-gencode arch=compute_100a,code=sm_100a -O3 -lineinfo``.  The CUDA runtime
 is linked statically, so the library only needs the NVIDIA driver at run time.
-Rebuilds only when a source file is newer than the library.
+
+The SHA-256 of the sources (``source_hash()``) is compiled into the library
+(``minikv_source_hash``).  The library is rebuilt when the hash it carries
+differs from the sources' hash, never by file times, and the loader refuses a
+library whose hash differs from the sources next to it.
 """
 
 from __future__ import annotations
 
 import argparse
+import hashlib
 import os
 import shutil
 import subprocess
@@ -35,18 +40,40 @@ def nvcc_path():
     return str(candidate) if candidate.exists() else (shutil.which("nvcc") or "nvcc")
 
 
+MARKER = b"minikv-source-hash:"
+
+
+def source_hash() -> str:
+    """SHA-256 over the sources' names (relative to the package root) and contents."""
+    digest = hashlib.sha256()
+    for src in sources():
+        digest.update(src.relative_to(ROOT).as_posix().encode() + b"\0")
+        digest.update(src.read_bytes() + b"\0")
+    return digest.hexdigest()
+
+
+def built_hash(path: Path = OUTPUT) -> str | None:
+    """The source hash compiled into a built library, read from the file without loading it."""
+    if not path.is_file():
+        return None
+    data = path.read_bytes()
+    at = data.find(MARKER)
+    if at < 0:
+        return None
+    end = at + len(MARKER)
+    return data[end:end + 64].decode("ascii", errors="replace")
+
+
 def up_to_date() -> bool:
-    if not OUTPUT.exists():
-        return False
-    built = OUTPUT.stat().st_mtime
-    return all(src.stat().st_mtime <= built for src in sources())
+    return built_hash() == source_hash()
 
 
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and up_to_date():
         return OUTPUT
     tmp = OUTPUT.with_suffix(".so.tmp")
-    cmd = [nvcc_path(), *ARCH, *FLAGS, "-o", str(tmp), str(CSRC / "abi.cu")]
+    cmd = [nvcc_path(), *ARCH, *FLAGS, f'-DMINIKV_SOURCE_HASH="{source_hash()}"', "-o", str(tmp),
+           str(CSRC / "abi.cu")]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)

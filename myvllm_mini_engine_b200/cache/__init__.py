@@ -1,4 +1,4 @@
-from .block_manager import BlockManager, BlockTable
-from .kv_cache import FP8KVCachePool, KVCachePool, KVCacheShape
+from .cow import copy_on_write, prepare_write
+from .kv_cache import FP8KVCachePool, PagedKVPool, PoolShape
 
-__all__ = ["BlockManager", "BlockTable", "FP8KVCachePool", "KVCachePool", "KVCacheShape"]
+__all__ = ["FP8KVCachePool", "PagedKVPool", "PoolShape", "copy_on_write", "prepare_write"]

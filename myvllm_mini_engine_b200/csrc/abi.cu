@@ -8,6 +8,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "../../include/minikv.h"
@@ -48,6 +49,26 @@ int sm_count() {
     return cached[device];
 }
 
+// Raise a kernel's opt-in dynamic shared-memory limit on the current device to at
+// least `bytes`.  `configured` is the kernel's per-device record of the limit
+// already set (64 entries).  The check and the set happen under one lock and the
+// limit only ever grows, so host threads launching the same kernel with
+// different plans never leave it below a plan that passed the check.
+std::mutex g_smem_attribute_lock;
+
+template <typename Kernel>
+cudaError_t ensure_smem_limit(Kernel kernel, int bytes, int* configured) {
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return err;
+    const bool tracked = device >= 0 && device < 64;
+    std::lock_guard<std::mutex> guard(g_smem_attribute_lock);
+    if (tracked && configured[device] >= bytes) return cudaSuccess;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err == cudaSuccess && tracked) configured[device] = bytes;
+    return err;
+}
+
 #define MINIKV_REQUIRE(cond, code, msg) \
     do {                                \
         if (!(cond)) return fail(code, msg); \
@@ -68,6 +89,14 @@ using namespace minikv;
 extern "C" {
 
 int minikv_abi_version(void) { return MINIKV_ABI_VERSION; }
+
+#ifndef MINIKV_SOURCE_HASH
+#define MINIKV_SOURCE_HASH "unknown"
+#endif
+// The marker prefix lets the build recipe read the hash from the file without loading it.
+static const char kSourceHash[] = "minikv-source-hash:" MINIKV_SOURCE_HASH;
+
+const char* minikv_source_hash(void) { return kSourceHash + sizeof("minikv-source-hash:") - 1; }
 
 const char* minikv_last_error(void) { return g_last_error.c_str(); }
 

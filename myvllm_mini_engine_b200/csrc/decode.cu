@@ -694,16 +694,10 @@ template <typename T, int D>
 static cudaError_t launch_decode_typed(const DecodeParams& p, const DecodePlan& plan, cudaStream_t stream) {
     using Consumer = typename std::conditional<sizeof(T) == 2, MmaConsumer<T, D>, CoreConsumer<T, D>>::type;
     auto kernel = paged_decode_kernel<T, D, Consumer>;
-    // the opt-in shared-memory size, set once per device and size (a host call per launch otherwise)
+    // the opt-in shared-memory size, raised once per device and size (a host call per launch otherwise)
     static int configured[64] = {0};
-    int device = 0;
-    cudaError_t err = cudaGetDevice(&device);
+    cudaError_t err = ensure_smem_limit(kernel, plan.smem_bytes, configured);
     if (err != cudaSuccess) return err;
-    if (device < 0 || device >= 64 || configured[device] < plan.smem_bytes) {
-        err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.smem_bytes);
-        if (err != cudaSuccess) return err;
-        if (device >= 0 && device < 64) configured[device] = plan.smem_bytes;
-    }
     return launch_chained(kernel, dim3(plan.grid, plan.head_groups), dim3(kDecodeThreads), plan.smem_bytes, stream, p);
 }
 

@@ -397,14 +397,8 @@ template <typename T, int D, bool E5M2>
 static cudaError_t launch_decode_fp8_typed(const DecodeParams& p, const DecodePlan& plan, cudaStream_t stream) {
     auto kernel = paged_decode_kernel<T, D, Fp8MmaConsumer<T, D, E5M2>>;
     static int configured[64] = {0};  // opt-in shared-memory size set per device
-    int device = 0;
-    cudaError_t err = cudaGetDevice(&device);
+    cudaError_t err = ensure_smem_limit(kernel, plan.smem_bytes, configured);
     if (err != cudaSuccess) return err;
-    if (device < 0 || device >= 64 || configured[device] < plan.smem_bytes) {
-        err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, plan.smem_bytes);
-        if (err != cudaSuccess) return err;
-        if (device >= 0 && device < 64) configured[device] = plan.smem_bytes;
-    }
     return launch_chained(kernel, dim3(plan.grid, plan.head_groups), dim3(kDecodeThreads), plan.smem_bytes, stream, p);
 }
 

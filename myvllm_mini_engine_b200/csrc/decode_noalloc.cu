@@ -20,7 +20,10 @@
 //    other's results, so callers must serialise them;
 //  * the first call on each device looks up the array's device address with
 //    cudaGetSymbolAddress (with that device current) and caches it; make that
-//    first call before any stream capture on the device.
+//    first call before any stream capture on the device.  The cached address
+//    belongs to the device's primary context: after cudaDeviceReset (or any
+//    teardown of that context) it is stale, so a process that resets a device
+//    must not call this entry point on it again.
 #include <mutex>
 
 #include "common.cuh"

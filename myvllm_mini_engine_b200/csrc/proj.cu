@@ -562,17 +562,27 @@ static ProjPlan make_proj_plan(int64_t tokens, int64_t in_features, int64_t tile
 template <typename T, int EPI, bool NORM>
 static cudaError_t launch_proj_typed(ProjParams p, int64_t tiles, cudaStream_t stream) {
     auto kernel = proj_kernel<T, EPI, NORM>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448 - 1024);
-        if (err != cudaSuccess) return err;
-        configured = true;
-    }
-    static int limit_smem = -1, limit = 8;  // cluster limit of this kernel, cached per shared-memory size
+    static int configured[64] = {0};  // the attribute is per device: set on each device the kernel runs on
+    cudaError_t set = ensure_smem_limit(kernel, 232448 - 1024, configured);
+    if (set != cudaSuccess) return set;
+    // cluster limit of this kernel, cached per device and shared-memory size
+    struct ClusterLimit {
+        int smem = -1, limit = 8;
+    };
+    static ClusterLimit limits[64];
+    int limit = 8;
     const ProjPlan probe = make_proj_plan(p.tokens, p.in_features, tiles, sm_count(), kProjMaxSplit);
-    if (probe.split > 8 && probe.smem != limit_smem) {
-        limit = proj_cluster_limit(kernel, probe.smem);
-        limit_smem = probe.smem;
+    if (probe.split > 8) {
+        int device = 0;
+        if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) device = -1;
+        std::lock_guard<std::mutex> guard(g_smem_attribute_lock);
+        if (device < 0) {
+            limit = proj_cluster_limit(kernel, probe.smem);
+        } else {
+            ClusterLimit& cached = limits[device];
+            if (cached.smem != probe.smem) cached = ClusterLimit{probe.smem, proj_cluster_limit(kernel, probe.smem)};
+            limit = cached.limit;
+        }
     }
     const ProjPlan pl = probe.split > 8 && limit < probe.split
                             ? make_proj_plan(p.tokens, p.in_features, tiles, sm_count(), limit)

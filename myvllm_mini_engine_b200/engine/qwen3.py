@@ -47,7 +47,7 @@ import torch
 from torch.nn import functional as F
 
 from .. import _lib
-from ..cache.kv_cache import FP8KVCachePool, KVCachePool
+from ..cache.kv_cache import FP8KVCachePool, PagedKVPool
 from ..kernels.fp8 import paged_attention_fp8, write_kv_cache_slots_fp8
 from ..kernels.paged import paged_attention
 
@@ -166,7 +166,7 @@ def pack_linear(weight: torch.Tensor, *, pair_offset: int = 0) -> torch.Tensor:
 class Qwen3DecodeStep:
     """One decode token per request through all layers, reading and appending the paged pool.
 
-    ``pool`` is a :class:`KVCachePool` shaped for ``config`` (layers, kv heads,
+    ``pool`` is a :class:`PagedKVPool` (or the reference engine's ``KVCachePool``) shaped for ``config`` (layers, kv heads,
     head_dim) in the weights' dtype and device, or an :class:`FP8KVCachePool`
     (an extension: the new token's K/V are written by the same kernels into a
     small bf16 staging buffer, then quantised into the pool by the FP8 slot
@@ -179,7 +179,7 @@ class Qwen3DecodeStep:
     #: batches up to this size take the fused tcgen05 projections; larger ones cuBLAS
     FUSED_MAX_BATCH = 32
 
-    def __init__(self, config: Qwen3Config, weights: Qwen3Weights, pool: KVCachePool, *,
+    def __init__(self, config: Qwen3Config, weights: Qwen3Weights, pool: PagedKVPool, *,
                  fused_projections: bool | None = None):
         shape = pool.shape
         if (shape.num_layers, shape.num_kv_heads, shape.head_dim) != (

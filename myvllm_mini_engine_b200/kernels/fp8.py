@@ -12,7 +12,9 @@ element ``x`` is stored as ``fp8(x * (1/scale))`` (fp32 product, nearest-even,
 saturated to the largest finite code) and read as ``code * scale``.
 ``kv_format`` picks the byte format: "e4m3" (3 mantissa bits, range 448) or
 "e5m2" (2 mantissa bits, range 57344, decoded with byte moves only, so its
-decode runs faster).  A decode step streams half the bytes of a bf16 pool.
+decode runs faster).  A float8 pool dtype names its own format: ``kv_format``
+may then be left as None, and a ``kv_format`` that contradicts it raises
+ValueError.  A uint8 pool reads ``kv_format`` (None means "e4m3").  A decode step streams half the bytes of a bf16 pool.
 """
 
 from __future__ import annotations
@@ -29,10 +31,18 @@ _POOL_DTYPES = (torch.uint8, getattr(torch, "float8_e4m3fn", torch.uint8), getat
 FORMATS = {"e4m3": 0, "e5m2": 1}
 
 
-def _format(kv_format):
-    if kv_format not in FORMATS:
+_DTYPE_FORMATS = {dtype: name for dtype, name in ((getattr(torch, "float8_e4m3fn", None), "e4m3"),
+                                                  (getattr(torch, "float8_e5m2", None), "e5m2")) if dtype is not None}
+
+
+def _format(kv_format, pool_dtype=torch.uint8):
+    """Format code of a pool: a float8 dtype decides it, a uint8 pool takes ``kv_format`` (default e4m3)."""
+    if kv_format is not None and kv_format not in FORMATS:
         raise ValueError("kv_format must be 'e4m3' or 'e5m2'")
-    return FORMATS[kv_format]
+    implied = _DTYPE_FORMATS.get(pool_dtype)
+    if implied is not None and kv_format not in (None, implied):
+        raise ValueError(f"kv_format {kv_format!r} contradicts the {pool_dtype} pool")
+    return FORMATS[implied or kv_format or "e4m3"]
 
 
 def _scale(value, name):
@@ -43,7 +53,7 @@ def _scale(value, name):
 
 
 def write_kv_cache_slots_fp8(key_cache, value_cache, slot_mapping, key, value, k_scale, v_scale, *,
-                             kv_format="e4m3", backend="cuda", validate=True):
+                             kv_format=None, backend="cuda", validate=True):
     """Quantise packed K/V rows into FP8 pools at ``slot_mapping`` (slots outside the capacity are skipped).
 
     ``key``/``value`` ``[tokens, kv_heads, head_dim]`` fp32/fp16/bf16 (token-strided
@@ -52,7 +62,7 @@ def write_kv_cache_slots_fp8(key_cache, value_cache, slot_mapping, key, value, k
     of ``write_kv_cache_slots`` (data.py:109-119).
     """
     _backend(backend)
-    fmt = _format(kv_format)
+    fmt = _format(kv_format, key_cache.dtype)
     k_scale, v_scale = _scale(k_scale, "k_scale"), _scale(v_scale, "v_scale")
     if (key_cache.ndim != 4 or value_cache.shape != key_cache.shape
             or any(size <= 0 for size in key_cache.shape)
@@ -101,7 +111,7 @@ _WS_BYTES: dict = {}
 
 
 def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_lens, block_size, k_scale, v_scale,
-                        *, kv_format="e4m3", backend="cuda", validate=True, workspace=None):
+                        *, kv_format=None, backend="cuda", validate=True, workspace=None):
     """Decode attention over FP8 pools: ``softmax(q . (K*k_scale)^T / sqrt(D)) (V*v_scale)``.
 
     Arguments and guards as :func:`paged_attention` (``query [B, Hq, D]`` fp16 or
@@ -110,7 +120,7 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_len
     rounded to fp16 (saturated at +-65504).  Returns ``[B, Hq, D]`` in the query dtype.
     """
     check_backend(backend)
-    fmt = _format(kv_format)
+    fmt = _format(kv_format, key_cache.dtype)
     k_scale, v_scale = _scale(k_scale, "k_scale"), _scale(v_scale, "v_scale")
     _require(query.is_cuda, "query must be CUDA")
     for t in (key_cache, value_cache, block_tables, context_lens):
@@ -166,7 +176,7 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_len
 
 
 def paged_prefill_attention_fp8(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens,
-                                block_size, k_scale, v_scale, *, kv_format="e4m3", backend="cuda", validate=True,
+                                block_size, k_scale, v_scale, *, kv_format=None, backend="cuda", validate=True,
                                 max_query_len=None):
     """Ragged causal prefill over FP8 pools: :func:`paged_prefill_attention` with K/V read as ``code * scale``.
 
@@ -178,7 +188,7 @@ def paged_prefill_attention_fp8(q, key_cache, value_cache, cu_seqlens_q, query_s
     """
     if backend != "cuda":
         raise ValueError("paged prefill backend must be cuda (this package has no torch/CPU path)")
-    fmt = _format(kv_format)
+    fmt = _format(kv_format, key_cache.dtype)
     k_scale, v_scale = _scale(k_scale, "k_scale"), _scale(v_scale, "v_scale")
     check_arguments(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens, block_size,
                     validate, cache_dtypes=_POOL_DTYPES)

@@ -48,11 +48,20 @@ def raw(t):
 
 
 def load_reference(reference: Path):
+    """Import the reference engine from ``baseline/_ref`` and its benchmarks from ``reference``.
+
+    ``baseline/_ref`` is the pip install of the reference
+    (``python -m pip install --no-index --no-build-isolation --no-deps --target
+    baseline/_ref <copy of the reference>``); when it is missing, the reference
+    tree is copied there instead.  The ``benchmarks`` package is not part of the
+    install and is imported read-only from ``reference`` (no bytecode written).
+    """
     copy = REPO / "baseline" / "_ref"
     if not (copy / "mini_engine").is_dir():
         shutil.copytree(reference, copy, ignore=shutil.ignore_patterns(".git"))
+    sys.dont_write_bytecode = True
     sys.path.insert(0, str(copy))
-    sys.path.insert(0, str(copy / "benchmarks" / ".."))
+    sys.path.append(str(reference))
     import mini_engine  # noqa: F401  (runs configure_local_cache inside the copy)
     from mini_engine.kernels import data, paged, prefill
     from mini_engine.engine.batch import PrefillBatch

@@ -77,3 +77,15 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setenv("MINIKV_LIBRARY", str(tmp_path / "absent.so"))
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _lib.load()
+
+
+def test_library_built_from_other_sources_is_refused(monkeypatch):
+    from myvllm_mini_engine_b200 import build
+
+    assert build.built_hash() == build.source_hash() == _lib.load().minikv_source_hash().decode()
+    monkeypatch.setattr(_lib, "_LIB", None)
+    monkeypatch.setattr(build, "source_hash", lambda: "0" * 64)
+    with pytest.raises(RuntimeError, match="built from other sources"):
+        _lib.load()
+    monkeypatch.undo()
+    assert _lib.load() is not None

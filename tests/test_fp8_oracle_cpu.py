@@ -101,11 +101,11 @@ def test_fp8_pool_and_wrappers_validate_arguments_on_the_host():
     assert pool.memory_bytes == 2 * 2 * 4 * 16 * 2 * 64 and pool.key.dtype == torch.uint8
     rows = torch.zeros(3, 2, 64, dtype=torch.bfloat16)
     with pytest.raises(IndexError, match="layer"):
-        pool.write_cuda(2, [0], 0, rows, rows)
+        pool.write_range(2, [0], 0, rows, rows)
     with pytest.raises(IndexError, match="block id"):
-        pool.write_cuda(0, [7], 0, rows, rows)
+        pool.write_range(0, [7], 0, rows, rows)
     with pytest.raises(ValueError, match="capacity"):
-        pool.write_cuda(0, [0], 15, rows, rows)
+        pool.write_range(0, [0], 15, rows, rows)
     with pytest.raises(ValueError, match="CUDA"):  # no CPU path
         pool.write_slots(0, torch.arange(3), rows, rows)
     kc = torch.zeros(4, 16, 2, 64, dtype=torch.uint8)
@@ -116,3 +116,19 @@ def test_fp8_pool_and_wrappers_validate_arguments_on_the_host():
     with pytest.raises(RuntimeError, match="CUDA"):
         paged_attention_fp8(torch.zeros(1, 4, 64, dtype=torch.bfloat16), kc, kc, torch.zeros(1, 1, dtype=torch.int64),
                             torch.ones(1, dtype=torch.int64), 16, 0.1, 0.1)
+
+
+def test_fp8_pool_dtype_decides_the_format():
+    from myvllm_mini_engine_b200.kernels import paged_attention_fp8, write_kv_cache_slots_fp8
+    from myvllm_mini_engine_b200.kernels.fp8 import FORMATS, _format
+
+    assert _format(None, torch.float8_e5m2) == FORMATS["e5m2"]
+    assert _format("e4m3", torch.float8_e4m3fn) == FORMATS["e4m3"]
+    assert _format(None) == FORMATS["e4m3"] and _format("e5m2", torch.uint8) == FORMATS["e5m2"]
+    kc = torch.zeros(4, 16, 2, 64, dtype=torch.float8_e5m2)
+    rows = torch.zeros(3, 2, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="contradicts"):  # an e5m2 pool read as e4m3 would decode wrong values
+        write_kv_cache_slots_fp8(kc, kc.clone(), torch.arange(3), rows, rows, 0.1, 0.1, kv_format="e4m3")
+    with pytest.raises(ValueError, match="contradicts"):
+        paged_attention_fp8(torch.zeros(1, 4, 64, dtype=torch.bfloat16), kc, kc, torch.zeros(1, 1, dtype=torch.int64),
+                            torch.ones(1, dtype=torch.int64), 16, 0.1, 0.1, kv_format="e4m3")

@@ -38,7 +38,7 @@ import torch
 
 import cases
 from myvllm_mini_engine_b200 import _lib
-from myvllm_mini_engine_b200.cache.kv_cache import KVCachePool
+from myvllm_mini_engine_b200.cache.kv_cache import PagedKVPool
 from myvllm_mini_engine_b200.engine.qwen3 import DecodeGraph, Qwen3Config, Qwen3DecodeStep, Qwen3Weights
 from oracle import qwen3 as ref
 
@@ -142,7 +142,7 @@ def model_case(batch_contexts, seed, layers=None):
     for b, n in enumerate(pages):
         tables[b, :n] = perm[used:used + n]
         used += n
-    pool = KVCachePool(cfg.num_hidden_layers, blocks, bs, cfg.num_key_value_heads, cfg.head_dim,
+    pool = PagedKVPool(cfg.num_hidden_layers, blocks, bs, cfg.num_key_value_heads, cfg.head_dim,
                        dtype=torch.bfloat16, device="cuda")
     pool.key.normal_(generator=gen)
     pool.value.normal_(generator=gen)

@@ -211,7 +211,7 @@ def test_fp8_pool_range_write_attend_gather_and_copy_on_write(cuda_device, fmt):
     ids, offset, tokens = [5, 17, 2, 9], 3, 50
     key = torch.randn(tokens, hkv, dim, generator=gen).to(torch.bfloat16)
     value = torch.randn(tokens, hkv, dim, generator=gen).to(torch.bfloat16)
-    pool.write_cuda(1, ids, offset, key.cuda(), value.cuda())
+    pool.write_range(1, ids, offset, key.cuda(), value.cuda())
     positions = torch.arange(tokens) + offset
     slots = torch.tensor(ids)[positions // bs] * bs + positions % bs
     kc = torch.zeros(blocks, bs, hkv, dim, dtype=torch.uint8)
@@ -219,7 +219,7 @@ def test_fp8_pool_range_write_attend_gather_and_copy_on_write(cuda_device, fmt):
     fp8_kv.scatter_slots_fp8(kc, vc, slots, key, value, K_SCALE, V_SCALE, fmt)
     assert torch.equal(pool.key[1].cpu(), kc) and torch.equal(pool.value[1].cpu(), vc)
     assert not pool.key[0].any() and not pool.value[0].any()
-    k_rows, v_rows = pool.gather(1, ids, offset + tokens)
+    k_rows, v_rows = pool.dequantized(1, ids, offset + tokens)
     assert torch.equal(k_rows[offset:].cpu(), fp8_kv.dequantize(kc.view(-1, hkv, dim)[slots], K_SCALE, fmt))
     assert torch.equal(v_rows[offset:].cpu(), fp8_kv.dequantize(vc.view(-1, hkv, dim)[slots], V_SCALE, fmt))
     query = torch.randn(2, 8, dim, generator=gen).to(torch.bfloat16)

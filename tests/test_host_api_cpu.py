@@ -10,7 +10,7 @@ import pytest
 import torch
 
 import cases
-from myvllm_mini_engine_b200.cache import BlockManager
+from myvllm_mini_engine_b200.cache import copy_on_write, prepare_write
 from myvllm_mini_engine_b200.engine import PrefillBatch
 from myvllm_mini_engine_b200.kernels import (copy_blocks, paged_attention, paged_prefill_attention,
                                              write_kv_cache, write_kv_cache_batch, write_kv_cache_slots)
@@ -94,23 +94,10 @@ def test_prefill_batch_rejects_write_into_shared_page_until_copy_on_write():
                                     num_blocks=c["num_blocks"], device="cpu")
 
 
-# ------------------------------------------------------------------ BlockManager
-def test_block_manager_matches_reference_allocation_order():
-    manager = BlockManager(8, 4)
-    assert manager.allocate("a", 9) == [0, 1, 2]          # LIFO free list: lowest ids first
-    assert manager.allocate_with_prefix("b", 10, [0, 1]) == [0, 1, 3]
-    assert manager.refcount(0) == 2 and manager.refcount(3) == 1
-    manager.pin([0])
-    assert manager.refcount(0) == 3
-    manager.release("a")
-    assert manager.refcount(0) == 2 and manager.free_blocks == 5
-    assert manager.grow("b", 17) == [0, 1, 3, 2, 4]
-    assert manager.truncate("b", 5) == [0, 1]
-    with pytest.raises(MemoryError):
-        manager.allocate("c", 100)
+# ------------------------------------------- copy-on-write on the reference allocator
+def test_copy_on_write_forks_only_shared_pages_of_the_reference_allocator(reference_engine):
+    from mini_engine.cache.block_manager import BlockManager
 
-
-def test_copy_on_write_forks_only_shared_pages():
     manager = BlockManager(128, 16)
     shared = manager.allocate("prefix-owner", 512)
     manager.pin(shared)                                   # prefix-cache pin
@@ -118,12 +105,39 @@ def test_copy_on_write_forks_only_shared_pages():
         manager.attach(f"r{r}", shared)
         manager.grow(f"r{r}", 512 + 128)
     assert manager.refcount(shared[31]) == 10
-    pairs = manager.prepare_write("r3", 496, 624)         # chunk starts inside shared page 31
+    free_before = manager.free_blocks
+    pairs = prepare_write(manager, "r3", 496, 624)        # chunk starts inside shared page 31
     assert len(pairs) == 1 and pairs[0][0] == shared[31]
     dst = pairs[0][1]
     assert manager.table("r3").block_ids[31] == dst and manager.refcount(dst) == 1
+    assert manager.free_blocks == free_before - 1
     assert manager.refcount(shared[31]) == 9 and manager.table("r2").block_ids[31] == shared[31]
-    assert manager.prepare_write("r3", 496, 624) == []   # already private
-    assert manager.prepare_write("r4", 512, 640) == []   # writes only private pages
-    manager.release("r3")
+    assert prepare_write(manager, "r3", 496, 624) == []  # already private
+    assert prepare_write(manager, "r4", 512, 640) == []  # writes only private pages
+    assert prepare_write(manager, "r4", 0, 0) == []
+    manager.release("r3")                                 # the reference's own release sees the fork
     assert manager.refcount(dst) == 0 and manager.refcount(shared[31]) == 9
+    manager.release("prefix-owner")
+    manager.unpin(shared)
+    for r in (0, 1, 2, 4, 5, 6, 7):
+        manager.release(f"r{r}")
+    assert manager.free_blocks == 128                     # every page, forked or not, back on the free list
+
+
+def test_copy_on_write_errors_leave_the_reference_allocator_unchanged(reference_engine):
+    from mini_engine.cache.block_manager import BlockManager
+
+    manager = BlockManager(3, 4)
+    shared = manager.allocate("a", 8)
+    manager.attach("b", shared)
+    manager.allocate("c", 4)                              # the last free page
+    with pytest.raises(KeyError):
+        copy_on_write(manager, "missing", 0)
+    with pytest.raises(IndexError):
+        copy_on_write(manager, "b", 2)
+    with pytest.raises(ValueError):
+        prepare_write(manager, "b", 5, 4)
+    with pytest.raises(MemoryError):
+        copy_on_write(manager, "b", 0)
+    assert manager.table("b").block_ids == tuple(shared) and manager.refcount(shared[0]) == 2
+    assert copy_on_write(manager, "c", 0) is None         # private page: nothing to fork
