@@ -12,12 +12,20 @@ step is the reference's per-layer decode hot path: ``write_kv_cache_batch``
 independent pool and batch (weak scaling, no collective on the data path).
 
 Metric: paged-decode KV-read GB/s (algorithmic KV bytes read by the step /
-step time), summed over GPUs; decode tok/s is reported beside it.  Timed with
-CUDA events around K replays of a CUDA graph of one step; the inputs (295 MB
-per GPU) exceed the 126 MB L2.  ``e2e`` repeats the step through the public
-Python API with host buffers: every step copies q/k/v/tables/lengths from
-pinned host memory and reads the output back.  ``--impl reference`` times the
-reference algorithm's CPU path (the oracle restatement) on the host cores.
+step time), summed over GPUs.  Timed with CUDA events around K replays of a
+CUDA graph of one step, in ``--repeats`` windows (median reported, min and max
+beside it); the inputs (295 MB per GPU) exceed the 126 MB L2.  ``e2e`` repeats
+the step through the public Python API with host buffers: every step copies
+q/k/v/tables/lengths from pinned host memory and reads the output back.
+``--impl reference`` times the reference algorithm's CPU path (the oracle
+restatement) on the host cores.
+
+The same JSON line also carries every BASELINE config (unless
+``--headline-only``): ``config1``..``config3`` (decode, one GPU, L2 flushed
+before every step), ``config4`` (copy-on-write + scatter + ragged prefill, one
+GPU) and ``qwen3`` (config 5, the whole Qwen3 decode step, 256 requests x 4096
+split over the N ranks: strong scaling, its ``value`` is the model's decode
+tok/s), each with its roofline fraction and the CPU path timed beside it.
 """
 
 from __future__ import annotations
@@ -46,8 +54,12 @@ HQ, HKV, D, BS = 16, 8, 128, 16
 def parse_args(argv=None):
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20000)
+    parser.add_argument("--steps", type=int, default=200)
     parser.add_argument("--warmup", type=int, default=20)
+    parser.add_argument("--repeats", type=int, default=25,
+                        help="decode: timed windows of --steps steps each; ms_per_step is their median")
+    parser.add_argument("--headline-only", action="store_true",
+                        help="decode: skip the per-config fields (configs 1-4 at one GPU, config 5 at every N)")
     parser.add_argument("--impl", choices=("ours", "reference"), default="ours")
     parser.add_argument("--workload", choices=("decode", "qwen3", "prefill"), default="decode",
                         help="decode: append + paged attention per GPU (weak scaling); qwen3: the full "
@@ -334,26 +346,32 @@ def run_ours(args, world, rank, local):
             torch.distributed.barrier()
         torch.cuda.synchronize(device)
 
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # R windows of exactly K steps, each bracketed by a barrier and a synchronize; a window's
+    # time is the max over ranks, and ms_per_step is the median window
+    repeats = max(1, args.repeats)
+    windows = []
     kernel_ms = []
     with ClockSampler(local) as clocks:
-        barrier()
-        start.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
-        end.record(stream)
-        barrier()
+        for _ in range(repeats):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            barrier()
+            start.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            end.record(stream)
+            barrier()
+            windows.append(start.elapsed_time(end))
         # per-launch decode time: the probe graph, reading its events after each replay
         for _ in range(min(args.steps, 50)):
             probe.replay()
             ev_b.synchronize()
             kernel_ms.append(ev_a.elapsed_time(ev_b))
-    elapsed_ms = start.elapsed_time(end)
     if world > 1:
-        t = torch.tensor([elapsed_ms], device=device)
+        t = torch.tensor(windows, device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    ms_per_step = elapsed_ms / args.steps
+        windows = [float(x) for x in t.tolist()]
+    per_step = sorted(w / args.steps for w in windows)
+    ms_per_step = statistics.median(per_step)
     value = world * step_bytes / (ms_per_step * 1e-3) / 1e9
     kernel_avg_ms = statistics.mean(kernel_ms)
     achieved = step_bytes / (kernel_avg_ms * 1e-3) / 1e9
@@ -448,7 +466,11 @@ def run_ours(args, world, rank, local):
                    "global_batch": args.batch * world, "seq_len": args.context,
                    "parallelism": f"request-sharded x{world} (independent KV pools)",
                    "l2": f"inputs {2 * x['key_cache'].numel() * 2 / 1e6:.0f} MB per GPU > 126 MB L2"},
-        "decode_tok_s": world * args.batch / (ms_per_step * 1e-3),
+        "windows": {"count": repeats, "steps_each": args.steps, "ms_per_step_median": ms_per_step,
+                    "ms_per_step_min": per_step[0], "ms_per_step_max": per_step[-1]},
+        "layer_op_tok_s": world * args.batch / (ms_per_step * 1e-3),
+        "layer_op_tok_s_note": "requests served per second by ONE layer's append + decode (an operator rate); "
+                               "the model's decode tok/s is qwen3.value (BASELINE config 5, all 28 layers)",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "traffic": ncu_traffic("decode_b32_ctx2048_bf16"),
@@ -459,12 +481,170 @@ def run_ours(args, world, rank, local):
                 "path": "write_kv_cache_batch + paged_attention (Python API, eager), one H2D copy of the packed "
                         "inputs and one D2H copy of the output per step, pinned host buffers; copies on a second "
                         "stream, pipelined across steps (double-buffered device inputs)"},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": 2 * args.steps * repeats,
+        "gpu_launches_note": "append + decode per step, in each of the timed windows",
         "clocks": clocks.summary(),
     }
     if world == 1:
         line["cpu_baseline"] = cpu_baseline(args.context, args.cpu_seconds)
     return line
+
+
+# ------------------------------------------------- BASELINE configs 1-3 (decode)
+def config_decode_bytes(c):
+    """Algorithmic bytes of one decode call of a case: KV read once + q and out + page-table entries."""
+    q, kc = c["query"], c["key_cache"]
+    batch, heads, dim = q.shape
+    _, bs, kv_heads, _ = kc.shape
+    lengths = [int(n) for n in c["context_lens"].tolist()]
+    es = q.element_size()
+    return (sum(lengths) * 2 * kv_heads * dim * es + 2 * batch * heads * dim * es
+            + 8 * sum(math.ceil(n / bs) for n in lengths))
+
+
+class CpuConfigReference:
+    """The reference's CPU path (oracle append + decode, restating data.py:67-81 and fallback.py:27-64) on a case."""
+
+    def __init__(self, c, label):
+        from oracle import kv_write, paged_decode
+
+        self.kv_write, self.paged_decode, self.c, self.label = kv_write, paged_decode, c, label
+        self.kc, self.vc = c["key_cache"].clone(), c["value_cache"].clone()
+        self.nbytes = config_decode_bytes(c)
+
+    def step(self):
+        c = self.c
+        self.kv_write.write_kv_cache_batch(self.kc, self.vc, c["block_tables"], c["token_offsets"], c["key"],
+                                           c["value"], c["block_size"])
+        self.paged_decode.paged_attention(c["query"], self.kc, self.vc, c["block_tables"], c["context_lens"],
+                                          c["block_size"])
+
+    def describe(self, seconds):
+        self.step()
+        done, start = 0, time.perf_counter()
+        while done < 2 or time.perf_counter() - start < seconds:
+            self.step()
+            done += 1
+        per_step = (time.perf_counter() - start) / done
+        threads = torch.get_num_threads()
+        return {"value": self.nbytes / per_step / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+                "ms_per_step": per_step * 1e3,
+                "sample": f"{done} steps of the oracle's append + decode on the whole of {self.label}, "
+                          f"torch threads={threads}"}
+
+
+def measure_decode_config(label, c, device, steps, warmup, cpu_seconds, peak):
+    """One BASELINE decode config at one GPU: KV append + paged decode, L2 flushed before every step.
+
+    Each replay of a CUDA graph writes a 256 MB buffer (more than the 126 MB L2), then runs the
+    step between events; a second graph times the decode launch alone (not chained to the append).
+    """
+    from myvllm_mini_engine_b200.kernels import paged_attention, write_kv_cache_batch
+
+    g = {k: (v.to(device) if isinstance(v, torch.Tensor) else v) for k, v in c.items()}
+    bs = g["block_size"]
+    nbytes = config_decode_bytes(c)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    events = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(4)]
+
+    def append():
+        write_kv_cache_batch(g["key_cache"], g["value_cache"], g["block_tables"], g["token_offsets"], g["key"],
+                             g["value"], bs, validate=False)
+
+    def decode(chained):
+        return paged_attention(g["query"], g["key_cache"], g["value_cache"], g["block_tables"], g["context_lens"],
+                               bs, validate=False, chained=chained)
+
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            append()
+            out = decode(True)
+    side.synchronize()
+    step_graph, launch_graph = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph, stream=side):
+        flush.fill_(1)
+        events[0].record()
+        append()
+        out = decode(True)
+        events[1].record()
+    with torch.cuda.graph(launch_graph, stream=side):
+        flush.fill_(1)
+        append()
+        events[2].record()
+        decode(False)
+        events[3].record()
+    for _ in range(warmup):
+        step_graph.replay()
+        launch_graph.replay()
+    torch.cuda.synchronize(device)
+    step_ms, launch_ms = [], []
+    for _ in range(max(1, min(steps, 200))):
+        step_graph.replay()
+        events[1].synchronize()
+        step_ms.append(events[0].elapsed_time(events[1]))
+        launch_graph.replay()
+        events[3].synchronize()
+        launch_ms.append(events[2].elapsed_time(events[3]))
+    del step_graph, launch_graph
+    step_avg, launch_avg = statistics.median(step_ms), statistics.median(launch_ms)
+    cpu = CpuConfigReference(c, label).describe(cpu_seconds)
+    achieved = nbytes / (launch_avg * 1e-3) / 1e9
+    return {"workload": label, "dtype": str(c["query"].dtype).replace("torch.", ""),
+            "value": nbytes / (step_avg * 1e-3) / 1e9, "unit": "GB/s (KV-read bytes / step time)",
+            "us_per_step": step_avg * 1e3, "decode_launch_us": launch_avg * 1e3, "bytes_per_launch": nbytes,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "frac": achieved / peak,
+                         "unit": "GB/s"},
+            "l2": "flushed (256 MB write) before every step", "steps": len(step_ms),
+            "cpu_baseline": cpu, "vs_cpu": (nbytes / (step_avg * 1e-3) / 1e9) / cpu["value"]}
+
+
+def run_configs(args, world, rank, local):
+    """BASELINE configs 1-3 (decode) and 4 (prefill) at one GPU, and config 5 (Qwen3 step) at every N.
+
+    Returns the fields to add to the headline line (rank 0), or None on other ranks.  Config 5 runs on
+    every rank, strong-scaled: 256 requests split over the ranks, each with its own KV pool.
+    """
+    import copy
+
+    sys.path.insert(0, str(ROOT / "tests" / "golden"))
+    import cases
+
+    extra = {}
+    device = torch.device("cuda", local)
+    peak, _ = measured_peaks()
+    if world == 1:
+        budget = min(args.cpu_seconds, 3.0)
+        for name, build, label in (
+                ("config1", cases.config1, "BASELINE config 1: fp32, 1 request, 128 cached + 1 appended, bs16"),
+                ("config2", cases.config2, "BASELINE config 2: fp16, 8 requests x 512 + 1, bs256"),
+                ("config3", cases.config3, "BASELINE config 3: bf16, 32 requests, contexts U[1,2048] seeded + 1, "
+                                           "bs16, pool 1.1x")):
+            extra[name] = measure_decode_config(label, build(), device, args.steps, args.warmup, budget, peak)
+        sub = copy.copy(args)
+        sub.workload, sub.steps, sub.cpu_seconds = "prefill", max(1, min(args.steps, 200)), min(args.cpu_seconds, 5.0)
+        line = run_prefill(sub, world, rank, local)
+        extra["config4"] = {k: line[k] for k in ("value", "unit", "ms_per_step", "prefill_tokens_s", "roofline", "e2e",
+                                                 "cpu_baseline", "clocks")}
+        extra["config4"]["workload"] = line["config"]["workload"]
+        extra["config4"]["vs_cpu"] = line["value"] / line["cpu_baseline"]["value"]
+    sub = copy.copy(args)
+    sub.workload, sub.batch, sub.context, sub.kv_dtype = "qwen3", 256, 4096, "bf16"
+    sub.steps = max(1, min(args.steps, 30))
+    try:
+        line = run_qwen3(sub, world, rank, local)
+    except SystemExit as error:
+        line = {"skipped": str(error)} if rank == 0 else None
+    if rank == 0 and line is not None:
+        keep = ("value", "unit", "ms_per_step", "scaling", "roofline", "step_roofline", "e2e", "projections",
+                "cpu_baseline", "gpu_launches", "clocks", "skipped")
+        extra["qwen3"] = {k: line[k] for k in keep if k in line}
+        if "config" in line:
+            extra["qwen3"]["workload"] = line["config"]["workload"] + f"; {256 // world} requests per GPU"
+        if "cpu_baseline" in line:
+            extra["qwen3"]["vs_cpu"] = line["value"] / line["cpu_baseline"]["value"]
+    return extra if rank == 0 else None
 
 
 def run_fp8(args, world, rank, local):
@@ -565,7 +745,11 @@ def run_fp8(args, world, rank, local):
                    "global_batch": args.batch * world, "seq_len": args.context,
                    "parallelism": f"request-sharded x{world} (independent KV pools)",
                    "l2": f"inputs {2 * kq.numel() / 1e6:.0f} MB per GPU > 126 MB L2"},
-        "decode_tok_s": world * args.batch / (ms_per_step * 1e-3),
+        "windows": {"count": repeats, "steps_each": args.steps, "ms_per_step_median": ms_per_step,
+                    "ms_per_step_min": per_step[0], "ms_per_step_max": per_step[-1]},
+        "layer_op_tok_s": world * args.batch / (ms_per_step * 1e-3),
+        "layer_op_tok_s_note": "requests served per second by ONE layer's append + decode (an operator rate); "
+                               "the model's decode tok/s is qwen3.value (BASELINE config 5, all 28 layers)",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": None,
                      "kernel": "fp8 paged decode, timed alone between events", "bytes_per_launch": step_bytes,
@@ -1042,6 +1226,10 @@ def main(argv=None):
                 line = run_fp8(args, world, rank, local)
             else:
                 line = run_ours(args, world, rank, local)
+                if not args.headline_only:
+                    extra = run_configs(args, world, rank, local)
+                    if rank == 0:
+                        line.update(extra)
         if line is not None and rank == 0:
             print(json.dumps(line), flush=True)
     finally:

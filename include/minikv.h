@@ -54,6 +54,15 @@ const char* minikv_last_error(void);
  * a bounded wait gives up.  New; the reference has no device status. */
 int minikv_device_status(unsigned int* status, int clear, void* stream);
 
+/* Synchronise `stream`, then set the limit (nanoseconds, default 2e9) of the
+ * waits in which a kernel's producer waits for its consumers to free a ring
+ * slot, on the current device.  When such a wait gives up, the kernel sets
+ * MINIKV_STATUS_WAIT_TIMEOUT, issues no more copies, waits for the copies it
+ * has issued and runs to its end (outputs of that call are undefined).  A short
+ * limit lets a test drive that path without a hang or a fault; production
+ * callers leave the default.  New; the reference's kernels have no bounded waits. */
+int minikv_set_wait_limit(uint64_t limit_ns, void* stream);
+
 /* ---------------------------------------------------------------- decode ---
  * Split-KV decode attention over paged K/V (GQA: q head h reads kv head
  * h / (q_heads / kv_heads)).  out[b, h] = softmax(q[b,h] . K^T / sqrt(D)) V over

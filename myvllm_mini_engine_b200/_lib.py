@@ -31,6 +31,7 @@ SIGNATURES = {
     "minikv_source_hash": (ctypes.c_char_p, []),
     "minikv_last_error": (ctypes.c_char_p, []),
     "minikv_device_status": (_int, [ctypes.POINTER(ctypes.c_uint), _int, _p]),
+    "minikv_set_wait_limit": (_int, [ctypes.c_uint64, _p]),
     "minikv_paged_decode_workspace_bytes": (_i64, [_i64] * 7 + [_int]),
     "minikv_paged_decode": (_int, [_p] * 6 + [_p, _i64] + [_i64] * 7 + [_int, _p]),
     "minikv_paged_decode_chained": (_int, [_p] * 6 + [_p, _i64] + [_i64] * 7 + [_int, _p]),
@@ -141,3 +142,14 @@ def device_status(device=None, *, clear=True) -> int:
     with torch.cuda.device(device):
         check(lib.minikv_device_status(ctypes.byref(value), int(clear), stream_of(device)), "device status")
     return value.value
+
+
+DEFAULT_WAIT_LIMIT_NS = 2_000_000_000
+
+
+def set_wait_limit(limit_ns: int, device=None) -> None:
+    """Limit of the kernels' slot waits (see ``minikv_set_wait_limit``); tests shorten it to drive the timeout path."""
+    lib = load()
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(device):
+        check(lib.minikv_set_wait_limit(int(limit_ns), stream_of(device)), "set_wait_limit")

@@ -115,6 +115,16 @@ int minikv_device_status(unsigned int* status, int clear, void* stream) {
     return MINIKV_OK;
 }
 
+int minikv_set_wait_limit(uint64_t limit_ns, void* stream) {
+    MINIKV_REQUIRE(limit_ns > 0, MINIKV_EINVAL, "the wait limit must be positive");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const unsigned long long value = limit_ns;
+    cudaError_t err = cudaStreamSynchronize(s);  // no kernel of the stream runs while the limit changes
+    if (err == cudaSuccess) err = cudaMemcpyToSymbol(g_space_wait_limit_ns, &value, sizeof(value));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_set_wait_limit");
+    return MINIKV_OK;
+}
+
 // ------------------------------------------------------------------- decode
 static int check_decode_shapes(int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
                                int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype) {

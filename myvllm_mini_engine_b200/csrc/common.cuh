@@ -3,8 +3,18 @@
 // * element traits: 16-byte vectors of fp32 / fp16 / bf16 <-> fp32 registers;
 // * mbarrier + 1-D bulk-copy (TMA engine) wrappers in inline PTX;
 // * bounded waits: every spin on an mbarrier polls with try_wait and gives up
-//   after two seconds of %globaltimer time, records an error bit in the device
-//   status word and lets the kernel run to its end.
+//   after a limit of %globaltimer time (2 s), records an error bit in the device
+//   status word and lets the kernel run to its end.  Three kinds:
+//     mbar_wait        data waits (copies or MMAs landing);
+//     mbar_wait_space  a producer waiting for consumers to free a ring slot;
+//                      its limit is g_space_wait_limit_ns, which the host can
+//                      shorten (minikv_set_wait_limit) to exercise this path;
+//     mbar_drain       a thread waiting for the copies or MMAs it issued itself
+//                      before its CTA exits (no early give-up).
+//   After a failed space wait a producer issues nothing more and drains what
+//   it has issued; after a failed data wait a consumer skips that stage's
+//   data (it may still be landing) but keeps its arrivals, so the CTA always
+//   exits with no copy or MMA in flight.
 #pragma once
 
 #include <cuda.h>
@@ -137,10 +147,19 @@ __device__ __forceinline__ uint64_t global_ns() {
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 constexpr uint64_t kWaitCheckNs = 200000ull;       // 200 us: from here on, check for another timeout
 
+// Limit of the space waits (mbar_wait_space); minikv_set_wait_limit changes it.
+__device__ unsigned long long g_space_wait_limit_ns = kWaitLimitNs;
+
+__device__ __forceinline__ bool status_timed_out() {
+    return (*reinterpret_cast<volatile unsigned int*>(&g_status) & kStatusWaitTimeout) != 0;
+}
+
 // Bounded wait for the phase with the given parity.  Returns false (and sets
-// the status bit) if the phase did not complete within kWaitLimitNs; callers
-// then carry on so that the kernel reaches its end instead of hanging the GPU.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+// the status bit) if the phase did not complete within `limit`; with
+// `early_out`, a wait that has lasted kWaitCheckNs also gives up when another
+// wait already timed out, so a broken pipeline costs one limit, not one per
+// wait.  Callers then carry on so that the kernel reaches its end.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, uint64_t limit, bool early_out) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = global_ns();
     for (;;) {
@@ -148,14 +167,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
         for (int i = 0; i < 32; ++i)
             if (mbar_try_wait(bar, parity)) return true;
         const uint64_t waited = global_ns() - start;
-        if (waited > kWaitLimitNs) break;
-        // A wait this long is already abnormal: give up at once if another one
-        // has timed out, so a broken pipeline costs one limit, not one per wait.
-        if (waited > kWaitCheckNs && (*reinterpret_cast<volatile unsigned int*>(&g_status) & kStatusWaitTimeout))
-            return false;
+        if (waited > limit) break;
+        if (early_out && waited > kWaitCheckNs && status_timed_out()) return false;
     }
     raise_status(kStatusWaitTimeout);
     return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, kWaitLimitNs, true);
+}
+
+__device__ __forceinline__ bool mbar_wait_space(uint64_t* bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, *reinterpret_cast<volatile unsigned long long*>(&g_space_wait_limit_ns),
+                         true);
+}
+
+__device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {
+    return mbar_wait_for(bar, parity, kWaitLimitNs, false);
 }
 
 // 1-D bulk copy global -> shared through the TMA engine; completion is

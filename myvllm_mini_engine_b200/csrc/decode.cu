@@ -456,8 +456,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
         const unsigned char* kbase = static_cast<const unsigned char*>(p.kc) + (size_t)h0 * D * esize;
         const unsigned char* vbase = static_cast<const unsigned char*>(p.vc) + (size_t)h0 * D * esize;
         const uint64_t tile_bits = (TT == 64) ? ~0ull : ((1ull << TT) - 1);
-        int gt = 0;
-        for (int w0 = tile_lo; w0 < tile_hi; w0 += kWindowTiles) {
+        int gt = 0;           // tiles issued
+        bool stopped = false;  // a space wait gave up: issue nothing more
+        for (int w0 = tile_lo; w0 < tile_hi && !stopped; w0 += kWindowTiles) {
             // Rows of tiles w0 .. w0+31: lane i resolves tile w0+i, one table
             // load per page, all lanes' loads in flight together.
             const int t = w0 + lane;
@@ -486,7 +487,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
             const int count = min(kWindowTiles, tile_hi - w0);
             for (int i = 0; i < count; ++i, ++gt) {
                 const int slot = gt % NS;
-                if (gt >= NS) mbar_wait(&empty[slot], ((gt / NS) - 1) & 1);
+                if (gt >= NS && !__all_sync(0xffffffffu, mbar_wait_space(&empty[slot], ((gt / NS) - 1) & 1))) {
+                    stopped = true;  // the consumers may still read this slot
+                    break;
+                }
                 int row[2];
                 bool ok[2];
 #pragma unroll
@@ -552,6 +556,12 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
             }
             __syncwarp();
         }
+        // Drain: the last phase issued into each slot has landed before this warp
+        // exits, so no bulk copy is in flight when the CTA releases its shared memory
+        // (on the normal path these phases are complete or about to be).
+        if (lane == 0)
+            for (int s2 = 0; s2 < NS && s2 < gt; ++s2) mbar_drain(&full[s2], ((s2 + NS * ((gt - 1 - s2) / NS)) / NS) & 1);
+        __syncwarp();
         return;
     }
 
@@ -570,8 +580,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
         if (active) cons.begin(static_cast<const T*>(p.q) + ((int64_t)b * p.q_heads + qh0) * D, item_heads);
         for (int k = t - prefix[b]; k < seg_hi - prefix[b]; ++k, ++gt) {
             const int slot = gt % NS;
-            mbar_wait(&full[slot], (gt / NS) & 1);
-            if (active) {
+            // a stage whose wait gave up is skipped (its copies may still be landing); the
+            // arrival below still happens, so the ticket protocol and the ring stay consistent
+            const bool landed = __all_sync(0xffffffffu, mbar_wait(&full[slot], (gt / NS) & 1));
+            if (active && landed) {
                 const unsigned char* ks = smem + slot * stage_bytes + local_head * D * esize;
                 cons.tile(ks, ks + TT * stride, stride, TT, min(TT, len - k * TT), masks[slot], p.scale_log2);
             }

@@ -177,6 +177,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     // the producer rewrites a slot for tile g + 4 only after S(g + 2), which
     // needs the softmax of tile g to have read its S buffer (and these words)
     uint32_t* key_ok = reinterpret_cast<uint32_t*>(bar + 18);
+    uint64_t* mma_drain = bar + 26;  // the issuer's last commit: every MMA it issued has completed
     int* qt_pfx = reinterpret_cast<int*>(smem + L::OFF_PFX);         // [requests + 1]
     uint32_t* order = reinterpret_cast<uint32_t*>(smem + L::OFF_ORD);  // [kPfMaxSort] sorted keys, then the keys
 
@@ -220,6 +221,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
         }
         mbar_init(p_full, 8);
         mbar_init(o_done, 1);
+        mbar_init(mma_drain, 1);
         mbar_init_fence();
     }
     if (warp == 1) {
@@ -271,18 +273,26 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
         uint64_t* empty = is_v ? v_empty : k_empty;
         const CUtensorMap* map = is_v ? &tm_v : &tm_k;
         unsigned char* ring = is_v ? sV : sK;
-        int gt = 0, active = 0;
-        for (int k = 0;; ++k) {
+        int gt = 0, active = 0;  // key tiles issued, items whose Q was issued
+        bool stopped = false;    // a space wait gave up: issue nothing more, drain, exit
+        for (int k = 0; !stopped; ++k) {
             const int it = pf_nth_item(k, c, nC, n_items);
             if (it < 0) break;
             const PfItem w = pf_item(p, qt_pfx, order, sorted, it, Hkv);
             if (w.n_tiles == 0) continue;
-            if (!is_v && lane == 0) {
-                if (active > 0) mbar_wait(q_empty, (active - 1) & 1);
-                mbar_arrive_expect_tx(q_full, (uint32_t)L::Q_BYTES);
+            if (!is_v) {
+                int q_ok = 1;
+                if (lane == 0) {
+                    if (active > 0) q_ok = mbar_wait_space(q_empty, (active - 1) & 1) ? 1 : 0;
+                    if (q_ok) {
+                        mbar_arrive_expect_tx(q_full, (uint32_t)L::Q_BYTES);
 #pragma unroll
-                for (int kb = 0; kb < L::KB; ++kb)
-                    tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, w.h * G, (int)(w.q0 + w.t_lo), q_full);
+                        for (int kb = 0; kb < L::KB; ++kb)
+                            tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, w.h * G, (int)(w.q0 + w.t_lo),
+                                        q_full);
+                    }
+                }
+                if (!__shfl_sync(full_mask, q_ok, 0)) break;
             }
             // Page-table entry of this lane's box of tile j (-1: no box).  The entry of
             // tile j + 2 is loaded while tile j is issued and checked an iteration
@@ -319,7 +329,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                     }
                 }
                 const uint32_t bytes = (uint32_t)__popc(__ballot_sync(full_mask, valid)) * L::KB * R * 128;
-                if (gt >= 2) mbar_wait(&empty[slot], ((gt >> 1) - 1) & 1);
+                if (gt >= 2 && !__all_sync(full_mask, mbar_wait_space(&empty[slot], ((gt >> 1) - 1) & 1))) {
+                    stopped = true;  // the MMAs may still read this slot
+                    break;
+                }
                 if (box == 0) {
                     if (!is_v) {
 #pragma unroll
@@ -340,6 +353,13 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
             }
             ++active;
         }
+        // Drain: the last phase issued into each slot (and Q's) has landed before this
+        // warp exits, so no TMA copy is in flight when the CTA releases its shared memory.
+        if (lane == 0) {
+            for (int s2 = 0; s2 < 2 && s2 < gt; ++s2) mbar_drain(&full[s2], ((s2 + 2 * ((gt - 1 - s2) / 2)) >> 1) & 1);
+            if (!is_v && active > 0) mbar_drain(q_full, (active - 1) & 1);
+        }
+        __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         // S(j) and P V(j) are issued in whichever order their operands become
@@ -419,6 +439,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                 gt += n_tiles;
                 ++active;
             }
+            // every MMA issued above has completed before TMEM is released (and before
+            // the shared-memory operands it reads go away)
+            umma_commit(mma_drain);
+            mbar_drain(mma_drain, 0);
         }
     } else {
         // ------------------------------------------------------------ softmax warps
@@ -536,10 +560,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                 l_run = l_run * alpha + ((sums[0] + sums[1]) + (sums[2] + sums[3]));
                 m_run = m_use;
                 const int vrow_key = st & 127;
-                if (!((wk[vrow_key >> 5] >> (vrow_key & 31)) & 1u)) {
+                if (!((wk[vrow_key >> 5] >> (vrow_key & 31)) & 1u) && mbar_wait(&v_full[slot], (gj >> 1) & 1)) {
                     // V rows of masked keys must be finite zeros before P V runs (a
                     // loaded box can hold rows past the context; unloaded rows hold stale data)
-                    mbar_wait(&v_full[slot], (gj >> 1) & 1);
                     unsigned char* vrow = sV + slot * L::KV_BYTES + vrow_key * 128;
                     for (int kb = st >> 7; kb < L::KB; kb += 2) {
                         uint4* v4 = reinterpret_cast<uint4*>(vrow + kb * L::BLOCK_BYTES);

@@ -266,3 +266,65 @@ def test_staged_decode_graph_serves_fewer_requests_than_its_batch(cuda_device):
     with pytest.raises(ValueError):
         graph.load(ids, positions, tables)
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("batch", [32, 256], ids=["per-gpu-share-32x4096", "one-gpu-256x4096"])
+def test_config5_greedy_ids_at_full_context(cuda_device, batch):
+    """BASELINE config 5 itself: Qwen3-0.6B architecture, N(0, 0.02) weights, every request at
+    context 4096, block 16; 32 requests (the per-GPU share at 8 GPUs, fused tcgen05 projections)
+    and 256 (the whole batch on one GPU, cuBLAS projections).
+
+    One pool serves both paths, so every step compares them on the same KV state: the rows a
+    step appends are saved, the step under test runs, its appended rows are kept aside and
+    the saved rows put back, then the reference model (torch backends, same GPU, same
+    weights) runs the step on that state.  Both continue from the reference's greedy tokens.
+    Per step and request: logits within the step tolerance, appended K/V rows within it, and
+    greedy ids equal unless the request is a near-tie (reference top-2 margin at most twice
+    that request's largest logit difference, the only way rounding can flip an argmax); the
+    counts are printed and near-ties are bounded.
+    """
+    cfg = Qwen3Config.qwen3_0_6b()
+    context, steps, bs = 4096, 3, 16
+    pages = (context + steps + bs - 1) // bs
+    blocks = batch * pages
+    need = 2 * cfg.num_hidden_layers * blocks * bs * cfg.num_key_value_heads * cfg.head_dim * 2
+    free, _ = torch.cuda.mem_get_info()
+    assert need + (12 << 30) < free, f"config 5 pool of {need / 1e9:.0f} GB needs a B200's memory"
+    weights = Qwen3Weights.random(cfg, dtype=torch.bfloat16, device="cuda", seed=50)
+    gen = torch.Generator(device="cuda").manual_seed(51)
+    pool = PagedKVPool(cfg.num_hidden_layers, blocks, bs, cfg.num_key_value_heads, cfg.head_dim,
+                       dtype=torch.bfloat16, device="cuda")
+    pool.storage.normal_(generator=gen)
+    tables = torch.randperm(blocks, device="cuda", generator=gen).view(batch, pages).contiguous()
+    ids = torch.randint(0, cfg.vocab_size, (batch,), device="cuda", generator=gen)
+    positions = torch.full((batch,), context, dtype=torch.int64, device="cuda")
+    step = Qwen3DecodeStep(cfg, weights, pool)
+    assert step.fused_projections == (batch <= Qwen3DecodeStep.FUSED_MAX_BATCH)
+    equal_total, near_ties, worst = 0, 0, 0.0
+    for i in range(steps):
+        pages_i, slots = tables.gather(1, (positions // bs)[:, None]).squeeze(1), positions % bs
+        saved = pool.key[:, pages_i, slots].clone(), pool.value[:, pages_i, slots].clone()
+        logits = step.forward_decode_batch(ids, tables, positions)
+        ours_rows = pool.key[:, pages_i, slots].clone(), pool.value[:, pages_i, slots].clone()
+        pool.key[:, pages_i, slots], pool.value[:, pages_i, slots] = saved
+        expected = ref.decode_step(cfg, weights, ids, pool.key, pool.value, tables, positions)
+        torch.testing.assert_close(logits.float(), expected.float(), atol=ATOL, rtol=RTOL)
+        for mine, theirs in zip(ours_rows, (pool.key[:, pages_i, slots], pool.value[:, pages_i, slots])):
+            torch.testing.assert_close(mine.float(), theirs.float(), atol=ATOL, rtol=RTOL)
+        diff = (logits.float() - expected.float()).abs().amax(-1)
+        margin = ref.top2_margin(expected)
+        ours_ids, ref_ids = logits.argmax(-1), expected.argmax(-1)
+        same = ours_ids == ref_ids
+        tie = margin <= 2 * diff
+        assert bool((same | tie).all()), f"step {i}: ids differ beyond the near-tie margin"
+        equal_total += int(same.sum())
+        near_ties += int(tie.sum())
+        worst = max(worst, float(diff.max()))
+        print(f"config 5, {batch} x {context}, step {i}: identical greedy ids {int(same.sum())}/{batch}, "
+              f"near-ties {int(tie.sum())} (of which differing {int((~same).sum())}), "
+              f"largest |dlogit| {float(diff.max()):.4f}")
+        ids, positions = ref_ids, positions + 1
+    print(f"config 5, {batch} x {context}: {equal_total}/{batch * steps} identical greedy ids over {steps} steps, "
+          f"{near_ties} near-ties, largest |dlogit| {worst:.4f}")
+    assert batch * steps - equal_total <= max(1, batch * steps // 50)  # differing ids: at most 2%, all near-ties
+    assert _lib.device_status() == 0

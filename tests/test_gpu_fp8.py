@@ -254,3 +254,40 @@ def test_ragged_prefill_over_fp8_pool_matches_oracle(cuda_device, fmt):
     assert out.dtype == c["q"].dtype and out.shape == c["q"].shape
     assert_close(out, expected, c["q"].dtype)
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
+def test_ragged_prefill_over_fp8_pool_in_several_chunks(cuda_device, dtype):
+    """More packed tokens than one launch chunk of the CUDA-core route (4096 query rows): the chunk
+    loop (ticket reset per chunk, q/out offsets, a shorter last chunk) over a small-head model,
+    fp16 and bf16 queries, both formats."""
+    from myvllm_mini_engine_b200.engine import PrefillBatch
+    from myvllm_mini_engine_b200.kernels import paged_prefill_attention_fp8
+    from oracle import prefill as prefill_oracle
+
+    gen = np.random.default_rng(61)
+    bs, heads, kv_heads, dim = 16, 2, 1, 64
+    starts = [0, 48, 3, 200]
+    chunks = [2500, 1800, 700, 1333]  # 6333 packed tokens: two chunks of the route
+    pages = [(s + n + bs - 1) // bs for s, n in zip(starts, chunks)]
+    blocks = sum(pages) + 3
+    perm = gen.permutation(blocks).tolist()
+    tables, at = [], 0
+    for n in pages:
+        tables.append(perm[at:at + n])
+        at += n
+    tokens = [gen.integers(0, 1000, size=n).tolist() for n in chunks]
+    batch = PrefillBatch.from_sequences(tokens, tables, starts, block_size=bs, num_blocks=blocks, device="cuda")
+    q = torch.from_numpy(gen.standard_normal((sum(chunks), heads, dim), dtype=np.float32)).to(dtype)
+    cache = torch.from_numpy(gen.standard_normal((2, blocks, bs, kv_heads, dim), dtype=np.float32))
+    meta = (batch.cu_seqlens_q, batch.query_starts, batch.block_tables, batch.context_lens)
+    for fmt in ("e4m3", "e5m2"):
+        kq = torch.from_numpy(fp8_kv.quantize(cache[0], K_SCALE, fmt))
+        vq = torch.from_numpy(fp8_kv.quantize(cache[1], V_SCALE, fmt))
+        out = paged_prefill_attention_fp8(q.cuda(), kq.cuda(), vq.cuda(), *meta, bs, K_SCALE, V_SCALE, kv_format=fmt)
+        expected = prefill_oracle.paged_prefill_fp32(q.float(), fp8_kv.dequantize(kq, K_SCALE, fmt),
+                                                     fp8_kv.dequantize(vq, V_SCALE, fmt), *(t.cpu() for t in meta),
+                                                     bs)
+        assert out.dtype == dtype and out.shape == q.shape
+        assert_close(out, expected, dtype)
+    assert _lib.device_status() == 0
