@@ -108,6 +108,26 @@ int minikv_paged_decode_chained(const void* query, const void* key_cache, const 
                                 int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
                                 int64_t table_width, int dtype, void* stream);
 
+/* KV append and decode attention in one launch: the result of
+ * minikv_kv_append_batch(key/value at token_offsets) followed by
+ * minikv_paged_decode over context_lens = token_offsets + 1, with the same
+ * guards.  key/value: [batch, kv_heads, head_dim], contiguous.  The new row of
+ * request b is written to its pool slot (bit-exact, skipped when the offset
+ * is negative, beyond the table or on an invalid page) by the CTA that
+ * attends it, which reads it from key/value instead of the pool.  16-bit and
+ * fp32 pools; workspace as for minikv_paged_decode (same size).  chained != 0:
+ * token_offsets and block_tables were written before the previous kernel on
+ * the stream started (key/value may come from that kernel), as for
+ * minikv_paged_decode_chained.  Replaces the two launches of
+ * Attention.forward_decode_batch (mini_engine/model/native_qwen3.py:188-196:
+ * write_kv_cache_batch, then paged_attention over positions + 1). */
+int minikv_paged_decode_append(const void* query, const void* key_cache, const void* value_cache,
+                               const int64_t* block_tables, const int64_t* token_offsets, const void* key,
+                               const void* value, void* out, void* workspace, int64_t workspace_bytes,
+                               int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                               int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype, int chained,
+                               void* stream);
+
 /* Same decode attention, for callers that cannot allocate device memory when
  * they call (a CUDA graph being captured under a framework that owns every
  * allocation, a serving loop that bans cudaMalloc after start-up, a cgo/JNI

@@ -35,6 +35,7 @@ SIGNATURES = {
     "minikv_paged_decode_workspace_bytes": (_i64, [_i64] * 7 + [_int]),
     "minikv_paged_decode": (_int, [_p] * 6 + [_p, _i64] + [_i64] * 7 + [_int, _p]),
     "minikv_paged_decode_chained": (_int, [_p] * 6 + [_p, _i64] + [_i64] * 7 + [_int, _p]),
+    "minikv_paged_decode_append": (_int, [_p] * 8 + [_p, _i64] + [_i64] * 7 + [_int, _int, _p]),
     "minikv_paged_decode_noalloc": (_int, [_p] * 6 + [_i64] * 7 + [_int, _p]),
     "minikv_kv_scatter_slots": (_int, [_p] * 5 + [_i64] * 7 + [_int, _p]),
     "minikv_kv_scatter_slots_fp8": (_int, [_p] * 5 + [_i64] * 7 + [_f32, _f32, _int, _int, _p]),

@@ -184,6 +184,24 @@ int minikv_paged_decode_chained(const void* query, const void* key_cache, const 
                       table_width, dtype, static_cast<cudaStream_t>(stream), true);
 }
 
+int minikv_paged_decode_append(const void* query, const void* key_cache, const void* value_cache,
+                               const int64_t* block_tables, const int64_t* token_offsets, const void* key,
+                               const void* value, void* out, void* workspace, int64_t workspace_bytes,
+                               int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                               int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype, int chained,
+                               void* stream) {
+    int rc = check_decode_shapes(batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype);
+    if (rc) return rc;
+    MINIKV_REQUIRE(query && key_cache && value_cache && block_tables && token_offsets && key && value && out,
+                   MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(query) && aligned16(key_cache) && aligned16(value_cache) && aligned16(out) &&
+                       aligned16(key) && aligned16(value),
+                   MINIKV_EINVAL, "query, caches, new K/V rows and output must be 16-byte aligned");
+    return run_decode(query, key_cache, value_cache, block_tables, token_offsets, nullptr, out, workspace,
+                      workspace_bytes, batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width,
+                      dtype, static_cast<cudaStream_t>(stream), chained != 0, key, value);
+}
+
 // ---------------------------------------------------------------- KV writes
 static int check_rows(const void* kc, const void* vc, const void* k, const void* v, int64_t kv_heads,
                       int64_t head_dim, int64_t k_stride, int64_t v_stride, int dtype) {

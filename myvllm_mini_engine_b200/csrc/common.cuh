@@ -163,9 +163,9 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t* bar, uint32_t parity, ui
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t start = global_ns();
     for (;;) {
-#pragma unroll 1
-        for (int i = 0; i < 32; ++i)
-            if (mbar_try_wait(bar, parity)) return true;
+        // one probe between clock reads: a probe can suspend the thread for a
+        // hardware-defined interval, so limits below a microsecond stay meaningful
+        if (mbar_try_wait(bar, parity)) return true;
         const uint64_t waited = global_ns() - start;
         if (waited > limit) break;
         if (early_out && waited > kWaitCheckNs && status_timed_out()) return false;
@@ -178,9 +178,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return mbar_wait_for(bar, parity, kWaitLimitNs, true);
 }
 
-__device__ __forceinline__ bool mbar_wait_space(uint64_t* bar, uint32_t parity) {
-    return mbar_wait_for(bar, parity, *reinterpret_cast<volatile unsigned long long*>(&g_space_wait_limit_ns),
-                         true);
+// The space-wait limit, read once per kernel by the producers.
+__device__ __forceinline__ uint64_t space_wait_limit() {
+    return *reinterpret_cast<volatile unsigned long long*>(&g_space_wait_limit_ns);
+}
+
+__device__ __forceinline__ bool mbar_wait_space(uint64_t* bar, uint32_t parity, uint64_t limit) {
+    if (limit >= kWaitCheckNs) return mbar_wait_for(bar, parity, limit, true);
+    // a short limit (a test of the timeout path): non-blocking probes between clock reads, so the
+    // limit is not hidden by the suspend interval of a blocking probe
+    if (mbar_test_wait(bar, parity)) return true;
+    const uint64_t start = global_ns();
+    while (!mbar_test_wait(bar, parity)) {
+        if (global_ns() - start > limit) {
+            raise_status(kStatusWaitTimeout);
+            return false;
+        }
+    }
+    return true;
 }
 
 __device__ __forceinline__ bool mbar_drain(uint64_t* bar, uint32_t parity) {

@@ -69,6 +69,10 @@ struct DecodeParams {
     int early_prologue;   // 1: lens/tables predate the previous kernel; read them before griddep_wait
     int coalesce;         // 1: rows unpadded and the CTA holds every kv head: one bulk copy per run of
                           //    consecutive physical rows (fp8 pool only)
+    int append;           // 1: fused KV append.  `lens` holds token offsets: request b appends new_k[b] /
+                          //    new_v[b] at position lens[b] and attends lens[b] + 1 tokens
+    const void* new_k;    // [batch, kv_heads, D] rows appended (append mode)
+    const void* new_v;
     float scale_log2;     // log2(e) / sqrt(D) (times the key scale for an fp8 pool)
     float out_scale;      // fp8 pool: the value scale, applied to the output (unused otherwise)
 };
@@ -87,15 +91,16 @@ __device__ __forceinline__ void consumers_sync() {
 }
 
 // lens_s[b] = usable length (0 when out of range); prefix[0..B] = exclusive
-// prefix of per-request tile counts.  All threads of the CTA take part.
+// prefix of per-request tile counts.  All threads of the CTA take part.  With
+// `plus_one`, lens[] holds append offsets and the length is offset + 1.
 __device__ void tile_prefix(const int64_t* __restrict__ lens, int B, int64_t cap, int TT, int* prefix,
-                            int* lens_s, int* warp_sums) {
+                            int* lens_s, int* warp_sums, int plus_one = 0) {
     const int tid = threadIdx.x, nthreads = blockDim.x, lane = tid & 31, warp = tid >> 5;
     const int per = (B + nthreads - 1) / nthreads;
     const int lo = min(B, tid * per), hi = min(B, lo + per);
     int local = 0;
     for (int i = lo; i < hi; ++i) {
-        const int64_t len = lens[i];
+        const int64_t len = lens[i] + plus_one;
         const int usable = (len > 0 && len <= cap) ? (int)len : 0;
         lens_s[i] = usable;
         local += (usable + TT - 1) / TT;
@@ -405,7 +410,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
     // one leave and stream its weights; it waits for this grid before reading
     // what the grid writes.
     griddep_launch_dependents();
-    tile_prefix(p.lens, B, cap, TT, prefix, lens_s, warp_sums);
+    tile_prefix(p.lens, B, cap, TT, prefix, lens_s, warp_sums, p.append);
     if (tid == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(&full[s], 1);
@@ -453,15 +458,21 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
     if (warp == kConsumerWarps) {
         // ------------------------------------------------------------ producer
         const uint64_t policy = policy_evict_first();
+        const uint64_t space_limit = space_wait_limit();
         const unsigned char* kbase = static_cast<const unsigned char*>(p.kc) + (size_t)h0 * D * esize;
         const unsigned char* vbase = static_cast<const unsigned char*>(p.vc) + (size_t)h0 * D * esize;
         const uint64_t tile_bits = (TT == 64) ? ~0ull : ((1ull << TT) - 1);
+        // fused append: the new rows of this CTA's heads (row stride: every kv head of a request)
+        const int new_row = p.kv_heads * D * esize;
+        const unsigned char* knew = static_cast<const unsigned char*>(p.new_k) + (size_t)h0 * D * esize;
+        const unsigned char* vnew = static_cast<const unsigned char*>(p.new_v) + (size_t)h0 * D * esize;
         int gt = 0;           // tiles issued
         bool stopped = false;  // a space wait gave up: issue nothing more
         for (int w0 = tile_lo; w0 < tile_hi && !stopped; w0 += kWindowTiles) {
             // Rows of tiles w0 .. w0+31: lane i resolves tile w0+i, one table
             // load per page, all lanes' loads in flight together.
             const int t = w0 + lane;
+            int append_dst = -1, append_b = 0;  // fused append: pool row this lane's tile writes, its request
             if (t < tile_hi) {
                 const int b = request_of_tile(prefix, B, t);
                 const int k = t - prefix[b];
@@ -480,14 +491,42 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                     for (int r = 0; r < run; ++r) rows[j + r] = ok ? base + r : -1;
                     j += run;
                 }
+                // Fused append: the last token of the request's last tile is the new one.  It is
+                // staged from the source row (entry -2 - b) and written to its pool row below.
+                if (p.append && t0 + n == lens_s[b] && rows[n - 1] >= 0) {
+                    append_dst = rows[n - 1];
+                    append_b = b;
+                    rows[n - 1] = -2 - b;
+                }
                 for (; j < TT; ++j) rows[j] = -1;
             }
             __syncwarp();
             if (p.early_prologue && w0 == tile_lo) griddep_wait();  // KV rows may come from the previous kernel
+            if (p.append) {
+                // write this window's appended rows (this CTA's heads) into the pool: every
+                // lane copies 16 bytes at a time of one row after the other; bit-exact copies
+                unsigned pending = __ballot_sync(0xffffffffu, append_dst >= 0);
+                unsigned char* kpool = const_cast<unsigned char*>(kbase);
+                unsigned char* vpool = const_cast<unsigned char*>(vbase);
+                while (pending) {
+                    const int from = __ffs(pending) - 1;
+                    pending &= pending - 1;
+                    const int64_t dst = __shfl_sync(0xffffffffu, append_dst, from);
+                    const int64_t src = __shfl_sync(0xffffffffu, append_b, from);
+                    const uint4* ks = reinterpret_cast<const uint4*>(knew + src * new_row);
+                    const uint4* vs = reinterpret_cast<const uint4*>(vnew + src * new_row);
+                    uint4* kd = reinterpret_cast<uint4*>(kpool + dst * cache_row);
+                    uint4* vd = reinterpret_cast<uint4*>(vpool + dst * cache_row);
+                    for (int v = lane; v < copy_row / 16; v += 32) {
+                        kd[v] = ld_global_nc(ks + v);
+                        vd[v] = ld_global_nc(vs + v);
+                    }
+                }
+            }
             const int count = min(kWindowTiles, tile_hi - w0);
             for (int i = 0; i < count; ++i, ++gt) {
                 const int slot = gt % NS;
-                if (gt >= NS && !__all_sync(0xffffffffu, mbar_wait_space(&empty[slot], ((gt / NS) - 1) & 1))) {
+                if (gt >= NS && !__all_sync(0xffffffffu, mbar_wait_space(&empty[slot], ((gt / NS) - 1) & 1, space_limit))) {
                     stopped = true;  // the consumers may still read this slot
                     break;
                 }
@@ -497,7 +536,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                 for (int h = 0; h < 2; ++h) {
                     const int j = lane + 32 * h;
                     row[h] = j < TT ? window[i * TT + j] : -1;
-                    ok[h] = row[h] >= 0;
+                    ok[h] = row[h] != -1;  // a pool row, or (append) -2 - b: request b's new row
                 }
                 const uint64_t mask = (uint64_t)__ballot_sync(0xffffffffu, ok[0]) |
                                       ((uint64_t)__ballot_sync(0xffffffffu, ok[1]) << 32);
@@ -549,8 +588,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                         if (!ok[h]) continue;
                         const int j = lane + 32 * h;
                         const int64_t r = row[h];
-                        bulk_load(kdst + j * stride, kbase + r * cache_row, copy_row, &full[slot], policy);
-                        bulk_load(vdst + j * stride, vbase + r * cache_row, copy_row, &full[slot], policy);
+                        const unsigned char* ksrc = r >= 0 ? kbase + r * cache_row : knew + (-2 - r) * new_row;
+                        const unsigned char* vsrc = r >= 0 ? vbase + r * cache_row : vnew + (-2 - r) * new_row;
+                        bulk_load(kdst + j * stride, ksrc, copy_row, &full[slot], policy);
+                        bulk_load(vdst + j * stride, vsrc, copy_row, &full[slot], policy);
                     }
                 }
             }
@@ -776,7 +817,8 @@ static int run_decode(const void* query, const void* key_cache, const void* valu
                       const int64_t* block_tables, const int64_t* context_lens, const int64_t* table_rows,
                       void* out, void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
                       int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
-                      int64_t table_width, int dtype, cudaStream_t stream, bool early_prologue = false) {
+                      int64_t table_width, int dtype, cudaStream_t stream, bool early_prologue = false,
+                      const void* new_k = nullptr, const void* new_v = nullptr) {
     DecodePlan plan;
     if (!make_decode_plan(batch, q_heads, kv_heads, head_dim, block_size, table_width, dtype, sm_count(), &plan))
         return fail(MINIKV_EUNSUPPORTED, "decode shape does not fit shared memory (batch too large?)");
@@ -790,6 +832,12 @@ static int run_decode(const void* query, const void* key_cache, const void* valu
                                          table_width, plan);
     DecodeParams q = p;
     q.early_prologue = early_prologue ? 1 : 0;
+    if (new_k != nullptr) {  // fused append: context_lens holds the token offsets
+        if (plan.coalesce) return fail(MINIKV_EUNSUPPORTED, "fused KV append needs a 16-bit or fp32 pool");
+        q.append = 1;
+        q.new_k = new_k;
+        q.new_v = new_v;
+    }
     const cudaError_t err = launch_decode(dtype, (int)head_dim, q, plan, stream);
     if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_decode launch");
     return MINIKV_OK;

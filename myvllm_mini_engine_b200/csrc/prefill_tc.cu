@@ -273,6 +273,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
         uint64_t* empty = is_v ? v_empty : k_empty;
         const CUtensorMap* map = is_v ? &tm_v : &tm_k;
         unsigned char* ring = is_v ? sV : sK;
+        const uint64_t space_limit = space_wait_limit();
         int gt = 0, active = 0;  // key tiles issued, items whose Q was issued
         bool stopped = false;    // a space wait gave up: issue nothing more, drain, exit
         for (int k = 0; !stopped; ++k) {
@@ -283,7 +284,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
             if (!is_v) {
                 int q_ok = 1;
                 if (lane == 0) {
-                    if (active > 0) q_ok = mbar_wait_space(q_empty, (active - 1) & 1) ? 1 : 0;
+                    if (active > 0) q_ok = mbar_wait_space(q_empty, (active - 1) & 1, space_limit) ? 1 : 0;
                     if (q_ok) {
                         mbar_arrive_expect_tx(q_full, (uint32_t)L::Q_BYTES);
 #pragma unroll
@@ -329,7 +330,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                     }
                 }
                 const uint32_t bytes = (uint32_t)__popc(__ballot_sync(full_mask, valid)) * L::KB * R * 128;
-                if (gt >= 2 && !__all_sync(full_mask, mbar_wait_space(&empty[slot], ((gt >> 1) - 1) & 1))) {
+                if (gt >= 2 && !__all_sync(full_mask, mbar_wait_space(&empty[slot], ((gt >> 1) - 1) & 1, space_limit))) {
                     stopped = true;  // the MMAs may still read this slot
                     break;
                 }

@@ -14,7 +14,12 @@ attributes:
   (device-side metadata: one host-to-device copy and one kernel)
 * ``BlockManager.copy_on_write`` / ``BlockManager.prepare_write`` (new methods
   on the reference class; ``cache/cow.py``) and ``KVCachePool.copy_blocks``
-  (new; the device copy of the forked pages over every layer).
+  (new; the device copy of the forked pages over every layer);
+* with ``fuse_decode_append`` (default), ``Attention.forward_decode_batch``
+  (model/native_qwen3.py:179-197) on the CUDA data and decode backends: its
+  KV append and paged decode become one launch
+  (``kernels.paged_attention_with_append``); other backends run the
+  reference method unchanged.
 
 Each rebound op keeps the reference's signature and default ``backend``.  A
 call with a CUDA backend ("cuda", and for decode "cuda_baseline" /
@@ -34,7 +39,7 @@ import sys
 from .cache.cow import copy_on_write, prepare_write
 from .engine.batch import PrefillBatch
 from .kernels import data as _data
-from .kernels.paged import CUDA_BACKENDS, paged_attention
+from .kernels.paged import CUDA_BACKENDS, paged_attention, paged_attention_with_append
 from .kernels.prefill import paged_prefill_attention
 
 # op name -> (module of its definition in the reference, our implementation, backends routed to ours)
@@ -80,7 +85,33 @@ def _pool_copy_blocks(self, pairs) -> None:
     _data.copy_blocks(self.key, self.value, pairs)
 
 
-def install(package) -> list[str]:
+def _fused_decode_batch(reference_method):
+    """``Attention.forward_decode_batch`` whose KV append and decode run as one kernel on the CUDA backends.
+
+    The steps before the attention are the reference's own (its projection,
+    q/k norms and the RoPE op its module binds); only the two calls at
+    native_qwen3.py:188-196 are replaced by ``paged_attention_with_append``,
+    which writes the same rows and returns the same attention.
+    """
+    if getattr(reference_method, "__minikv_reference__", None) is not None:
+        return reference_method  # already installed
+
+    @functools.wraps(reference_method)
+    def forward_decode_batch(self, x, cos, sin, cache, block_tables, positions, layer, decode_backend):
+        if self.data_backend != "cuda" or decode_backend not in CUDA_BACKENDS:
+            return reference_method(self, x, cos, sin, cache, block_tables, positions, layer, decode_backend)
+        rope = sys.modules[type(self).__module__].apply_rope_backend
+        q, k, v = self._project_qkv(x)
+        q, k = rope(self.q_norm(q), self.k_norm(k), cos, sin, backend="cuda", validate=False)
+        attention = paged_attention_with_append(q, cache.key[layer], cache.value[layer], block_tables, positions,
+                                                k, v, cache.shape.block_size, validate=False)
+        return self.o_proj(attention.reshape(x.shape[0], -1))
+
+    forward_decode_batch.__minikv_reference__ = reference_method
+    return forward_decode_batch
+
+
+def install(package, *, fuse_decode_append: bool = True) -> list[str]:
     """Patch the reference package object (or its name) in place; idempotent."""
     if isinstance(package, str):
         package = importlib.import_module(package)
@@ -110,6 +141,10 @@ def install(package) -> list[str]:
         allocator.BlockManager.copy_on_write = copy_on_write
         allocator.BlockManager.prepare_write = prepare_write
         patched += [f"{root}.cache.block_manager.BlockManager.{n}" for n in ("copy_on_write", "prepare_write")]
+    model = _module(root, "model.native_qwen3")
+    if fuse_decode_append and model is not None and hasattr(model, "Attention"):
+        model.Attention.forward_decode_batch = _fused_decode_batch(model.Attention.forward_decode_batch)
+        patched.append(f"{root}.model.native_qwen3.Attention.forward_decode_batch")
     pools = _module(root, "cache.kv_cache")
     if pools is not None:
         pools.KVCachePool.copy_blocks = _pool_copy_blocks

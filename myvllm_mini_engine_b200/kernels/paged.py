@@ -50,6 +50,13 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
     launch overlaps its prologue with that kernel (``minikv_paged_decode_chained``).
     """
     check_backend(backend)
+    return _decode(query, key_cache, value_cache, block_tables, context_lens, block_size, validate=validate,
+                   workspace=workspace, chained=chained)
+
+
+def _decode(query, key_cache, value_cache, block_tables, context_lens, block_size, *, validate, workspace, chained,
+            append=None):
+    """Checks and launch of the decode; ``append = (key, value, token_offsets)`` selects the fused append."""
     _require(query.is_cuda, "query must be CUDA")
     for t in (key_cache, value_cache, block_tables, context_lens):
         _require(t.device == query.device, "all inputs must be on the same CUDA device")
@@ -95,11 +102,19 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
         elif workspace.numel() < need:
             raise RuntimeError("decode workspace too small")
         out = torch.empty_like(query)
-        entry = lib.minikv_paged_decode_chained if chained else lib.minikv_paged_decode
-        status = entry(
-            query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
-            context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
-            batch, heads, kv_heads, dim, num_blocks, block_size, width, code, stream)
+        if append is not None:
+            key, value, offsets = append
+            status = lib.minikv_paged_decode_append(
+                query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
+                offsets.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(), workspace.data_ptr(),
+                workspace.numel(), batch, heads, kv_heads, dim, num_blocks, block_size, width, code, int(chained),
+                stream)
+        else:
+            entry = lib.minikv_paged_decode_chained if chained else lib.minikv_paged_decode
+            status = entry(
+                query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
+                context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
+                batch, heads, kv_heads, dim, num_blocks, block_size, width, code, stream)
     _lib.check(status, "paged_attention")
     return out
 
@@ -137,3 +152,37 @@ def workspace_bytes(query, key_cache, block_tables):
     if need < 0:
         _lib.check(_lib.EINVAL, "workspace_bytes")
     return need
+
+
+def paged_attention_with_append(query, key_cache, value_cache, block_tables, token_offsets, key, value, block_size,
+                                *, backend="cuda", validate=True, workspace=None, chained=False):
+    """KV append and decode attention in one launch (``minikv_paged_decode_append``).
+
+    The same results as ``write_kv_cache_batch(key_cache, value_cache,
+    block_tables, token_offsets, key, value, block_size)`` followed by
+    ``paged_attention(query, key_cache, value_cache, block_tables,
+    token_offsets + 1, block_size)`` -- the two calls of the reference's
+    ``Attention.forward_decode_batch`` (``mini_engine/model/native_qwen3.py:188-196``)
+    -- with one kernel: the CTA that attends a request's last tile writes the new
+    K/V row into its pool slot (bit-exact) and reads it from ``key``/``value``.
+    ``key``/``value`` are ``[B, Hkv, D]`` in the cache dtype.  ``validate=True``
+    runs the checks of both calls.  Returns ``[B, Hq, D]``.  ``chained=True``:
+    ``token_offsets`` and ``block_tables`` predate the previous kernel on the
+    stream (``key``/``value`` may come from it), as for ``paged_attention``.
+    """
+    check_backend(backend)
+    _require(query.is_cuda, "query must be CUDA")
+    _require(key.shape == value.shape and key.dim() == 3 and key.shape[0] == query.shape[0],
+             "batch key/value must be [batch, kv_heads, head_dim]")
+    for t in (key, value, token_offsets):
+        _require(t.device == query.device and t.is_contiguous(), "batch KV write inputs must be contiguous CUDA tensors")
+    _require(key.dtype == key_cache.dtype and value.dtype == key_cache.dtype, "batch KV dtype mismatch")
+    _require(key_cache.dim() == 4 and key.shape[1:] == key_cache.shape[2:], "batch K/V shape mismatch")
+    _require(token_offsets.dtype == torch.int64 and token_offsets.dim() == 1, "metadata must be int64")
+    if validate:
+        width = block_tables.shape[1] if block_tables.dim() == 2 else 0
+        _require(not bool(((token_offsets < 0) | (token_offsets >= width * block_size)).any()),
+                 "batch KV offset out of range")
+    lengths = token_offsets + 1 if validate else token_offsets
+    return _decode(query, key_cache, value_cache, block_tables, lengths, block_size, validate=validate,
+                   workspace=workspace, chained=chained, append=(key, value, token_offsets))

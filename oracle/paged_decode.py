@@ -29,12 +29,13 @@ def _check(query, key_cache, value_cache, block_size):
         raise ValueError("query heads must be divisible by KV heads")
 
 
-def paged_attention_fp32(query, key_cache, value_cache, block_tables, context_lens, block_size):
+def paged_attention_fp32(query, key_cache, value_cache, block_tables, context_lens, block_size, acc=torch.float32):
     """fp32 result of decode attention over each request's pages.
 
     ``query [B,Hq,D]``, caches ``[num_blocks, block_size, Hkv, D]``,
     ``block_tables [B, W]`` int64, ``context_lens [B]`` int64.  Raises
-    ValueError("invalid context length") like fallback.py:50-52.
+    ValueError("invalid context length") like fallback.py:50-52.  ``acc``
+    (test control only) evaluates the same formula in another precision.
     """
     _check(query, key_cache, value_cache, block_size)
     scale = 1.0 / math.sqrt(query.shape[-1])  # fallback.py:48
@@ -49,9 +50,9 @@ def paged_attention_fp32(query, key_cache, value_cache, block_tables, context_le
         keys = key_cache[ids].reshape(-1, key_cache.shape[2], key_cache.shape[3])[:length]
         values = value_cache[ids].reshape(-1, value_cache.shape[2], value_cache.shape[3])[:length]
         group = query.shape[1] // keys.shape[1]
-        keys = keys.float().repeat_interleave(group, dim=1)
-        values = values.float().repeat_interleave(group, dim=1)
-        scores = torch.einsum("hd,thd->ht", query[batch].float(), keys) * scale
+        keys = keys.to(acc).repeat_interleave(group, dim=1)
+        values = values.to(acc).repeat_interleave(group, dim=1)
+        scores = torch.einsum("hd,thd->ht", query[batch].to(acc), keys) * scale
         probs = torch.softmax(scores, dim=-1)
         outputs.append(torch.einsum("ht,thd->hd", probs, values))
     return torch.stack(outputs)
@@ -61,6 +62,16 @@ def paged_attention(query, key_cache, value_cache, block_tables, context_lens, b
     """Reference-dtype result (fallback.py:63: ``.to(query.dtype)``)."""
     return paged_attention_fp32(query, key_cache, value_cache, block_tables,
                                 context_lens, block_size).to(query.dtype)
+
+
+def paged_attention_fp64(query, key_cache, value_cache, block_tables, context_lens, block_size):
+    """The same formula evaluated in float64, rounded to the query dtype.
+
+    Not a reference path: a control that shows how far two valid evaluation
+    orders of the reference's own formula move a model's outputs.
+    """
+    return paged_attention_fp32(query, key_cache, value_cache, block_tables, context_lens, block_size,
+                                acc=torch.float64).to(query.dtype)
 
 
 def paged_attention_trusted_fp32(query, key_cache, value_cache, block_tables, context_lens, block_size):

@@ -72,12 +72,15 @@ def append_rows(key_cache, value_cache, block_tables, positions, key, value, blo
         value_cache[page, position % block_size] = value[batch]
 
 
-def decode_step(config, weights, input_ids, key_pool, value_pool, block_tables, positions):
+def decode_step(config, weights, input_ids, key_pool, value_pool, block_tables, positions, attention=None):
     """Logits ``[B, vocab]`` of one decode step; appends each request's K/V to the pools.
 
     ``key_pool``/``value_pool`` are ``[layers, num_blocks, block_size, kv_heads,
     head_dim]`` and are modified in place, like the reference's KVCachePool.
+    ``attention`` replaces the decode attention (default: the reference's,
+    ``paged_decode.paged_attention``) -- for test controls only.
     """
+    attention = paged_decode.paged_attention if attention is None else attention
     cfg = config
     hq, hkv, dim = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
     block_size = key_pool.shape[2]
@@ -96,9 +99,8 @@ def decode_step(config, weights, input_ids, key_pool, value_pool, block_tables, 
         k = rms_norm(k, w.k_norm, cfg.rms_norm_eps)
         q, k = apply_rope(q, k, cos.unsqueeze(1), sin.unsqueeze(1))
         append_rows(key_pool[layer], value_pool[layer], block_tables, positions, k, v, block_size)
-        attention = paged_decode.paged_attention(q, key_pool[layer], value_pool[layer], block_tables,
-                                                 lengths, block_size)
-        o = torch.mm(attention.reshape(batch, -1), w.o.t())
+        attended = attention(q, key_pool[layer], value_pool[layer], block_tables, lengths, block_size)
+        o = torch.mm(attended.reshape(batch, -1), w.o.t())
         summed = o + x
         normalized = rms_norm(summed, w.post_norm, cfg.rms_norm_eps)
         gate, up = (part.contiguous() for part in torch.mm(normalized, w.gate_up.t()).chunk(2, dim=-1))

@@ -36,6 +36,7 @@ def test_install_routes_cuda_backends_of_every_reference_entry_point(reference_e
     assert batch.PrefillBatch is PrefillBatch and runtime.PrefillBatch is PrefillBatch
     assert data.write_kv_cache_batch.__minikv_reference__ is original
     assert data.write_kv_cache_batch.__kwdefaults__["backend"] == "torch"  # the reference default is kept
+    assert nq.Attention.forward_decode_batch.__minikv_reference__ is not None  # append + decode fused
     assert len(patched) >= 15
 
 
