@@ -17,7 +17,11 @@
 // when lengths change (the reference derives its partition count from the
 // table width for the same reason, paged_attention.cu:271).
 //
-// CTA layout: 8 consumer warps + 1 producer warp.  The producer first reads
+// CTA layout: 8 consumer warps + 1 producer warp + 1 ticket warp.  The
+// ticket warp takes the merge tickets of the segments that end inside the
+// CTA's range (a request boundary mid-range), so the consumers move on to the
+// next request as soon as their partial is stored; the segment that ends the
+// CTA's range is ticketed (and merged) by the consumers.  The producer first reads
 // the physical rows of the next 32 tiles into shared memory with independent
 // loads (one page-table lookup per page, all in flight together), then stages
 // every tile's K and V rows -- all kv heads of the CTA's head group -- into
@@ -40,7 +44,9 @@
 namespace minikv {
 
 constexpr int kConsumerWarps = 8;
-constexpr int kDecodeThreads = (kConsumerWarps + 1) * 32;
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kTicketWarp = kConsumerWarps + 1;
+constexpr int kDecodeThreads = (kConsumerWarps + 2) * 32;
 constexpr int kCoreHeads = 2;       // query heads per CUDA-core consumer warp
 constexpr int kMmaHeads = 8;        // query heads per tensor-core consumer warp (MMA N)
 constexpr int kTokensPerGroup = 4;  // CUDA-core: tokens per lane group per sub-chunk
@@ -153,7 +159,7 @@ __device__ __forceinline__ int request_of_tile(const int* prefix, int B, int t) 
 template <typename T, int D>
 __device__ void merge_heads(const DecodeParams& p, int b, int qh0, bool two, int c0, int c1, int G, int total,
                             int lane) {
-    constexpr int kBatch = 4;
+    constexpr int kBatch = (sizeof(T) == 2 && D <= 128) ? 6 : 4;  // one load round for the typical record count
     constexpr int kDims = (D + 31) / 32;
     const int nh = two ? 2 : 1;
     const int n = c1 - c0 + 1;
@@ -388,6 +394,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int warp_sums[kDecodeThreads / 32];
     __shared__ int last_ticket;
+    __shared__ __align__(8) uint64_t seg_bar;  // consumers -> ticket warp: a mid-range partial is stored
 
     const int TT = p.tile_tokens, NS = p.stages, stride = p.row_stride;
     const int B = p.batch;
@@ -416,6 +423,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kConsumerWarps);
         }
+        mbar_init(&seg_bar, kConsumerWarps);
         mbar_init_fence();
     }
     __syncthreads();
@@ -434,28 +442,72 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
     const int tile_lo = (int)((int64_t)c * total / G), tile_hi = (int)((int64_t)(c + 1) * total / G);
     if (tile_lo >= tile_hi) return;
 
-    // Head group of this CTA and the query heads of this consumer warp.
+    // Head group of this CTA, and the kv head / query-head chunk of consumer warp w.
     const int cph = p.chunks_per_head;
-    int h0, nh, kvh, chunk;
-    bool active;
-    if (cph >= kConsumerWarps) {
-        h0 = blockIdx.y / p.chunk_groups;
-        nh = 1;
-        kvh = h0;
-        chunk = (blockIdx.y % p.chunk_groups) * kConsumerWarps + warp;
-        active = chunk < cph;
-    } else {
-        h0 = blockIdx.y * p.heads_per_cta;
-        nh = min(p.heads_per_cta, p.kv_heads - h0);
-        kvh = h0 + warp / cph;
-        chunk = warp % cph;
-        active = warp < nh * cph;
-    }
+    const int h0 = cph >= kConsumerWarps ? blockIdx.y / p.chunk_groups : blockIdx.y * p.heads_per_cta;
+    const int nh = cph >= kConsumerWarps ? 1 : min(p.heads_per_cta, p.kv_heads - h0);
+    auto warp_heads = [&](int w, int& kvh_w, int& chunk_w) -> bool {
+        if (cph >= kConsumerWarps) {
+            kvh_w = h0;
+            chunk_w = (blockIdx.y % p.chunk_groups) * kConsumerWarps + w;
+            return chunk_w < cph;
+        }
+        kvh_w = h0 + w / cph;
+        chunk_w = w % cph;
+        return w < nh * cph;
+    };
+    int kvh, chunk;
+    const bool active = warp_heads(warp, kvh, chunk);
     constexpr int esize = Consumer::kKvBytes;  // bytes per cached element
     const int copy_row = nh * D * esize;              // bytes per token and K|V
     const int cache_row = p.kv_heads * D * esize;     // global row stride
 
-    if (warp == kConsumerWarps) {
+    if (warp == kTicketWarp) {
+        // ------------------------------------------------------------ ticket warp
+        // Walks the CTA's segments like the consumers; for each one that ends inside
+        // the range and is not a whole request, it waits until the consumers have
+        // stored the partial (seg_bar, a CTA-scope release/acquire) and takes the
+        // request's ticket (acquire-release at GPU scope, cumulative over those
+        // stores).  The holder of the last ticket merges every query head of the
+        // CTA's head group, while the consumers already stream the next request.
+        griddep_wait();  // tickets and outputs may still be in use by the previous kernel
+        int k = 0;
+        int b = request_of_tile(prefix, B, tile_lo);
+        for (int t = tile_lo; t < tile_hi;) {
+            while (b + 1 < B && prefix[b + 1] <= t) ++b;
+            const int seg_hi = min(tile_hi, prefix[b + 1]);
+            const int c0 = cta_of_tile(prefix[b], G, total), c1 = cta_of_tile(prefix[b + 1] - 1, G, total);
+            if (c0 != c1 && seg_hi < tile_hi) {
+                mbar_wait(&seg_bar, k & 1);  // on a timeout the ticket is still taken: the counter stays consistent
+                ++k;
+                int owners = 0;
+                for (int cc = c0; cc <= c1; ++cc) owners += cta_owns_tiles(cc, G, total) ? 1 : 0;
+                unsigned int ticket = 0;
+                if (lane == 0)
+                    asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
+                                 : "=r"(ticket)
+                                 : "l"(p.tickets + (int64_t)b * gridDim.y + blockIdx.y),
+                                   "r"((unsigned int)(owners - 1))
+                                 : "memory");
+                ticket = __shfl_sync(0xffffffffu, ticket, 0);
+                __syncwarp();  // the other lanes' partial loads come after lane 0's acquire
+                if (ticket == (unsigned int)(owners - 1)) {
+                    for (int w = 0; w < kConsumerWarps; ++w) {
+                        int kvh_w, chunk_w;
+                        if (!warp_heads(w, kvh_w, chunk_w)) continue;
+                        const int ih = min(p.heads_per_item, p.group - chunk_w * p.heads_per_item);
+                        const int qh_w = kvh_w * p.group + chunk_w * p.heads_per_item;
+                        for (int h = 0; h < ih; h += 2)
+                            merge_heads<T, D>(p, b, qh_w + h, h + 1 < ih, c0, c1, G, total, lane);
+                    }
+                }
+            }
+            t = seg_hi;
+        }
+        return;
+    }
+
+    if (warp == kProducerWarp) {
         // ------------------------------------------------------------ producer
         const uint64_t policy = policy_evict_first();
         const uint64_t space_limit = space_wait_limit();
@@ -634,7 +686,11 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
         const int c0 = cta_of_tile(prefix[b], G, total), c1 = cta_of_tile(prefix[b + 1] - 1, G, total);
         const bool final_row = c0 == c1;
         if (active) cons.finish(p, b, qh0, item_heads, final_row, (int64_t)b + c);
-        if (!final_row) {
+        if (!final_row && seg_hi < tile_hi) {
+            // a request boundary inside the range: the ticket warp takes the ticket
+            __syncwarp();  // the warp's partial stores before lane 0's release
+            if (lane == 0) mbar_arrive(&seg_bar);
+        } else if (!final_row) {
             // Ticket: the CTA that completes request b last merges its records.
             // The consumer barrier orders every thread's partial stores before
             // thread 0's ticket, an acquire-release atomic at GPU scope: it
