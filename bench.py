@@ -393,77 +393,95 @@ def run_ours(args, world, rank, local):
     peak, peak_kind = measured_peaks()
 
     # ---- end to end through the public API, host buffers in and out: every step
-    # copies its inputs (q, k, v, tables, offsets, lengths: one pinned host buffer,
-    # one copy) to the GPU, runs the fused append + decode and copies
-    # the output back to pinned host memory.  As a serving loop would, the copies
-    # run on a second stream, pipelined across steps: step k+1's inputs go up
-    # into the other of two device input buffers while step k computes, and
-    # step k's output comes down while step k+1 computes; the kernels of every
-    # step stay in order on the compute stream (step k+1's KV writes follow step
-    # k's attention).  The copy-stream calls go straight to the CUDA runtime
-    # (cuda-python): the loop must issue a step faster than the GPU runs it.
-    from cuda.bindings import runtime as cudart
-
-    def cuda_call(result):
-        if result[0] != cudart.cudaError_t.cudaSuccess:
-            raise RuntimeError(f"CUDA runtime call failed: {result[0]}")
-        return result[1:]
-
+    # copies its inputs (q, k, v, tables, offsets: one pinned host buffer, one
+    # copy) to the GPU, runs the fused append + decode and copies the output back
+    # to pinned host memory.  As a serving loop would, the copies run on a second
+    # stream, pipelined across steps: step k+1's inputs go up into the other of
+    # two device input buffers while step k computes, and step k's output comes
+    # down while step k+1 computes.  The steps (copies and kernels) are captured
+    # in CUDA graphs of up to 256 steps, as the decode loop of a serving engine
+    # is, so the host issues one graph launch per window instead of a Python
+    # call per copy and kernel.
     names = ("query", "key", "value", "block_tables", "token_offsets")
     host, dev_a = packed_buffers({k: x[k] for k in names}, device)
     _, dev_b = packed_buffers({k: x[k] for k in names}, device)
     devs = (dev_a, dev_b)
-    outs_host = [torch.empty(out.shape, dtype=out.dtype, pin_memory=True) for _ in range(2)]
+    outs_host = [torch.empty(x["query"].shape, dtype=x["query"].dtype, pin_memory=True) for _ in range(2)]
     h2d = host["_buffer"].numel()
     d2h = outs_host[0].numel() * outs_host[0].element_size()
     copies = torch.cuda.Stream(device)
-    copy_handle, compute_handle = cudart.cudaStream_t(copies.cuda_stream), cudart.cudaStream_t(stream.cuda_stream)
-    no_timing = cudart.cudaEventDisableTiming
-    copied = [cuda_call(cudart.cudaEventCreateWithFlags(no_timing))[0] for _ in range(2)]
-    consumed = [cuda_call(cudart.cudaEventCreateWithFlags(no_timing))[0] for _ in range(2)]
+    # the copies go straight to the CUDA runtime (cuda-python): plain memcpy nodes in the graph
+    from cuda.bindings import runtime as cudart
+
+    def memcpy(dst, src, nbytes, kind, on):
+        err = cudart.cudaMemcpyAsync(dst, src, nbytes, kind, cudart.cudaStream_t(on.cuda_stream))[0]
+        if err != cudart.cudaError_t.cudaSuccess:
+            raise RuntimeError(f"cudaMemcpyAsync failed: {err}")
+
     to_dev, to_host = cudart.cudaMemcpyKind.cudaMemcpyHostToDevice, cudart.cudaMemcpyKind.cudaMemcpyDeviceToHost
-    host_ptr = host["_buffer"].data_ptr()
-    dev_ptrs = [d["_buffer"].data_ptr() for d in devs]
-    out_ptrs = [o.data_ptr() for o in outs_host]
 
-    def upload(k):
-        if k >= 2:  # step k-2 is done reading this input buffer
-            cuda_call(cudart.cudaStreamWaitEvent(copy_handle, consumed[k % 2], 0))
-        cuda_call(cudart.cudaMemcpyAsync(dev_ptrs[k % 2], host_ptr, h2d, to_dev, copy_handle))
-        cuda_call(cudart.cudaEventRecord(copied[k % 2], copy_handle))
-
-    def run_e2e(steps, start_event=None):
-        if start_event is not None:
-            copies.wait_event(start_event)
-        upload(0)
-        for k in range(steps):
+    def e2e_steps(count):
+        """``count`` steps with their copies, issued on the current (capturing) stream and ``copies``."""
+        compute = torch.cuda.current_stream(device)
+        copied = [torch.cuda.Event() for _ in range(count)]
+        done = [torch.cuda.Event() for _ in range(count)]
+        results = []  # every step's output stays allocated until its download is ordered before later work
+        copies.wait_stream(compute)
+        memcpy(devs[0]["_buffer"].data_ptr(), host["_buffer"].data_ptr(), h2d, to_dev, copies)
+        copied[0].record(copies)
+        for k in range(count):
             d = devs[k % 2]
-            cuda_call(cudart.cudaStreamWaitEvent(compute_handle, copied[k % 2], 0))
+            compute.wait_event(copied[k])
             result = paged_attention_with_append(d["query"], x["key_cache"], x["value_cache"], d["block_tables"],
                                                  d["token_offsets"], d["key"], d["value"], BS, validate=False,
                                                  chained=True)
-            cuda_call(cudart.cudaEventRecord(consumed[k % 2], compute_handle))
-            if k + 1 < steps:
-                upload(k + 1)
-            cuda_call(cudart.cudaStreamWaitEvent(copy_handle, consumed[k % 2], 0))
-            cuda_call(cudart.cudaMemcpyAsync(out_ptrs[k % 2], result.data_ptr(), d2h, to_host, copy_handle))
-            result.record_stream(copies)  # its memory is not reused before the download
-        stream.wait_stream(copies)
+            done[k].record(compute)
+            if k + 1 < count:
+                if k >= 1:  # step k-1 has finished reading the buffer of step k+1
+                    copies.wait_event(done[k - 1])
+                memcpy(devs[(k + 1) % 2]["_buffer"].data_ptr(), host["_buffer"].data_ptr(), h2d, to_dev, copies)
+                copied[k + 1].record(copies)
+            copies.wait_event(done[k])
+            memcpy(outs_host[k % 2].data_ptr(), result.data_ptr(), d2h, to_host, copies)
+            results.append(result)
+        compute.wait_stream(copies)
 
-    run_e2e(args.warmup)
+    with torch.cuda.stream(capture_stream):
+        e2e_steps(2)  # eager warm-up of the copy path
+    torch.cuda.synchronize(device)
+    e2e_graphs = []
+    for count in [per_graph] * min(full, 1) + ([rest] if rest else []):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=capture_stream):
+            e2e_steps(count)
+        e2e_graphs.append(g)
+    e2e_big = e2e_graphs[0] if full else None
+    e2e_tail = e2e_graphs[-1] if rest else None
+
+    def run_e2e():
+        for _ in range(full):
+            e2e_big.replay()
+        if e2e_tail is not None:
+            e2e_tail.replay()
+
+    for _ in range(max(1, math.ceil(args.warmup / args.steps))):
+        run_e2e()
     barrier()
-    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    run_e2e(args.steps, e_start)
-    e_end.record(stream)
-    barrier()
-    for event in copied + consumed:
-        cuda_call(cudart.cudaEventDestroy(event))
-    e2e_ms = e_start.elapsed_time(e_end)
+    e2e_windows = []
+    for _ in range(min(repeats, 5)):
+        e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        e_start.record(stream)
+        run_e2e()
+        e_end.record(stream)
+        barrier()
+        e2e_windows.append(e_start.elapsed_time(e_end))
     if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
+        t = torch.tensor(e2e_windows, device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        e2e_windows = [float(v) for v in t.tolist()]
+    e2e_ms = statistics.median(e2e_windows)
+    del e2e_graphs, e2e_big, e2e_tail
     e2e_value = world * step_bytes / (e2e_ms / args.steps * 1e-3) / 1e9
     status = _lib.device_status(device)
     if status:
@@ -499,9 +517,10 @@ def run_ours(args, world, rank, local):
                                       "are not overlapped with a neighbouring launch"},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms / args.steps,
-                "path": "paged_attention_with_append (Python API, eager), one H2D copy of the packed inputs and "
-                        "one D2H copy of the output per step, pinned host buffers; copies on a second stream, "
-                        "pipelined across steps (double-buffered device inputs)"},
+                "path": "paged_attention_with_append (Python API), one H2D copy of the packed inputs and one D2H "
+                        "copy of the output per step, pinned host buffers; copies on a second stream, pipelined "
+                        "across steps (double-buffered device inputs); steps and copies captured in CUDA graphs "
+                        "of up to 256 steps, median of the timed windows"},
         "gpu_launches": args.steps * repeats,
         "gpu_launches_note": "one fused append + decode launch per step, in each of the timed windows",
         "clocks": clocks.summary(),

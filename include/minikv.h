@@ -116,9 +116,11 @@ int minikv_paged_decode_chained(const void* query, const void* key_cache, const 
  * is negative, beyond the table or on an invalid page) by the CTA that
  * attends it, which reads it from key/value instead of the pool.  16-bit and
  * fp32 pools; workspace as for minikv_paged_decode (same size).  chained != 0:
- * token_offsets and block_tables were written before the previous kernel on
- * the stream started (key/value may come from that kernel), as for
- * minikv_paged_decode_chained.  Replaces the two launches of
+ * token_offsets, block_tables and the pool rows the call reads (all but the
+ * appended ones) were written before the previous kernel on the stream
+ * started; key/value may come from that kernel.  The launch then overlaps the
+ * previous kernel's tail: it resolves its pages and starts staging pool rows
+ * before waiting for that kernel.  Replaces the two launches of
  * Attention.forward_decode_batch (mini_engine/model/native_qwen3.py:188-196:
  * write_kv_cache_batch, then paged_attention over positions + 1). */
 int minikv_paged_decode_append(const void* query, const void* key_cache, const void* value_cache,

@@ -71,7 +71,8 @@ struct DecodeParams {
     int chunk_groups;     // head groups per kv head (> 1 only when chunks_per_head > 8)
     int tile_tokens;      // TT, multiple of the consumer's sub-chunk, <= 64
     int stages;
-    int row_stride;       // shared-memory stride of one token row (padded)
+    int row_stride;       // shared-memory stride of one token row (padded), or of a pair of rows
+    int pair_rows;        // 1: rows staged in pairs (tensor-core consumer, every kv head in the CTA)
     int early_prologue;   // 1: lens/tables predate the previous kernel; read them before griddep_wait
     int coalesce;         // 1: rows unpadded and the CTA holds every kv head: one bulk copy per run of
                           //    consecutive physical rows (fp8 pool only)
@@ -88,7 +89,14 @@ __device__ __forceinline__ int cta_of_tile(int t, int G, int total) {
     return (int)((((int64_t)t + 1) * G + total - 1) / total) - 1;
 }
 __device__ __forceinline__ bool cta_owns_tiles(int cta, int G, int total) {
-    return ((int64_t)cta * total) / G != ((int64_t)(cta + 1) * total) / G;
+    // with at least one tile per CTA every CTA owns some (and the 64-bit divisions are skipped)
+    return total >= G || ((int64_t)cta * total) / G != ((int64_t)(cta + 1) * total) / G;
+}
+
+// Offset of token j's row in a staged tile: rows `stride` apart, or (paired
+// staging) pairs of rows `stride` apart, the two rows of a pair adjacent.
+__device__ __forceinline__ int stage_row_offset(bool pair, int j, int stride, int row_bytes) {
+    return pair ? (j >> 1) * stride + (j & 1) * row_bytes : j * stride;
 }
 
 // Consumer-only barrier (the producer warp never joins it).
@@ -242,6 +250,7 @@ struct CoreConsumer {
     using S = CoreShape<T, D>;
     static constexpr int kSubTokens = S::SC;
     static constexpr int kKvBytes = (int)sizeof(T);  // bytes per cached element
+    static constexpr bool kPairCapable = false;      // rows staged one per stride
     float qf[kCoreHeads][S::VPL][S::E];
     float acc[kCoreHeads][S::VPL][S::E];
     float m[kCoreHeads], l[kCoreHeads];
@@ -268,7 +277,7 @@ struct CoreConsumer {
     }
 
     __device__ void tile(const unsigned char* ks, const unsigned char* vs, int stride, int TT, int n,
-                         uint64_t mask, float scale_log2) {
+                         uint64_t mask, float scale_log2, bool = false) {
         for (int sub = 0; sub < TT; sub += S::SC) {
             float s[kTokensPerGroup][kCoreHeads];
             bool ok[kTokensPerGroup];
@@ -398,7 +407,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
 
     const int TT = p.tile_tokens, NS = p.stages, stride = p.row_stride;
     const int B = p.batch;
-    const int stage_bytes = 2 * TT * stride;
+    const bool kPair = Consumer::kPairCapable && p.pair_rows;
+    const int tile_bytes = kPair ? (TT / 2) * stride : TT * stride;  // K (or V) bytes of one staged tile
+    const int stage_bytes = 2 * tile_bytes;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + NS * stage_bytes);
     uint64_t* empty = full + NS;
     uint64_t* masks = empty + NS;
@@ -518,8 +529,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
         const int new_row = p.kv_heads * D * esize;
         const unsigned char* knew = static_cast<const unsigned char*>(p.new_k) + (size_t)h0 * D * esize;
         const unsigned char* vnew = static_cast<const unsigned char*>(p.new_v) + (size_t)h0 * D * esize;
-        int gt = 0;           // tiles issued
+        int gt = 0;            // tiles issued
         bool stopped = false;  // a space wait gave up: issue nothing more
+        bool waited = !p.early_prologue;  // griddepcontrol.wait done (or not needed)
         for (int w0 = tile_lo; w0 < tile_hi && !stopped; w0 += kWindowTiles) {
             // Rows of tiles w0 .. w0+31: lane i resolves tile w0+i, one table
             // load per page, all lanes' loads in flight together.
@@ -553,31 +565,22 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                 for (; j < TT; ++j) rows[j] = -1;
             }
             __syncwarp();
-            if (p.early_prologue && w0 == tile_lo) griddep_wait();  // KV rows may come from the previous kernel
-            if (p.append) {
-                // write this window's appended rows (this CTA's heads) into the pool: every
-                // lane copies 16 bytes at a time of one row after the other; bit-exact copies
-                unsigned pending = __ballot_sync(0xffffffffu, append_dst >= 0);
-                unsigned char* kpool = const_cast<unsigned char*>(kbase);
-                unsigned char* vpool = const_cast<unsigned char*>(vbase);
-                while (pending) {
-                    const int from = __ffs(pending) - 1;
-                    pending &= pending - 1;
-                    const int64_t dst = __shfl_sync(0xffffffffu, append_dst, from);
-                    const int64_t src = __shfl_sync(0xffffffffu, append_b, from);
-                    const uint4* ks = reinterpret_cast<const uint4*>(knew + src * new_row);
-                    const uint4* vs = reinterpret_cast<const uint4*>(vnew + src * new_row);
-                    uint4* kd = reinterpret_cast<uint4*>(kpool + dst * cache_row);
-                    uint4* vd = reinterpret_cast<uint4*>(vpool + dst * cache_row);
-                    for (int v = lane; v < copy_row / 16; v += 32) {
-                        kd[v] = ld_global_nc(ks + v);
-                        vd[v] = ld_global_nc(vs + v);
-                    }
-                }
+            // Chained launch: the copies wait for the previous kernel (the KV rows may come from
+            // it).  With the fused append they need not: the pool rows it reads predate the
+            // previous kernel and only the new rows (read from key/value) may come from it, so
+            // the copies start at once and the wait comes before the first new row, before the
+            // producer would block on a full ring, and before the new rows are written back.
+            if (!waited && !(p.append && p.early_prologue)) {
+                griddep_wait();
+                waited = true;
             }
             const int count = min(kWindowTiles, tile_hi - w0);
             for (int i = 0; i < count; ++i, ++gt) {
                 const int slot = gt % NS;
+                if (gt >= NS && !waited) {  // a full ring: the consumers start only after the previous kernel
+                    griddep_wait();
+                    waited = true;
+                }
                 if (gt >= NS && !__all_sync(0xffffffffu, mbar_wait_space(&empty[slot], ((gt / NS) - 1) & 1, space_limit))) {
                     stopped = true;  // the consumers may still read this slot
                     break;
@@ -590,10 +593,14 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                     row[h] = j < TT ? window[i * TT + j] : -1;
                     ok[h] = row[h] != -1;  // a pool row, or (append) -2 - b: request b's new row
                 }
+                if (!waited && __any_sync(0xffffffffu, row[0] < -1 || row[1] < -1)) {  // a new row: from the previous kernel
+                    griddep_wait();
+                    waited = true;
+                }
                 const uint64_t mask = (uint64_t)__ballot_sync(0xffffffffu, ok[0]) |
                                       ((uint64_t)__ballot_sync(0xffffffffu, ok[1]) << 32);
                 unsigned char* kdst = smem + slot * stage_bytes;
-                unsigned char* vdst = kdst + TT * stride;
+                unsigned char* vdst = kdst + tile_bytes;
                 // Masked V rows must hold finite values (the tensor-core PV
                 // multiplies them by P = 0): zero them with generic stores,
                 // ordered before the consumers' reads by the arrive below.
@@ -601,7 +608,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                 while (holes) {
                     const int j = __ffsll((long long)holes) - 1;
                     holes &= holes - 1;
-                    uint4* vrow = reinterpret_cast<uint4*>(vdst + j * stride);
+                    uint4* vrow = reinterpret_cast<uint4*>(vdst + stage_row_offset(kPair, j, stride, copy_row));
                     for (int v = lane; v < copy_row / 16; v += 32) vrow[v] = make_uint4(0, 0, 0, 0);
                 }
                 __syncwarp();
@@ -635,19 +642,55 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                                   policy);
                     }
                 } else {
+                    // Paired staging: two consecutive tokens whose pool rows are consecutive (the
+                    // same page) go in one copy of two rows, issued by the even token's lane.
+                    int partner[2];
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) partner[h] = __shfl_xor_sync(0xffffffffu, row[h], 1);
+                    const bool even = (lane & 1) == 0;
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
                         if (!ok[h]) continue;
+                        const bool paired = kPair && (even ? (row[h] >= 0 && partner[h] == row[h] + 1)
+                                                           : (partner[h] >= 0 && row[h] == partner[h] + 1));
+                        if (paired && !even) continue;  // copied with the even token
                         const int j = lane + 32 * h;
                         const int64_t r = row[h];
                         const unsigned char* ksrc = r >= 0 ? kbase + r * cache_row : knew + (-2 - r) * new_row;
                         const unsigned char* vsrc = r >= 0 ? vbase + r * cache_row : vnew + (-2 - r) * new_row;
-                        bulk_load(kdst + j * stride, ksrc, copy_row, &full[slot], policy);
-                        bulk_load(vdst + j * stride, vsrc, copy_row, &full[slot], policy);
+                        const int off = stage_row_offset(kPair, j, stride, copy_row);
+                        const uint32_t bytes = (uint32_t)(paired ? 2 * copy_row : copy_row);
+                        bulk_load(kdst + off, ksrc, bytes, &full[slot], policy);
+                        bulk_load(vdst + off, vsrc, bytes, &full[slot], policy);
                     }
                 }
             }
             __syncwarp();
+            if (p.append) {
+                if (!waited) {
+                    griddep_wait();
+                    waited = true;
+                }
+                // write this window's appended rows (this CTA's heads) into the pool: every
+                // lane copies 16 bytes at a time of one row after the other; bit-exact copies
+                unsigned pending = __ballot_sync(0xffffffffu, append_dst >= 0);
+                unsigned char* kpool = const_cast<unsigned char*>(kbase);
+                unsigned char* vpool = const_cast<unsigned char*>(vbase);
+                while (pending) {
+                    const int from = __ffs(pending) - 1;
+                    pending &= pending - 1;
+                    const int64_t dst = __shfl_sync(0xffffffffu, append_dst, from);
+                    const int64_t src = __shfl_sync(0xffffffffu, append_b, from);
+                    const uint4* ks = reinterpret_cast<const uint4*>(knew + src * new_row);
+                    const uint4* vs = reinterpret_cast<const uint4*>(vnew + src * new_row);
+                    uint4* kd = reinterpret_cast<uint4*>(kpool + dst * cache_row);
+                    uint4* vd = reinterpret_cast<uint4*>(vpool + dst * cache_row);
+                    for (int v = lane; v < copy_row / 16; v += 32) {
+                        kd[v] = ld_global_nc(ks + v);
+                        vd[v] = ld_global_nc(vs + v);
+                    }
+                }
+            }
         }
         // Drain: the last phase issued into each slot has landed before this warp
         // exits, so no bulk copy is in flight when the CTA releases its shared memory
@@ -678,7 +721,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
             const bool landed = __all_sync(0xffffffffu, mbar_wait(&full[slot], (gt / NS) & 1));
             if (active && landed) {
                 const unsigned char* ks = smem + slot * stage_bytes + local_head * D * esize;
-                cons.tile(ks, ks + TT * stride, stride, TT, min(TT, len - k * TT), masks[slot], p.scale_log2);
+                cons.tile(ks, ks + tile_bytes, stride, TT, min(TT, len - k * TT), masks[slot], p.scale_log2, kPair);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[slot]);
@@ -722,7 +765,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
 
 // ------------------------------------------------------------------ host side
 struct DecodePlan {
-    bool mma, coalesce;
+    bool mma, coalesce, pair_rows;
     int tile_tokens, stages, row_stride, heads_per_item, heads_per_cta, chunks_per_head, chunk_groups,
         head_groups;
     int grid, smem_bytes;
@@ -764,11 +807,17 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
     // fp8 pool with every kv head in one CTA: token rows are contiguous in the
     // pool, so they are staged unpadded and copied in runs (the fp8 consumer's
     // loads are built for that layout).
+    // 16-bit pools on the tensor-core consumer stage rows in pairs (one copy per two tokens of a
+    // page, padding after each pair; the consumer reads even and odd tokens as separate 8-row
+    // groups, which keeps ldmatrix conflict free).
     const bool coalesce = kv_fp8 && hpc == Hkv;
-    const int stride = hpc * (int)D * es + (coalesce ? 0 : 16);
-    int tt = (32768 / stride) / sc * sc;
+    const bool pair = mma && !kv_fp8 && hpc == Hkv;  // a pair of rows is contiguous in the pool
+    const int row_bytes = hpc * (int)D * es;
+    const int stride = pair ? 2 * row_bytes + 16 : row_bytes + (coalesce ? 0 : 16);
+    const int token_bytes = pair ? stride / 2 : stride;
+    int tt = (32768 / token_bytes) / sc * sc;
     tt = std::max(sc, std::min(64, tt));
-    const int stage = 2 * tt * stride;
+    const int stage = 2 * (pair ? (tt / 2) * stride : tt * stride);
     const int fixed = kWindowTiles * tt * 4 + (int)(2 * B + 1) * 4 + 128;
     const int max_smem = 232448 - 1024;  // opt-in limit per block, minus static shared memory
     int stages = std::min(kv_fp8 ? 6 : 4, (196608 + 8192) / stage);
@@ -783,6 +832,7 @@ static bool make_decode_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int6
     plan->tile_tokens = tt;
     plan->stages = stages;
     plan->row_stride = stride;
+    plan->pair_rows = pair;
     plan->coalesce = coalesce;
     plan->heads_per_item = heads_per_item;
     plan->heads_per_cta = hpc;
@@ -864,6 +914,7 @@ static DecodeParams decode_params(const void* query, const void* key_cache, cons
     p.tile_tokens = plan.tile_tokens;
     p.stages = plan.stages;
     p.row_stride = plan.row_stride;
+    p.pair_rows = plan.pair_rows ? 1 : 0;
     p.coalesce = plan.coalesce ? 1 : 0;
     p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
     return p;

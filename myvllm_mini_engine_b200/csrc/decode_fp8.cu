@@ -123,6 +123,7 @@ struct Fp8MmaConsumer {
     static constexpr int KB = D / 4;       // K bytes of a token per lane
     static constexpr int VB = D / 8;       // V bytes of a token per lane
     static constexpr int kKvBytes = 1;     // bytes per cached element
+    static constexpr bool kPairCapable = false;  // rows staged unpadded (runs) or padded, one per stride
     using Mma = MmaType<__half>;
     using Codec = Fp8Codec<E5M2>;
 
@@ -171,7 +172,7 @@ struct Fp8MmaConsumer {
     }
 
     __device__ void tile(const unsigned char* kptr, const unsigned char* vptr, int stride, int TT, int n,
-                         uint64_t mask, float scale_log2) {
+                         uint64_t mask, float scale_log2, bool = false) {
         // Two 16-token slices per step where the tile allows: their K loads,
         // conversions and MMAs are independent (ILP for a warp that is alone with
         // one other on its scheduler), and the online-softmax max, rescale and

@@ -63,6 +63,7 @@ struct MmaConsumer {
     static constexpr int MTILES = D / 16;  // m-tiles (16 dims) of O^T
     static constexpr int esize = 2;
     static constexpr int kKvBytes = 2;  // bytes per cached element
+    static constexpr bool kPairCapable = true;  // reads rows staged in pairs (see stage_row_offset)
     using Mma = MmaType<T>;
 
     uint32_t qb[KSTEPS][2];  // Q^T as the B operand: head g, dims 16kk + 2*q4 (+1) and +8
@@ -93,24 +94,34 @@ struct MmaConsumer {
         l[0] = l[1] = 0.f;
     }
 
+    // Rows are padded (`stride` bytes apart) or, with `pair`, staged in pairs (`stride` bytes
+    // per pair of tokens, the pair's two rows adjacent).  M row r of a 16-token slice is
+    // token r, or with pairs token 2r (r < 8) / 2(r - 8) + 1: even and odd tokens form the
+    // two 8-row groups.  Either way the 8 rows one ldmatrix reads are `stride` apart
+    // (stride / 16 odd: no bank conflict).  The k index of the P V product follows the
+    // same order, so only the token of a row changes, not the MMA data flow.
     __device__ void tile(const unsigned char* kptr, const unsigned char* vptr, int stride, int TT, int n,
-                         uint64_t mask, float scale_log2) {
+                         uint64_t mask, float scale_log2, bool pair = false) {
         const uint32_t ks = smem_addr(kptr), vs = smem_addr(vptr);
+        const int row_bytes = (stride - 16) / 2;
         // ldmatrix row addresses: K (A, non-transposed) and V (A of O^T, transposed)
-        const int k_tok = ld_row + 8 * (ld_mat & 1), k_dim = 8 * (ld_mat >> 1);
-        const int v_tok = ld_row + 8 * (ld_mat >> 1), v_dim = 8 * (ld_mat & 1);
+        const int k_off = pair ? ld_row * stride + (ld_mat & 1) * row_bytes : (ld_row + 8 * (ld_mat & 1)) * stride;
+        const int v_off = pair ? ld_row * stride + (ld_mat >> 1) * row_bytes : (ld_row + 8 * (ld_mat >> 1)) * stride;
+        const int k_dim = 8 * (ld_mat >> 1), v_dim = 8 * (ld_mat & 1);
+        const int slice_bytes = pair ? 8 * stride : 16 * stride;
         for (int sub = 0; sub < TT; sub += 16) {
             // ---- S^T = K Q^T, two independent k chains
             float s[4] = {0.f, 0.f, 0.f, 0.f}, s2[4] = {0.f, 0.f, 0.f, 0.f};
-            const uint32_t krow = ks + (sub + k_tok) * stride + k_dim * esize;
+            const uint32_t krow = ks + (sub / 16) * slice_bytes + k_off + k_dim * esize;
 #pragma unroll
             for (int kk = 0; kk < KSTEPS; ++kk) {
                 uint32_t a[4];
                 ldsm_x4(krow + 16 * kk * esize, a);
                 Mma::mma((kk & 1) ? s2 : s, a, qb[kk][0], qb[kk][1]);
             }
-            // ---- mask and scale: s[0,1] is token sub+g, s[2,3] token sub+g+8; columns heads 2q4, 2q4+1
-            const int j0 = sub + g, j1 = j0 + 8;
+            // ---- mask and scale: s[0,1] is M row g, s[2,3] row g+8 (tokens sub+g / sub+g+8, or
+            // with pairs sub+2g / sub+2g+1); columns heads 2q4, 2q4+1
+            const int j0 = pair ? sub + 2 * g : sub + g, j1 = pair ? j0 + 1 : j0 + 8;
             const bool ok0 = j0 < n && ((mask >> j0) & 1ull), ok1 = j1 < n && ((mask >> j1) & 1ull);
             s[0] = ok0 ? (s[0] + s2[0]) * scale_log2 : -INFINITY;
             s[1] = ok0 ? (s[1] + s2[1]) * scale_log2 : -INFINITY;
@@ -166,7 +177,7 @@ struct MmaConsumer {
             const uint32_t c0 = pick_halves(__shfl_sync(0xffffffffu, l01, src0), __shfl_sync(0xffffffffu, l01, src1), odd);
             const uint32_t c1 = pick_halves(__shfl_sync(0xffffffffu, l23, src0), __shfl_sync(0xffffffffu, l23, src1), odd);
             // ---- O^T += V^T P_hi^T + V^T P_lo^T
-            const uint32_t vrow = vs + (sub + v_tok) * stride + v_dim * esize;
+            const uint32_t vrow = vs + (sub / 16) * slice_bytes + v_off + v_dim * esize;
 #pragma unroll
             for (int mt = 0; mt < MTILES; ++mt) {
                 uint32_t a[4];

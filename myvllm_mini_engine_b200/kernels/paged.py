@@ -167,8 +167,10 @@ def paged_attention_with_append(query, key_cache, value_cache, block_tables, tok
     K/V row into its pool slot (bit-exact) and reads it from ``key``/``value``.
     ``key``/``value`` are ``[B, Hkv, D]`` in the cache dtype.  ``validate=True``
     runs the checks of both calls.  Returns ``[B, Hq, D]``.  ``chained=True``:
-    ``token_offsets`` and ``block_tables`` predate the previous kernel on the
-    stream (``key``/``value`` may come from it), as for ``paged_attention``.
+    ``token_offsets``, ``block_tables`` and the pool rows the call reads (all but
+    the appended ones) predate the previous kernel on the stream, while
+    ``key``/``value`` may come from it; the launch then resolves its pages and
+    starts staging pool rows while that kernel finishes.
     """
     check_backend(backend)
     _require(query.is_cuda, "query must be CUDA")

@@ -30,10 +30,14 @@ def short_space_waits(cuda_device):
     _lib.device_status()  # clear
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-def test_decode_slot_wait_timeout_sets_status_and_exits_cleanly(short_space_waits, dtype):
+@pytest.mark.parametrize("dtype,dim", [(torch.float32, 128)])
+def test_decode_slot_wait_timeout_sets_status_and_exits_cleanly(short_space_waits, dtype, dim):
+    # fp32: the CUDA-core consumers are slower than the copies, so the producer waits for a free
+    # slot on every tile and the shortened wait runs out.  (With fp16/bf16 the tensor-core
+    # consumers free each slot before the producer has issued the next tile, so those waits
+    # never block; the producer and the timeout path are the same code for every dtype.)
     gen = torch.Generator(device="cuda").manual_seed(71)
-    batch, context, bs, hq, hkv, dim = 4, 16384, 16, 16, 8, 128
+    batch, context, bs, hq, hkv = 4, 16384, 16, 16, 8
     pages = context // bs
     kc = torch.randn(batch * pages, bs, hkv, dim, device="cuda", generator=gen).to(dtype)
     vc = torch.randn(batch * pages, bs, hkv, dim, device="cuda", generator=gen).to(dtype)
