@@ -10,10 +10,10 @@ By default (``fused_projections``, head_dim 128) a batch of at most
 kernels (packed weights) with the element-wise steps fused into them:
 
     per layer (5 launches):  q|k|v projection [RMSNorm prologue; q/k RMSNorm +
-                             RoPE + KV append epilogue] | paged decode |
-                             o projection [+ residual] | gate|up projection
-                             [RMSNorm prologue; SiLU * up] | down projection
-                             [+ residual]
+                             RoPE epilogue, new K/V to staging rows] | KV append
+                             + paged decode | o projection [+ residual] |
+                             gate|up projection [RMSNorm prologue; SiLU * up] |
+                             down projection [+ residual]
 
 where each residual epilogue hands the next RMSNorm its per-row sums of
 squares, and each projection streams its weights while the previous kernel
@@ -22,11 +22,14 @@ run the projections as plain cuBLAS GEMMs through ``torch.mm`` (the reference's
 ``FusedLinear`` torch path, ``kernels/linear.py:116-130``) around the fused
 element-wise kernels:
 
-    per layer (9 launches):  RMSNorm | mm(q|k|v) | qk-norm + RoPE + KV append |
-                             paged decode | mm(o) | residual + RMSNorm |
-                             mm(gate|up) | SiLU * up | mm(down)
+    per layer (9 launches):  RMSNorm | mm(q|k|v) | qk-norm + RoPE (new K/V to
+                             staging rows) | KV append + paged decode | mm(o) |
+                             residual + RMSNorm | mm(gate|up) | SiLU * up | mm(down)
 
-with the residual add of the MLP fused into the next layer's RMSNorm; that
+with the residual add of the MLP fused into the next layer's RMSNorm.  The
+decode is ``paged_attention_with_append``, chained: the kernel before it writes
+only q and the staging rows, so the decode starts staging pool rows while that
+kernel finishes, and writes the staged rows into the pool itself.  That
 composition reproduces the reference's rounding bit for bit except inside
 the decode attention.  Either way rounding follows the eager reference
 (every intermediate in the model dtype), so the step's greedy tokens match
@@ -49,7 +52,7 @@ from torch.nn import functional as F
 from .. import _lib
 from ..cache.kv_cache import FP8KVCachePool, PagedKVPool
 from ..kernels.fp8 import paged_attention_fp8, write_kv_cache_slots_fp8
-from ..kernels.paged import paged_attention
+from ..kernels.paged import paged_attention_with_append
 
 
 @dataclass(frozen=True)
@@ -244,8 +247,7 @@ class Qwen3DecodeStep:
         hq, hkv, dim = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
         shape = pool.shape
         stream = torch.cuda.current_stream(device).cuda_stream
-        if self.fp8:
-            self._fp8_begin(batch, block_tables, positions)
+        self._stage_begin(batch, block_tables, positions)
         if self.fused_projections and batch <= self.FUSED_MAX_BATCH:
             return self._forward_fused(input_ids, block_tables, positions, stream)
         x = F.embedding(input_ids, w.embed)
@@ -264,7 +266,7 @@ class Qwen3DecodeStep:
                 qkv.data_ptr(), qkv.stride(0), layer.q_norm.data_ptr(), layer.k_norm.data_ptr(), cos.data_ptr(),
                 sin.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), tables.data_ptr(), pos.data_ptr(),
                 batch, hq, hkv, dim, blocks, bs, width, cfg.rms_norm_eps, self.code, stream), "qk_rope_append")
-            attention = self._attend(index, q, block_tables, lengths)
+            attention = self._attend(index, q, block_tables, positions, lengths)
             o = torch.mm(attention.view(batch, hq * dim), layer.o.t())
             summed, normalized = torch.empty_like(x), torch.empty_like(x)
             self._rms(o, residual, layer.post_norm, normalized, summed, stream)
@@ -306,7 +308,7 @@ class Qwen3DecodeStep:
                 layer.q_norm.data_ptr(), layer.k_norm.data_ptr(), cos.data_ptr(), sin.data_ptr(), q.data_ptr(),
                 kc.data_ptr(), vc.data_ptr(), tables.data_ptr(), pos.data_ptr(), batch, hidden, hq, hkv, dim,
                 blocks, bs, width, code, stream), "linear_qk_rope_append")
-            attention = self._attend(index, q, block_tables, lengths)
+            attention = self._attend(index, q, block_tables, positions, lengths)
             summed = torch.empty_like(x)
             summed_sums = torch.empty((hidden // 128, batch), dtype=torch.float32, device=device)
             _check(lib.minikv_linear_residual(
@@ -326,8 +328,8 @@ class Qwen3DecodeStep:
         return torch.mm(h, w.lm_head.t())
 
     # ------------------------------------------------------ KV pool access
-    def _fp8_begin(self, batch, block_tables, positions):
-        """Per-step state of the FP8 pool: the staging rows and each request's slot (device ops only)."""
+    def _stage_begin(self, batch, block_tables, positions):
+        """Per-step staging rows of the new tokens' K/V (and, for an FP8 pool, each request's slot)."""
         cfg, bs = self.config, self.pool.shape.block_size
         device = positions.device
         shape = (batch, 1, cfg.num_key_value_heads, cfg.head_dim)
@@ -335,26 +337,26 @@ class Qwen3DecodeStep:
         self._stage_v = torch.empty_like(self._stage_k)
         self._stage_tables = torch.arange(batch, dtype=torch.long, device=device).view(batch, 1)
         self._stage_pos = torch.zeros(batch, dtype=torch.long, device=device)
-        page = block_tables.gather(1, (positions // bs).view(-1, 1)).view(-1)
-        self._slots = (page * bs + positions % bs).contiguous()
+        if self.fp8:
+            page = block_tables.gather(1, (positions // bs).view(-1, 1)).view(-1)
+            self._slots = (page * bs + positions % bs).contiguous()
 
     def _append_target(self, index, block_tables, positions):
-        """Where the append kernels write the new token's K/V: the pool, or the FP8 path's staging rows."""
-        shape = self.pool.shape
-        if not self.fp8:
-            return (self.pool.key[index], self.pool.value[index], block_tables, positions, shape.num_blocks,
-                    shape.block_size, block_tables.shape[1])
-        # staging "pool": one 1-token page per request (page b, offset 0)
+        """Where the q/k-norm + RoPE kernels write the new token's K/V: staging rows, one 1-token page
+        per request (page b, offset 0).  The decode appends them to the pool."""
         return (self._stage_k, self._stage_v, self._stage_tables, self._stage_pos, self._stage_k.shape[0], 1, 1)
 
-    def _attend(self, index, q, block_tables, lengths):
+    def _attend(self, index, q, block_tables, positions, lengths):
         pool = self.pool
-        if not self.fp8:
-            # lengths and tables predate the append kernel just launched: chained decode
-            return paged_attention(q, pool.key[index], pool.value[index], block_tables, lengths,
-                                   pool.shape.block_size, validate=False, chained=True)
         batch = q.shape[0]
         rows = (batch, self.config.num_key_value_heads, self.config.head_dim)
+        if not self.fp8:
+            # append (from the staging rows) and decode in one launch, chained: the tables,
+            # positions and the pool rows it reads predate the kernel just launched, which
+            # wrote only q and the staging rows, so the decode stages pool rows at once
+            return paged_attention_with_append(q, pool.key[index], pool.value[index], block_tables, positions,
+                                               self._stage_k.view(rows), self._stage_v.view(rows),
+                                               pool.shape.block_size, validate=False, chained=True)
         write_kv_cache_slots_fp8(pool.key[index], pool.value[index], self._slots, self._stage_k.view(rows),
                                  self._stage_v.view(rows), pool.k_scale, pool.v_scale, kv_format=pool.kv_format,
                                  validate=False)

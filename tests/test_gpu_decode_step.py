@@ -205,8 +205,11 @@ def test_decode_step_is_bit_exact_with_the_reference_attention(cuda_device, monk
     contexts = (1, 17, 255, 700, 2047)
     cfg, weights, pool, tables, ids, positions = model_case(contexts, seed=33)
     ref_key, ref_value = pool.key.clone(), pool.value.clone()
-    monkeypatch.setattr(engine_qwen3, "paged_attention",
-                        lambda q, kc, vc, t, lens, bs, **_: paged_decode.paged_attention(q, kc, vc, t, lens, bs))
+    def reference_append_and_attention(q, kc, vc, t, offsets, key, value, bs, **_):
+        ref.append_rows(kc, vc, t, offsets, key, value, bs)
+        return paged_decode.paged_attention(q, kc, vc, t, offsets + 1, bs)
+
+    monkeypatch.setattr(engine_qwen3, "paged_attention_with_append", reference_append_and_attention)
     step = Qwen3DecodeStep(cfg, weights, pool, fused_projections=False)
     logits = step.forward_decode_batch(ids, tables, positions)
     expected = ref.decode_step(cfg, weights, ids, ref_key, ref_value, tables, positions)
