@@ -95,7 +95,8 @@ def dist_setup(args):
         backend = "nccl" if args.impl == "ours" else "gloo"
         if backend == "nccl":
             torch.cuda.set_device(local)
-        torch.distributed.init_process_group(backend, timeout=timedelta(seconds=300))
+        kwargs = {"device_id": torch.device("cuda", local)} if backend == "nccl" else {}
+        torch.distributed.init_process_group(backend, timeout=timedelta(seconds=300), **kwargs)
     elif args.impl == "ours":
         torch.cuda.set_device(local)
     return world, rank, local
@@ -785,8 +786,6 @@ def run_fp8(args, world, rank, local):
                    "global_batch": args.batch * world, "seq_len": args.context,
                    "parallelism": f"request-sharded x{world} (independent KV pools)",
                    "l2": f"inputs {2 * kq.numel() / 1e6:.0f} MB per GPU > 126 MB L2"},
-        "windows": {"count": repeats, "steps_each": args.steps, "ms_per_step_median": ms_per_step,
-                    "ms_per_step_min": per_step[0], "ms_per_step_max": per_step[-1]},
         "layer_op_tok_s": world * args.batch / (ms_per_step * 1e-3),
         "layer_op_tok_s_note": "requests served per second by ONE layer's append + decode (an operator rate); "
                                "the model's decode tok/s is qwen3.value (BASELINE config 5, all 28 layers)",
