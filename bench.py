@@ -77,7 +77,7 @@ def parse_args(argv=None):
                              "element-wise kernels")
     parser.add_argument("--kv-dtype", choices=("bf16", "fp8", "fp8_e5m2"), default="bf16",
                         help="decode: the KV pool format; fp8 = E4M3 pool, fp8_e5m2 = E5M2 pool, with per-pool "
-                             "scales (quantising slot scatter + fp8 paged attention), device-timed only")
+                             "scales (fused quantising KV append + fp8 paged attention), device-timed only")
     args = parser.parse_args(argv)
     if args.batch is None:
         args.batch = 32 if args.workload == "decode" else 256
@@ -689,14 +689,15 @@ def run_configs(args, world, rank, local):
 
 
 def run_fp8(args, world, rank, local):
-    """Decode step over an FP8 (E4M3) pool: quantising scatter of the new token + fp8 paged attention.
+    """Decode step over an FP8 pool: the fused quantising KV append + fp8 paged attention, one launch.
 
-    The bf16 pools of the decode workload are quantised once (untimed) with the
-    same scatter; the step is captured as a graph.  Bytes per step count the KV
-    pool at one byte per element, q and the output at two.
+    The bf16 pools of the decode workload are quantised once (untimed) by the
+    quantising slot scatter; the timed steps are chained fused launches captured
+    as graphs of up to 256 steps, as in the bf16 headline.  Bytes per step count
+    the KV pool at one byte per element, q and the output at two.
     """
     from myvllm_mini_engine_b200 import _lib
-    from myvllm_mini_engine_b200.kernels import paged_attention_fp8, write_kv_cache_slots_fp8
+    from myvllm_mini_engine_b200.kernels import paged_attention_fp8_with_append, write_kv_cache_slots_fp8
 
     device = torch.device("cuda", local)
     x = make_inputs(args.batch, args.context, device, seed=1234 + rank)
@@ -708,19 +709,14 @@ def run_fp8(args, world, rank, local):
     write_kv_cache_slots_fp8(kq, vq, torch.arange(pool_rows, device=device), x["key_cache"].view(-1, HKV, D),
                              x["value_cache"].view(-1, HKV, D), k_scale, v_scale, kv_format=fmt, validate=False)
     del x["key_cache"], x["value_cache"]
-    last = x["context_lens"] - 1
-    slots = (x["block_tables"].gather(1, (last // BS).view(-1, 1)).view(-1) * BS + last % BS).contiguous()
+    offsets = (x["context_lens"] - 1).contiguous()
     lengths = [args.context] * args.batch
     step_bytes = kv_bytes(lengths, 1) + 2 * args.batch * HQ * D * 2 + 8 * sum(math.ceil(n / BS) for n in lengths)
     stream = torch.cuda.current_stream(device)
 
-    def attend():
-        return paged_attention_fp8(x["query"], kq, vq, x["block_tables"], x["context_lens"], BS, k_scale, v_scale,
-                                   kv_format=fmt, validate=False)
-
-    def step():
-        write_kv_cache_slots_fp8(kq, vq, slots, x["key"], x["value"], k_scale, v_scale, kv_format=fmt, validate=False)
-        return attend()
+    def step(chained=True):
+        return paged_attention_fp8_with_append(x["query"], kq, vq, x["block_tables"], offsets, x["key"], x["value"],
+                                               BS, k_scale, v_scale, kv_format=fmt, validate=False, chained=chained)
 
     capture_stream = torch.cuda.Stream(device)
     capture_stream.wait_stream(stream)
@@ -728,19 +724,33 @@ def run_fp8(args, world, rank, local):
         for _ in range(3):
             step()
     torch.cuda.synchronize(device)
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=capture_stream):
-        step()
+    per_graph = max(1, min(args.steps, 256))
+    full, rest = divmod(args.steps, per_graph)
+    graphs = []
+    for count in [per_graph] * min(full, 1) + ([rest] if rest else []):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=capture_stream):
+            for _ in range(count):
+                step()
+        graphs.append(g)
+    big = graphs[0] if full else None
+    tail = graphs[-1] if rest else None
+
+    def run_steps():
+        for _ in range(full):
+            big.replay()
+        if tail is not None:
+            tail.replay()
+
     ev_a = torch.cuda.Event(enable_timing=True, external=True)
     ev_b = torch.cuda.Event(enable_timing=True, external=True)
     probe = torch.cuda.CUDAGraph()
     with torch.cuda.graph(probe, stream=capture_stream):
-        write_kv_cache_slots_fp8(kq, vq, slots, x["key"], x["value"], k_scale, v_scale, kv_format=fmt, validate=False)
         ev_a.record()
-        attend()
+        step(chained=False)
         ev_b.record()
-    for _ in range(args.warmup):
-        graph.replay()
+    for _ in range(max(1, math.ceil(args.warmup / args.steps))):  # at least W untimed steps
+        run_steps()
     torch.cuda.synchronize(device)
 
     def barrier():
@@ -753,8 +763,7 @@ def run_fp8(args, world, rank, local):
     with ClockSampler(local) as clocks:
         barrier()
         start.record(stream)
-        for _ in range(args.steps):
-            graph.replay()
+        run_steps()
         end.record(stream)
         barrier()
         for _ in range(min(args.steps, 50)):
@@ -773,7 +782,7 @@ def run_fp8(args, world, rank, local):
     status = _lib.device_status(device)
     if status:
         raise RuntimeError(f"device status bits set during the benchmark: {status}")
-    del graph, probe
+    del graphs, big, tail, probe
     if rank != 0:
         return None
     return {
@@ -781,7 +790,7 @@ def run_fp8(args, world, rank, local):
         "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": f"{fmt} KV, bf16 q/out",
         "data": "synthetic",
-        "config": {"workload": f"decode step (quantising KV scatter + fp8 paged attention) of {args.batch} "
+        "config": {"workload": f"decode step (fused quantising KV append + fp8 paged attention) of {args.batch} "
                                f"requests x {args.context} tokens per GPU, Hq16/Hkv8/D128, block 16",
                    "global_batch": args.batch * world, "seq_len": args.context,
                    "parallelism": f"request-sharded x{world} (independent KV pools)",
@@ -791,9 +800,10 @@ def run_fp8(args, world, rank, local):
                                "the model's decode tok/s is qwen3.value (BASELINE config 5, all 28 layers)",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                      "peak_source": peak_kind, "traffic": None,
-                     "kernel": "fp8 paged decode, timed alone between events", "bytes_per_launch": step_bytes,
-                     "launch_ms": kernel_avg_ms},
-        "e2e": None, "gpu_launches": 2 * args.steps, "clocks": clocks.summary(),
+                     "kernel": "fused fp8 KV append + paged decode, one launch timed alone between events",
+                     "bytes_per_launch": step_bytes, "launch_ms": kernel_avg_ms,
+                     "step_frac": step_bytes / (ms_per_step * 1e-3) / 1e9 / peak},
+        "e2e": None, "gpu_launches": args.steps, "clocks": clocks.summary(),
     }
 
 
@@ -1105,8 +1115,11 @@ class CpuPrefillReference:
                           f"{per_step * 1e3:.0f} ms/run, torch threads={threads}"}
 
 
+PREFILL_METRIC = "paged-prefill TFLOP/s (BASELINE config 4: CoW + slot scatter + ragged prefill)"
+
+
 def prefill_line_base(args, world):
-    return {"metric": METRIC, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+    return {"metric": PREFILL_METRIC, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "BASELINE config 4: copy-on-write of a shared prefix page, slot scatter of "
                                    "16 x 128-token chunks, ragged causal paged prefill over prefixes U[0,1024] "

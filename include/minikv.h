@@ -200,6 +200,21 @@ int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void
                             int64_t table_width, float k_scale, float v_scale, int fp8_format, int dtype,
                             void* stream);
 
+/* KV append and fp8 decode in one launch: minikv_kv_scatter_slots_fp8 of
+ * key/value ([batch, kv_heads, head_dim] in the query dtype, contiguous) at
+ * each request's slot for position token_offsets[b], followed by
+ * minikv_paged_decode_fp8 over token_offsets + 1.  The new row is quantised
+ * into its pool slot (bit-exact with the scatter: fp8(x * (1/scale))) by the
+ * CTA that attends it, then staged from the pool; the guards are those of
+ * minikv_paged_decode_append.  chained as for minikv_paged_decode_append.  No
+ * counterpart in the reference (it has no fp8 pool). */
+int minikv_paged_decode_fp8_append(const void* query, const void* key_cache, const void* value_cache,
+                                   const int64_t* block_tables, const int64_t* token_offsets, const void* key,
+                                   const void* value, void* out, void* workspace, int64_t workspace_bytes,
+                                   int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                   int64_t num_blocks, int64_t block_size, int64_t table_width, float k_scale,
+                                   float v_scale, int fp8_format, int dtype, int chained, void* stream);
+
 /* Ragged causal paged prefill over an FP8 pool: minikv_paged_prefill's
  * contract (arguments, guards, packed [tokens, q_heads, head_dim] query and
  * output) with fp16/bf16 query/output (`dtype`), K/V read as code * scale.

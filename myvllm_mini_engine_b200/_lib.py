@@ -41,6 +41,7 @@ SIGNATURES = {
     "minikv_kv_scatter_slots_fp8": (_int, [_p] * 5 + [_i64] * 7 + [_f32, _f32, _int, _int, _p]),
     "minikv_paged_decode_fp8_workspace_bytes": (_i64, [_i64] * 7 + [_int]),
     "minikv_paged_decode_fp8": (_int, [_p] * 6 + [_p, _i64] + [_i64] * 7 + [_f32, _f32, _int, _int, _p]),
+    "minikv_paged_decode_fp8_append": (_int, [_p] * 8 + [_p, _i64] + [_i64] * 7 + [_f32, _f32, _int, _int, _int, _p]),
     "minikv_paged_prefill_fp8_workspace_bytes": (_i64, [_i64] * 9 + [_int]),
     "minikv_paged_prefill_fp8": (_int, [_p] * 8 + [_p, _i64] + [_i64] * 9 + [_f32, _f32, _int, _int, _p]),
     "minikv_kv_append_batch": (_int, [_p] * 6 + [_i64] * 8 + [_int, _p]),

@@ -260,19 +260,19 @@ int64_t minikv_paged_decode_fp8_workspace_bytes(int64_t batch, int64_t q_heads, 
     return plan.ws_bytes;
 }
 
-int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void* value_cache,
-                            const int64_t* block_tables, const int64_t* context_lens, void* out,
-                            void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
-                            int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
-                            int64_t table_width, float k_scale, float v_scale, int fp8_format, int dtype,
-                            void* stream) {
+static int run_decode_fp8(const void* query, const void* key_cache, const void* value_cache,
+                          const int64_t* block_tables, const int64_t* lens, const void* key, const void* value,
+                          void* out, void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
+                          int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                          int64_t table_width, float k_scale, float v_scale, int fp8_format, int dtype, bool chained,
+                          void* stream) {
     MINIKV_REQUIRE(fp8_format == MINIKV_FP8_E4M3 || fp8_format == MINIKV_FP8_E5M2, MINIKV_EINVAL,
                    "fp8 format must be E4M3 or E5M2");
     int rc = check_fp8_decode(batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype);
     if (rc) return rc;
     MINIKV_REQUIRE(valid_scale(k_scale) && valid_scale(v_scale), MINIKV_EINVAL,
                    "fp8 KV scales must be finite and positive");
-    MINIKV_REQUIRE(query && key_cache && value_cache && block_tables && context_lens && out, MINIKV_EINVAL,
+    MINIKV_REQUIRE(query && key_cache && value_cache && block_tables && lens && out, MINIKV_EINVAL,
                    "null pointer argument");
     MINIKV_REQUIRE(aligned16(query) && aligned16(key_cache) && aligned16(value_cache) && aligned16(out),
                    MINIKV_EINVAL, "query, caches and output must be 16-byte aligned");
@@ -281,17 +281,49 @@ int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void
         return fail(MINIKV_EUNSUPPORTED, "decode shape does not fit shared memory (batch too large?)");
     MINIKV_REQUIRE(workspace != nullptr && workspace_bytes >= plan.ws_bytes && aligned16(workspace),
                    MINIKV_EINVAL, "decode workspace too small or misaligned");
-    DecodeParams p = decode_params(query, key_cache, value_cache, block_tables, context_lens, nullptr, out,
+    DecodeParams p = decode_params(query, key_cache, value_cache, block_tables, lens, nullptr, out,
                                    static_cast<unsigned char*>(workspace), batch, q_heads, kv_heads, head_dim,
                                    num_blocks, block_size, table_width, plan);
     p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim) * (double)k_scale);
     p.out_scale = v_scale;
+    p.early_prologue = chained ? 1 : 0;
+    if (key != nullptr) {  // fused append: lens holds the token offsets
+        p.append = 1;
+        p.new_k = key;
+        p.new_v = value;
+        p.k_inv = 1.0f / k_scale;  // the factors of the quantising slot scatter
+        p.v_inv = 1.0f / v_scale;
+    }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const bool e5m2 = fp8_format == MINIKV_FP8_E5M2;
     const cudaError_t err = dtype == MINIKV_F16 ? launch_decode_fp8<__half>(e5m2, (int)head_dim, p, plan, s)
                                                 : launch_decode_fp8<__nv_bfloat16>(e5m2, (int)head_dim, p, plan, s);
     if (err != cudaSuccess) return cuda_fail(err, "minikv_paged_decode_fp8 launch");
     return MINIKV_OK;
+}
+
+int minikv_paged_decode_fp8(const void* query, const void* key_cache, const void* value_cache,
+                            const int64_t* block_tables, const int64_t* context_lens, void* out,
+                            void* workspace, int64_t workspace_bytes, int64_t batch, int64_t q_heads,
+                            int64_t kv_heads, int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                            int64_t table_width, float k_scale, float v_scale, int fp8_format, int dtype,
+                            void* stream) {
+    return run_decode_fp8(query, key_cache, value_cache, block_tables, context_lens, nullptr, nullptr, out,
+                          workspace, workspace_bytes, batch, q_heads, kv_heads, head_dim, num_blocks, block_size,
+                          table_width, k_scale, v_scale, fp8_format, dtype, false, stream);
+}
+
+int minikv_paged_decode_fp8_append(const void* query, const void* key_cache, const void* value_cache,
+                                   const int64_t* block_tables, const int64_t* token_offsets, const void* key,
+                                   const void* value, void* out, void* workspace, int64_t workspace_bytes,
+                                   int64_t batch, int64_t q_heads, int64_t kv_heads, int64_t head_dim,
+                                   int64_t num_blocks, int64_t block_size, int64_t table_width, float k_scale,
+                                   float v_scale, int fp8_format, int dtype, int chained, void* stream) {
+    MINIKV_REQUIRE(key && value && token_offsets, MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(aligned16(key) && aligned16(value), MINIKV_EINVAL, "new K/V rows must be 16-byte aligned");
+    return run_decode_fp8(query, key_cache, value_cache, block_tables, token_offsets, key, value, out, workspace,
+                          workspace_bytes, batch, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width,
+                          k_scale, v_scale, fp8_format, dtype, chained != 0, stream);
 }
 
 int minikv_kv_scatter_slots_fp8(void* key_cache, void* value_cache, const int64_t* slot_mapping, const void* key,

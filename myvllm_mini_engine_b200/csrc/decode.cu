@@ -39,6 +39,8 @@
 // [0, num_blocks) masks its tokens (score -inf, paged_attention.cu:72-82); a
 // length outside [1, table_width*block_size] yields an all-zero row (:62-64);
 // a row with no unmasked token yields zeros (:99, :120).
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace minikv {
@@ -82,6 +84,7 @@ struct DecodeParams {
     const void* new_v;
     float scale_log2;     // log2(e) / sqrt(D) (times the key scale for an fp8 pool)
     float out_scale;      // fp8 pool: the value scale, applied to the output (unused otherwise)
+    float k_inv, v_inv;   // fp8 pool with the fused append: 1 / scale, the new rows' quantisation factors
 };
 
 // CTA c of G owns tiles [c*total/G, (c+1)*total/G); cta_of_tile(t) inverts it.
@@ -91,6 +94,28 @@ __device__ __forceinline__ int cta_of_tile(int t, int G, int total) {
 __device__ __forceinline__ bool cta_owns_tiles(int cta, int G, int total) {
     // with at least one tile per CTA every CTA owns some (and the 64-bit divisions are skipped)
     return total >= G || ((int64_t)cta * total) / G != ((int64_t)(cta + 1) * total) / G;
+}
+
+// One warp quantises a row of `elems` values of T (16 per lane step) into an fp8
+// pool row as fp8(x * inv): the fp32 product, then nearest-even with saturation
+// to the largest finite code.  Used by the quantising slot scatter and by the
+// fused append into an fp8 pool, so both write the same bytes.
+template <typename T, bool E5M2>
+__device__ __forceinline__ void quantize_row_warp(unsigned char* dst, const T* src, int elems, float inv, int lane) {
+    for (int c = lane * 16; c < elems; c += 32 * 16) {
+        uint32_t word[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            uint32_t packed = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float x = __fmul_rn(Elem<T>::to_float(src[c + 4 * w + i]), inv);
+                packed |= (uint32_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, E5M2 ? __NV_E5M2 : __NV_E4M3) << (8 * i);
+            }
+            word[w] = packed;
+        }
+        *reinterpret_cast<uint4*>(dst + c) = make_uint4(word[0], word[1], word[2], word[3]);
+    }
 }
 
 // Offset of token j's row in a staged tile: rows `stride` apart, or (paired
@@ -560,7 +585,9 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                 if (p.append && t0 + n == lens_s[b] && rows[n - 1] >= 0) {
                     append_dst = rows[n - 1];
                     append_b = b;
-                    rows[n - 1] = -2 - b;
+                    // 16-bit pools stage the new row from its source; an fp8 pool stages it from the
+                    // pool once it has been quantised there (below, before its tile is issued)
+                    if constexpr (esize != 1) rows[n - 1] = -2 - b;
                 }
                 for (; j < TT; ++j) rows[j] = -1;
             }
@@ -596,6 +623,26 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                 if (!waited && __any_sync(0xffffffffu, row[0] < -1 || row[1] < -1)) {  // a new row: from the previous kernel
                     griddep_wait();
                     waited = true;
+                }
+                if constexpr (esize == 1) {
+                    // fused append into an fp8 pool: quantise the tile's new row into its pool slot,
+                    // then order those generic stores before the bulk copies that read the slot
+                    const int new_dst = __shfl_sync(0xffffffffu, append_dst, i);
+                    if (p.append && new_dst >= 0) {
+                        const int64_t src = __shfl_sync(0xffffffffu, append_b, i);
+                        if (!waited) {
+                            griddep_wait();
+                            waited = true;
+                        }
+                        unsigned char* kpool = const_cast<unsigned char*>(kbase) + (int64_t)new_dst * cache_row;
+                        unsigned char* vpool = const_cast<unsigned char*>(vbase) + (int64_t)new_dst * cache_row;
+                        const T* ks = static_cast<const T*>(p.new_k) + (src * p.kv_heads + h0) * D;
+                        const T* vs = static_cast<const T*>(p.new_v) + (src * p.kv_heads + h0) * D;
+                        quantize_row_warp<T, Consumer::kE5M2>(kpool, ks, copy_row, p.k_inv, lane);
+                        quantize_row_warp<T, Consumer::kE5M2>(vpool, vs, copy_row, p.v_inv, lane);
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                        __syncwarp();
+                    }
                 }
                 const uint64_t mask = (uint64_t)__ballot_sync(0xffffffffu, ok[0]) |
                                       ((uint64_t)__ballot_sync(0xffffffffu, ok[1]) << 32);
@@ -666,7 +713,7 @@ __global__ void __launch_bounds__(kDecodeThreads, 1) paged_decode_kernel(const D
                 }
             }
             __syncwarp();
-            if (p.append) {
+            if (esize != 1 && p.append) {  // (an fp8 pool's new rows were written before their tiles)
                 if (!waited) {
                     griddep_wait();
                     waited = true;

@@ -124,6 +124,7 @@ struct Fp8MmaConsumer {
     static constexpr int VB = D / 8;       // V bytes of a token per lane
     static constexpr int kKvBytes = 1;     // bytes per cached element
     static constexpr bool kPairCapable = false;  // rows staged unpadded (runs) or padded, one per stride
+    static constexpr bool kE5M2 = E5M2;          // the pool's byte format (the fused append quantises to it)
     using Mma = MmaType<__half>;
     using Codec = Fp8Codec<E5M2>;
 
@@ -340,9 +341,9 @@ struct Fp8MmaConsumer {
 };
 
 // ------------------------------------------------------ quantising scatter
-// One warp per token: K and V rows of `row_elems` elements, 16 per lane step,
-// each rounded as e4m3(x * inv_scale) (fp32 product, then nearest-even E4M3,
-// saturating) into 16 bytes of the pool row.
+// One warp per token: K and V rows of `row_elems` elements quantised by
+// quantize_row_warp (the fused fp8 append of the decode kernel uses the same
+// function, so the two write identical bytes).
 template <typename T, bool E5M2>
 __global__ void __launch_bounds__(256) quantize_slots_kernel(
     unsigned char* __restrict__ kc, unsigned char* __restrict__ vc, const T* __restrict__ k,
@@ -359,21 +360,7 @@ __global__ void __launch_bounds__(256) quantize_slots_kernel(
         for (int which = 0; which < 2; ++which) {
             const T* src = which ? v + t * v_stride : k + t * k_stride;
             unsigned char* dst = (which ? vc : kc) + slot * row_elems;
-            const float inv = which ? v_inv : k_inv;
-            for (int64_t c = (int64_t)lane * 16; c < row_elems; c += 32 * 16) {
-                uint32_t word[4];
-#pragma unroll
-                for (int w = 0; w < 4; ++w) {
-                    uint32_t packed = 0;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float x = __fmul_rn(Elem<T>::to_float(src[c + 4 * w + i]), inv);
-                        packed |= (uint32_t)__nv_cvt_float_to_fp8(x, __NV_SATFINITE, E5M2 ? __NV_E5M2 : __NV_E4M3) << (8 * i);
-                    }
-                    word[w] = packed;
-                }
-                *reinterpret_cast<uint4*>(dst + c) = make_uint4(word[0], word[1], word[2], word[3]);
-            }
+            quantize_row_warp<T, E5M2>(dst, src, (int)row_elems, which ? v_inv : k_inv, lane);
         }
     }
 }

@@ -183,6 +183,10 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int B = p.requests, G = p.group, TM = p.tm;
+    // Chained launch: the metadata, q and the K/V pages may come from the previous kernel
+    // (the slot scatter of the same step); the launch itself overlaps that kernel's tail.
+    griddep_wait();
+    griddep_launch_dependents();
     const int Hkv = p.kv_heads;
 
     // ---- query-tile prefix over the requests (warp 0)
@@ -651,10 +655,10 @@ static cudaError_t launch_prefill_tc_typed(const CUtensorMap& mq, const CUtensor
                                            const PrefillTcParams& p, int grid, cudaStream_t stream) {
     using L = PfLayout<T, D>;
     auto kernel = paged_prefill_tc_kernel<T, D>;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::SMEM);
+    static int configured[64] = {0};  // opt-in shared-memory size, set once per device
+    cudaError_t err = ensure_smem_limit(kernel, L::SMEM, configured);
     if (err != cudaSuccess) return err;
-    kernel<<<dim3(grid), kPfThreads, L::SMEM, stream>>>(mq, mk, mv, p);
-    return cudaGetLastError();
+    return launch_chained(kernel, dim3(grid), dim3(kPfThreads), (size_t)L::SMEM, stream, mq, mk, mv, p);
 }
 
 static int run_prefill_tc(const void* q, const void* key_cache, const void* value_cache, const int64_t* cu_seqlens_q,

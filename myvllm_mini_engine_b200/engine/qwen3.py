@@ -51,7 +51,7 @@ from torch.nn import functional as F
 
 from .. import _lib
 from ..cache.kv_cache import FP8KVCachePool, PagedKVPool
-from ..kernels.fp8 import paged_attention_fp8, write_kv_cache_slots_fp8
+from ..kernels.fp8 import paged_attention_fp8_with_append
 from ..kernels.paged import paged_attention_with_append
 
 
@@ -254,7 +254,6 @@ class Qwen3DecodeStep:
         inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim))
         angles = positions.to(dtype=torch.float32)[:, None] * inv_freq[None, :]
         cos, sin = angles.cos().to(x.dtype), angles.sin().to(x.dtype)
-        lengths = positions + 1
         h = torch.empty_like(x)
         self._rms(x, None, w.layers[0].input_norm, h, None, stream)
         residual = x
@@ -266,7 +265,7 @@ class Qwen3DecodeStep:
                 qkv.data_ptr(), qkv.stride(0), layer.q_norm.data_ptr(), layer.k_norm.data_ptr(), cos.data_ptr(),
                 sin.data_ptr(), q.data_ptr(), kc.data_ptr(), vc.data_ptr(), tables.data_ptr(), pos.data_ptr(),
                 batch, hq, hkv, dim, blocks, bs, width, cfg.rms_norm_eps, self.code, stream), "qk_rope_append")
-            attention = self._attend(index, q, block_tables, positions, lengths)
+            attention = self._attend(index, q, block_tables, positions)
             o = torch.mm(attention.view(batch, hq * dim), layer.o.t())
             summed, normalized = torch.empty_like(x), torch.empty_like(x)
             self._rms(o, residual, layer.post_norm, normalized, summed, stream)
@@ -291,7 +290,6 @@ class Qwen3DecodeStep:
         inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim))
         angles = positions.to(dtype=torch.float32)[:, None] * inv_freq[None, :]
         cos, sin = angles.cos().to(x.dtype), angles.sin().to(x.dtype)
-        lengths = positions + 1
         h = torch.empty_like(x)
         self._rms(x, None, w.layers[0].input_norm, h, None, stream)
         residual, sums = x, None  # sums: per-row partial sums of squares of `residual`
@@ -308,7 +306,7 @@ class Qwen3DecodeStep:
                 layer.q_norm.data_ptr(), layer.k_norm.data_ptr(), cos.data_ptr(), sin.data_ptr(), q.data_ptr(),
                 kc.data_ptr(), vc.data_ptr(), tables.data_ptr(), pos.data_ptr(), batch, hidden, hq, hkv, dim,
                 blocks, bs, width, code, stream), "linear_qk_rope_append")
-            attention = self._attend(index, q, block_tables, positions, lengths)
+            attention = self._attend(index, q, block_tables, positions)
             summed = torch.empty_like(x)
             summed_sums = torch.empty((hidden // 128, batch), dtype=torch.float32, device=device)
             _check(lib.minikv_linear_residual(
@@ -329,40 +327,36 @@ class Qwen3DecodeStep:
 
     # ------------------------------------------------------ KV pool access
     def _stage_begin(self, batch, block_tables, positions):
-        """Per-step staging rows of the new tokens' K/V (and, for an FP8 pool, each request's slot)."""
-        cfg, bs = self.config, self.pool.shape.block_size
+        """Per-step staging rows of the new tokens' K/V."""
+        cfg = self.config
         device = positions.device
         shape = (batch, 1, cfg.num_key_value_heads, cfg.head_dim)
         self._stage_k = torch.empty(shape, dtype=self.weights.embed.dtype, device=device)
         self._stage_v = torch.empty_like(self._stage_k)
         self._stage_tables = torch.arange(batch, dtype=torch.long, device=device).view(batch, 1)
         self._stage_pos = torch.zeros(batch, dtype=torch.long, device=device)
-        if self.fp8:
-            page = block_tables.gather(1, (positions // bs).view(-1, 1)).view(-1)
-            self._slots = (page * bs + positions % bs).contiguous()
 
     def _append_target(self, index, block_tables, positions):
         """Where the q/k-norm + RoPE kernels write the new token's K/V: staging rows, one 1-token page
         per request (page b, offset 0).  The decode appends them to the pool."""
         return (self._stage_k, self._stage_v, self._stage_tables, self._stage_pos, self._stage_k.shape[0], 1, 1)
 
-    def _attend(self, index, q, block_tables, positions, lengths):
+    def _attend(self, index, q, block_tables, positions):
+        """Append (from the staging rows) and decode in one launch, chained: the tables, positions
+        and the pool rows it reads predate the kernel just launched, which wrote only q and the
+        staging rows, so the decode stages pool rows at once.  An fp8 pool quantises the new rows
+        into their slots inside the same launch."""
         pool = self.pool
         batch = q.shape[0]
         rows = (batch, self.config.num_key_value_heads, self.config.head_dim)
+        stage_k, stage_v = self._stage_k.view(rows), self._stage_v.view(rows)
         if not self.fp8:
-            # append (from the staging rows) and decode in one launch, chained: the tables,
-            # positions and the pool rows it reads predate the kernel just launched, which
-            # wrote only q and the staging rows, so the decode stages pool rows at once
             return paged_attention_with_append(q, pool.key[index], pool.value[index], block_tables, positions,
-                                               self._stage_k.view(rows), self._stage_v.view(rows),
-                                               pool.shape.block_size, validate=False, chained=True)
-        write_kv_cache_slots_fp8(pool.key[index], pool.value[index], self._slots, self._stage_k.view(rows),
-                                 self._stage_v.view(rows), pool.k_scale, pool.v_scale, kv_format=pool.kv_format,
-                                 validate=False)
-        return paged_attention_fp8(q, pool.key[index], pool.value[index], block_tables, lengths,
-                                   pool.shape.block_size, pool.k_scale, pool.v_scale, kv_format=pool.kv_format,
-                                   validate=False)
+                                               stage_k, stage_v, pool.shape.block_size, validate=False,
+                                               chained=True)
+        return paged_attention_fp8_with_append(q, pool.key[index], pool.value[index], block_tables, positions,
+                                               stage_k, stage_v, pool.shape.block_size, pool.k_scale, pool.v_scale,
+                                               kv_format=pool.kv_format, validate=False, chained=True)
 
     def greedy(self, input_ids, block_tables, positions):
         """Greedy next token of every request (argmax of the step's logits)."""

@@ -120,6 +120,46 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_len
     rounded to fp16 (saturated at +-65504).  Returns ``[B, Hq, D]`` in the query dtype.
     """
     check_backend(backend)
+    return _decode_fp8(query, key_cache, value_cache, block_tables, context_lens, block_size, k_scale, v_scale,
+                       kv_format=kv_format, validate=validate, workspace=workspace)
+
+
+def paged_attention_fp8_with_append(query, key_cache, value_cache, block_tables, token_offsets, key, value,
+                                    block_size, k_scale, v_scale, *, kv_format=None, backend="cuda", validate=True,
+                                    workspace=None, chained=False):
+    """KV append and fp8 decode in one launch (``minikv_paged_decode_fp8_append``).
+
+    The same results as quantising ``key``/``value`` ``[B, Hkv, D]`` (query dtype)
+    into each request's slot for position ``token_offsets[b]`` with
+    :func:`write_kv_cache_slots_fp8` and then :func:`paged_attention_fp8` over
+    ``token_offsets + 1`` tokens: the CTA that attends a request's last tile
+    quantises the new row into the pool (bit-exact with the scatter) and stages
+    it from there.  The fp8 counterpart of
+    :func:`~myvllm_mini_engine_b200.kernels.paged.paged_attention_with_append`,
+    with the same ``chained`` contract.  Returns ``[B, Hq, D]``.
+    """
+    check_backend(backend)
+    _require(query.is_cuda, "query must be CUDA")
+    _require(key.shape == value.shape and key.dim() == 3 and key.shape[0] == query.shape[0],
+             "batch key/value must be [batch, kv_heads, head_dim]")
+    for t in (key, value, token_offsets):
+        _require(t.device == query.device and t.is_contiguous(), "batch KV write inputs must be contiguous CUDA tensors")
+    _require(key.dtype == query.dtype and value.dtype == query.dtype, "batch KV dtype must be the query dtype")
+    _require(key_cache.dim() == 4 and key.shape[1:] == key_cache.shape[2:], "batch K/V shape mismatch")
+    _require(token_offsets.dtype == torch.int64 and token_offsets.dim() == 1, "metadata must be int64")
+    if validate:
+        width = block_tables.shape[1] if block_tables.dim() == 2 else 0
+        _require(not bool(((token_offsets < 0) | (token_offsets >= width * block_size)).any()),
+                 "batch KV offset out of range")
+    lengths = token_offsets + 1 if validate else token_offsets
+    return _decode_fp8(query, key_cache, value_cache, block_tables, lengths, block_size, k_scale, v_scale,
+                       kv_format=kv_format, validate=validate, workspace=workspace, chained=chained,
+                       append=(key, value, token_offsets))
+
+
+def _decode_fp8(query, key_cache, value_cache, block_tables, context_lens, block_size, k_scale, v_scale, *,
+                kv_format, validate, workspace, chained=False, append=None):
+    """Checks and launch of the fp8 decode; ``append = (key, value, token_offsets)`` selects the fused append."""
     fmt = _format(kv_format, key_cache.dtype)
     k_scale, v_scale = _scale(k_scale, "k_scale"), _scale(v_scale, "v_scale")
     _require(query.is_cuda, "query must be CUDA")
@@ -167,10 +207,18 @@ def paged_attention_fp8(query, key_cache, value_cache, block_tables, context_len
         elif workspace.numel() < need:
             raise RuntimeError("decode workspace too small")
         out = torch.empty_like(query)
-        status = lib.minikv_paged_decode_fp8(
-            query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
-            context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
-            batch, heads, kv_heads, dim, num_blocks, block_size, width, k_scale, v_scale, fmt, code, stream)
+        if append is not None:
+            key, value, offsets = append
+            status = lib.minikv_paged_decode_fp8_append(
+                query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
+                offsets.data_ptr(), key.data_ptr(), value.data_ptr(), out.data_ptr(), workspace.data_ptr(),
+                workspace.numel(), batch, heads, kv_heads, dim, num_blocks, block_size, width, k_scale, v_scale,
+                fmt, code, int(chained), stream)
+        else:
+            status = lib.minikv_paged_decode_fp8(
+                query.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), block_tables.data_ptr(),
+                context_lens.data_ptr(), out.data_ptr(), workspace.data_ptr(), workspace.numel(),
+                batch, heads, kv_heads, dim, num_blocks, block_size, width, k_scale, v_scale, fmt, code, stream)
     _lib.check(status, "paged_attention_fp8")
     return out
 
