@@ -335,6 +335,20 @@ int minikv_rms_norm(const void* x, const void* residual, const void* weight, voi
  * fused gate|up projection (elementwise.py:47-54, native_qwen3.py:232-240). */
 int minikv_silu_mul(const void* gate_up, void* out, int64_t rows, int64_t inter, int dtype, void* stream);
 
+/* Greedy next tokens: out[r] = index of the largest of x[r, 0 .. cols) (rows
+ * row_stride elements apart; fp32, fp16 or bf16), where a NaN counts as the
+ * largest and ties take the lowest index -- the semantics of the reference's
+ * greedy sampler, logits.argmax(dim=-1) (mini_engine/sampling.py:14-22; its
+ * CUDA variant sampling.cu:52-70).  One launch: column slices per row, the
+ * last slice to finish combines them.  `workspace` holds
+ * minikv_argmax_workspace_bytes(rows, cols) bytes (16-byte aligned), zero
+ * before its first use and left zero by every call (its ticket counters);
+ * calls that may overlap on the GPU need separate workspaces.  No host
+ * synchronisation: capturable in a CUDA graph. */
+int64_t minikv_argmax_workspace_bytes(int64_t rows, int64_t cols);
+int minikv_argmax_rows(const void* x, int64_t rows, int64_t cols, int64_t row_stride, int dtype, void* workspace,
+                       int64_t workspace_bytes, int64_t* out, void* stream);
+
 /* Decode-step attention prologue in one launch over the fused q|k|v
  * projection rows (qkv[b, (q_heads + 2 kv_heads) * head_dim], row stride
  * qkv_stride elements): RMSNorm of every q and k head (q_weight, k_weight),

@@ -53,6 +53,8 @@ SIGNATURES = {
     "minikv_build_decode_tables": (_int, [_p] * 6 + [_i64, _i64] + [_p] * 3 + [_p]),
     "minikv_rms_norm": (_int, [_p] * 5 + [_i64, _i64, ctypes.c_double, _int, _p]),
     "minikv_silu_mul": (_int, [_p, _p, _i64, _i64, _int, _p]),
+    "minikv_argmax_workspace_bytes": (_i64, [_i64, _i64]),
+    "minikv_argmax_rows": (_int, [_p, _i64, _i64, _i64, _int, _p, _i64, _p, _p]),
     "minikv_qk_rope_append": (_int, [_p, _i64] + [_p] * 9 + [_i64] * 7 + [ctypes.c_double, _int, _p]),
     "minikv_pack_linear": (_int, [_p, _p, _i64, _i64, _i64, _int, _p]),
     "minikv_linear": (_int, [_p, _i64, _p, _p, ctypes.c_double, _p, _p, _i64, _i64, _i64, _int, _p]),

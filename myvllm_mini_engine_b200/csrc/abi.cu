@@ -588,6 +588,25 @@ int minikv_silu_mul(const void* gate_up, void* out, int64_t rows, int64_t inter,
     return MINIKV_OK;
 }
 
+int64_t minikv_argmax_workspace_bytes(int64_t rows, int64_t cols) {
+    if (rows <= 0 || cols <= 0 || rows > 65535) return -1;
+    return argmax_workspace_bytes(rows, cols, sm_count());
+}
+
+int minikv_argmax_rows(const void* x, int64_t rows, int64_t cols, int64_t row_stride, int dtype, void* workspace,
+                       int64_t workspace_bytes, int64_t* out, void* stream) {
+    MINIKV_REQUIRE(valid_dtype(dtype), MINIKV_EINVAL, "FP32/FP16/BF16 required");
+    MINIKV_REQUIRE(rows > 0 && rows <= 65535 && cols > 0 && row_stride >= cols, MINIKV_EINVAL,
+                   "argmax needs 1..65535 rows of at least one column within the row stride");
+    MINIKV_REQUIRE(x && out && workspace, MINIKV_EINVAL, "null pointer argument");
+    MINIKV_REQUIRE(workspace_bytes >= argmax_workspace_bytes(rows, cols, sm_count()) && aligned16(workspace),
+                   MINIKV_EINVAL, "argmax workspace too small or misaligned");
+    cudaError_t err = launch_argmax(dtype, x, rows, cols, row_stride, workspace, out, sm_count(),
+                                    static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return cuda_fail(err, "minikv_argmax_rows launch");
+    return MINIKV_OK;
+}
+
 int minikv_qk_rope_append(const void* qkv, int64_t qkv_stride, const void* q_weight, const void* k_weight,
                           const void* cos, const void* sin, void* q_out, void* key_cache, void* value_cache,
                           const int64_t* block_tables, const int64_t* token_offsets, int64_t batch, int64_t q_heads,

@@ -213,6 +213,136 @@ __global__ void __launch_bounds__(256) qk_rope_append_kernel(const QkRopeParams 
     }
 }
 
+// ------------------------------------------------------------ greedy argmax
+// out[r] = index of the largest value of row r: a NaN counts as the largest
+// and ties take the lowest index, the semantics of torch.argmax (the
+// reference's greedy sampler, mini_engine/sampling.py:14-22).  One launch:
+// CTA (s, r) scans columns [s * per, (s + 1) * per) of row r with 16-byte
+// loads and stores its best (value, index); the CTA that takes the row's last
+// ticket (an acquire-release atomic that wraps to zero, so the counters are
+// left zero) combines the slices in column order.
+__device__ __forceinline__ bool argmax_before(float a, int64_t ai, float b, int64_t bi) {
+    // does (a, ai) win over (b, bi)?
+    const bool an = a != a, bn = b != b;
+    if (an || bn) return an && (!bn || ai < bi);
+    return a > b || (a == b && ai < bi);
+}
+
+struct ArgmaxBest {
+    float v;
+    int64_t i;
+    __device__ __forceinline__ void take(float x, int64_t j) {
+        if (argmax_before(x, j, v, i)) {
+            v = x;
+            i = j;
+        }
+    }
+};
+
+template <typename T, bool kVec>
+__global__ void __launch_bounds__(256) argmax_rows_kernel(const T* __restrict__ x, int64_t cols, int64_t stride,
+                                                          int64_t per, float* __restrict__ part_v,
+                                                          int64_t* __restrict__ part_i,
+                                                          unsigned int* __restrict__ tickets,
+                                                          int64_t* __restrict__ out) {
+    __shared__ float wv[8];
+    __shared__ int64_t wi[8];
+    __shared__ int last;
+    griddep_wait();
+    griddep_launch_dependents();
+    const int splits = gridDim.x, s = blockIdx.x;
+    const int64_t r = blockIdx.y;
+    const T* row = x + r * stride;
+    const int64_t lo = (int64_t)s * per, hi = min(cols, lo + per);
+    ArgmaxBest best{-INFINITY, INT64_MAX};
+    if (kVec) {  // the row start and `per` are 16-byte multiples: [lo, hiv) in 16-byte vectors of kV elements
+        constexpr int kV = Elem<T>::kPerVec;
+        const int64_t hiv = lo + ((hi - lo) / kV) * kV;
+        for (int64_t c = lo + kV * (int64_t)threadIdx.x; c < hiv; c += kV * (int64_t)blockDim.x) {
+            float f[kV];
+            Elem<T>::load(*reinterpret_cast<const uint4*>(row + c), f);
+#pragma unroll
+            for (int e = 0; e < kV; ++e) best.take(f[e], c + e);
+        }
+        for (int64_t c = hiv + threadIdx.x; c < hi; c += blockDim.x) best.take(Elem<T>::to_float(row[c]), c);
+    } else {
+        for (int64_t c = lo + threadIdx.x; c < hi; c += blockDim.x) best.take(Elem<T>::to_float(row[c]), c);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
+        const int64_t oi = __shfl_xor_sync(0xffffffffu, best.i, o);
+        best.take(ov, oi);
+    }
+    const int warp = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) {
+        wv[warp] = best.v;
+        wi[warp] = best.i;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best.take(wv[w], wi[w]);
+        part_v[r * splits + s] = best.v;
+        part_i[r * splits + s] = best.i;
+        unsigned int ticket = 0;
+        asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
+                     : "=r"(ticket) : "l"(tickets + r), "r"((unsigned int)(splits - 1)) : "memory");
+        last = ticket == (unsigned int)(splits - 1);
+    }
+    __syncthreads();
+    if (!last || threadIdx.x != 0) return;
+    ArgmaxBest row_best{-INFINITY, INT64_MAX};
+    for (int k = 0; k < splits; ++k) row_best.take(part_v[r * splits + k], part_i[r * splits + k]);
+    out[r] = row_best.i == INT64_MAX ? 0 : row_best.i;
+}
+
+// Column slices per row: enough CTAs for two per SM, slices of at least 2048
+// columns, a multiple of 8 columns each.
+static void argmax_plan(int64_t rows, int64_t cols, int sms, int* splits, int64_t* per) {
+    const int64_t want = std::max<int64_t>(1, std::min<int64_t>((2 * (int64_t)sms + rows - 1) / rows,
+                                                                (cols + 2047) / 2048));
+    int64_t p = (cols + want - 1) / want;
+    p = (p + 7) / 8 * 8;
+    *per = std::max<int64_t>(p, 8);
+    *splits = (int)((cols + *per - 1) / *per);
+}
+
+static int64_t argmax_workspace_bytes(int64_t rows, int64_t cols, int sms) {
+    int splits;
+    int64_t per;
+    argmax_plan(rows, cols, sms, &splits, &per);
+    const int64_t tickets = (rows * 4 + 255) / 256 * 256;
+    const int64_t values = (rows * splits * 4 + 255) / 256 * 256;
+    return tickets + values + rows * splits * 8;
+}
+
+template <typename T>
+static cudaError_t launch_argmax_typed(const void* x, int64_t rows, int64_t cols, int64_t stride, void* ws,
+                                       int64_t* out, int sms, cudaStream_t s) {
+    int splits;
+    int64_t per;
+    argmax_plan(rows, cols, sms, &splits, &per);
+    unsigned char* w = static_cast<unsigned char*>(ws);
+    unsigned int* tickets = reinterpret_cast<unsigned int*>(w);
+    float* part_v = reinterpret_cast<float*>(w + (rows * 4 + 255) / 256 * 256);
+    int64_t* part_i = reinterpret_cast<int64_t*>(w + (rows * 4 + 255) / 256 * 256 + (rows * splits * 4 + 255) / 256 * 256);
+    const T* xt = static_cast<const T*>(x);
+    const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (stride * (int64_t)sizeof(T)) % 16 == 0;
+    const dim3 grid((unsigned)splits, (unsigned)rows);
+    if (vec)
+        return launch_chained(argmax_rows_kernel<T, true>, grid, dim3(256), 0, s, xt, cols, stride, per, part_v,
+                              part_i, tickets, out);
+    return launch_chained(argmax_rows_kernel<T, false>, grid, dim3(256), 0, s, xt, cols, stride, per, part_v, part_i,
+                          tickets, out);
+}
+
+static cudaError_t launch_argmax(int dtype, const void* x, int64_t rows, int64_t cols, int64_t stride, void* ws,
+                                 int64_t* out, int sms, cudaStream_t s) {
+    if (dtype == MINIKV_F32) return launch_argmax_typed<float>(x, rows, cols, stride, ws, out, sms, s);
+    if (dtype == MINIKV_F16) return launch_argmax_typed<__half>(x, rows, cols, stride, ws, out, sms, s);
+    return launch_argmax_typed<__nv_bfloat16>(x, rows, cols, stride, ws, out, sms, s);
+}
+
 // ---------------------------------------------------------------- launchers
 template <typename T>
 static cudaError_t launch_rms_norm_typed(const void* x, const void* residual, const void* weight, void* out,

@@ -148,6 +148,41 @@ def _check(status, what):
     _lib.check(status, what)
 
 
+_ARGMAX_WORKSPACES: dict = {}
+_ARGMAX_RETIRED: list = []
+
+
+def greedy_ids(logits: torch.Tensor) -> torch.Tensor:
+    """Greedy next token of every row of ``logits [batch, vocab]``: ``logits.argmax(dim=-1)``.
+
+    The reference samples greedily with ``logits.argmax(dim=-1)`` (``mini_engine/sampling.py:14-22``):
+    a NaN counts as the largest value and ties take the lowest index.  ``minikv_argmax_rows``
+    computes the same in one launch.  Its ticket counters live in a zero-filled buffer kept per
+    CUDA stream (left zero by every call; never freed, since a captured graph may use it).
+    """
+    if logits.ndim != 2 or not logits.is_cuda or logits.stride(1) != 1:
+        raise ValueError("logits must be a 2D CUDA tensor with contiguous rows")
+    lib = _lib.load()
+    rows, cols = logits.shape
+    need = lib.minikv_argmax_workspace_bytes(rows, cols)
+    if need < 0:
+        raise ValueError("argmax takes 1..65535 rows of at least one column")
+    device = logits.device
+    with _lib.on_device(device):
+        stream = _lib.stream_of(device)
+        key = (device.index, stream)
+        ws = _ARGMAX_WORKSPACES.get(key)
+        if ws is None or ws.numel() < need:
+            if ws is not None:
+                _ARGMAX_RETIRED.append(ws)
+            ws = torch.zeros(max(need, 256), dtype=torch.uint8, device=device)
+            _ARGMAX_WORKSPACES[key] = ws
+        out = torch.empty(rows, dtype=torch.long, device=device)
+        _check(lib.minikv_argmax_rows(logits.data_ptr(), rows, cols, logits.stride(0), _lib.dtype_code(logits.dtype),
+                                      ws.data_ptr(), ws.numel(), out.data_ptr(), stream), "argmax_rows")
+    return out
+
+
 def pack_linear(weight: torch.Tensor, *, pair_offset: int = 0) -> torch.Tensor:
     """A packed copy of an ``[out_features, in_features]`` weight for the fused projections.
 
@@ -203,6 +238,16 @@ class Qwen3DecodeStep:
             raise ValueError("fused projections need head_dim 128, hidden and q-head sizes that are multiples "
                              "of 128 and an intermediate size that is a multiple of 64")
         self.fused_projections = fusable if fused_projections is None else bool(fused_projections)
+        # Rotary tables of every position, computed once with the torch ops the reference applies per
+        # step (inv_freq, fp32 angles, cos/sin rounded to the model dtype), so a step's rows are
+        # bit-identical to computing them on the fly; a step gathers its rows.
+        dim, device = config.head_dim, weights.embed.device
+        inv_freq = 1.0 / (config.rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim))
+        angles = torch.arange(config.max_position_embeddings, device=device, dtype=torch.float32)[:, None] * inv_freq
+        self._cos_table = angles.cos().to(weights.embed.dtype)
+        self._sin_table = angles.sin().to(weights.embed.dtype)
+        del angles
+        self._stage_index = {}
         self._packed = []
         if self.fused_projections:
             # the fused projections read packed weights (copies made once, here)
@@ -219,6 +264,15 @@ class Qwen3DecodeStep:
                 and config.intermediate_size % 64 == 0)
 
     # ------------------------------------------------------------ fused ops
+    def _rotary(self, positions):
+        """cos / sin rows ``[batch, head_dim / 2]`` of the positions, gathered from the tables.
+
+        Positions are clamped into the table (a captured graph skips the host range check; the
+        KV kernels guard the pool on their own), so the gather never reads outside it.
+        """
+        rows = positions.clamp(0, self._cos_table.shape[0] - 1)
+        return self._cos_table.index_select(0, rows), self._sin_table.index_select(0, rows)
+
     def _rms(self, x, residual, weight, out, sum_out, stream):
         _check(self.lib.minikv_rms_norm(x.data_ptr(), None if residual is None else residual.data_ptr(),
                                         weight.data_ptr(), out.data_ptr(),
@@ -251,9 +305,7 @@ class Qwen3DecodeStep:
         if self.fused_projections and batch <= self.FUSED_MAX_BATCH:
             return self._forward_fused(input_ids, block_tables, positions, stream)
         x = F.embedding(input_ids, w.embed)
-        inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim))
-        angles = positions.to(dtype=torch.float32)[:, None] * inv_freq[None, :]
-        cos, sin = angles.cos().to(x.dtype), angles.sin().to(x.dtype)
+        cos, sin = self._rotary(positions)
         h = torch.empty_like(x)
         self._rms(x, None, w.layers[0].input_norm, h, None, stream)
         residual = x
@@ -287,9 +339,7 @@ class Qwen3DecodeStep:
         hidden, inter, eps = cfg.hidden_size, cfg.intermediate_size, cfg.rms_norm_eps
         shape = pool.shape
         x = F.embedding(input_ids, w.embed)
-        inv_freq = 1.0 / (cfg.rope_theta ** (torch.arange(0, dim, 2, device=device).float() / dim))
-        angles = positions.to(dtype=torch.float32)[:, None] * inv_freq[None, :]
-        cos, sin = angles.cos().to(x.dtype), angles.sin().to(x.dtype)
+        cos, sin = self._rotary(positions)
         h = torch.empty_like(x)
         self._rms(x, None, w.layers[0].input_norm, h, None, stream)
         residual, sums = x, None  # sums: per-row partial sums of squares of `residual`
@@ -333,8 +383,11 @@ class Qwen3DecodeStep:
         shape = (batch, 1, cfg.num_key_value_heads, cfg.head_dim)
         self._stage_k = torch.empty(shape, dtype=self.weights.embed.dtype, device=device)
         self._stage_v = torch.empty_like(self._stage_k)
-        self._stage_tables = torch.arange(batch, dtype=torch.long, device=device).view(batch, 1)
-        self._stage_pos = torch.zeros(batch, dtype=torch.long, device=device)
+        key = (batch, device)
+        if key not in self._stage_index:  # read-only index tensors: made once per batch size
+            self._stage_index[key] = (torch.arange(batch, dtype=torch.long, device=device).view(batch, 1),
+                                      torch.zeros(batch, dtype=torch.long, device=device))
+        self._stage_tables, self._stage_pos = self._stage_index[key]
 
     def _append_target(self, index, block_tables, positions):
         """Where the q/k-norm + RoPE kernels write the new token's K/V: staging rows, one 1-token page
@@ -360,7 +413,7 @@ class Qwen3DecodeStep:
 
     def greedy(self, input_ids, block_tables, positions):
         """Greedy next token of every request (argmax of the step's logits)."""
-        return torch.argmax(self.forward_decode_batch(input_ids, block_tables, positions), dim=-1)
+        return greedy_ids(self.forward_decode_batch(input_ids, block_tables, positions))
 
 
 class DecodeGraph:

@@ -89,3 +89,16 @@ def test_library_built_from_other_sources_is_refused(monkeypatch):
         _lib.load()
     monkeypatch.undo()
     assert _lib.load() is not None
+
+
+def test_argmax_argument_errors():
+    lib = _lib.load()
+    assert lib.minikv_argmax_workspace_bytes(0, 10) < 0
+    assert lib.minikv_argmax_workspace_bytes(4, 151936) > 0
+    null = ctypes.c_void_p(16)
+    rc = lib.minikv_argmax_rows(null, 0, 10, 10, _lib.BF16, null, 1 << 20, null, None)
+    assert rc == _lib.EINVAL and "rows" in lib.minikv_last_error().decode()
+    rc = lib.minikv_argmax_rows(null, 4, 10, 8, _lib.BF16, null, 1 << 20, null, None)
+    assert rc == _lib.EINVAL and "row stride" in lib.minikv_last_error().decode()
+    rc = lib.minikv_argmax_rows(null, 4, 151936, 151936, _lib.BF16, null, 16, null, None)
+    assert rc == _lib.EINVAL and "workspace" in lib.minikv_last_error().decode()
