@@ -178,6 +178,12 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     // needs the softmax of tile g to have read its S buffer (and these words)
     uint32_t* key_ok = reinterpret_cast<uint32_t*>(bar + 18);
     uint64_t* mma_drain = bar + 26;  // the issuer's last commit: every MMA it issued has completed
+    // [2] by S buffer: the MMA thread has issued S of the tile (after acquiring its K slot and key_ok
+    // words).  The softmax waits here, not on k_full: at an item boundary the first two S of the next
+    // item need no P V, so the K ring can complete a slot's phase twice before the softmax warps,
+    // still in the previous item's epilogue, reach that tile, and a parity wait two phases behind
+    // never returns; S(g + 2) waits for the softmax of tile g, so this barrier stays within one phase.
+    uint64_t* bits_full = bar + 29;
     int* qt_pfx = reinterpret_cast<int*>(smem + L::OFF_PFX);         // [requests + 1]
     uint32_t* order = reinterpret_cast<uint32_t*>(smem + L::OFF_ORD);  // [kPfMaxSort] sorted keys, then the keys
 
@@ -226,6 +232,8 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
         mbar_init(p_full, 8);
         mbar_init(o_done, 1);
         mbar_init(mma_drain, 1);
+        mbar_init(&bits_full[0], 1);
+        mbar_init(&bits_full[1], 1);
         mbar_init_fence();
     }
     if (warp == 1) {
@@ -404,6 +412,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                             }
                             umma_commit(&s_full[slot]);
                             umma_commit(&k_empty[slot]);
+                            mbar_arrive(&bits_full[slot]);  // release: the key_ok words acquired with K
                             if (ns == n_tiles - 1) umma_commit(q_empty);
                             ++ns;
                             progressed = true;
@@ -481,7 +490,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
             float m_run = -INFINITY, l_run = 0.f;
             for (int j = 0; j < n_tiles; ++j) {
                 const int gj = gt + j, slot = gj & 1;
-                mbar_wait(&k_full[slot], (gj >> 1) & 1);
+                mbar_wait(&bits_full[slot], (gj >> 1) & 1);
                 uint32_t wk[4];
 #pragma unroll
                 for (int q = 0; q < 4; ++q) wk[q] = key_ok[4 * (gj & 3) + q];
