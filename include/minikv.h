@@ -339,12 +339,12 @@ int minikv_silu_mul(const void* gate_up, void* out, int64_t rows, int64_t inter,
  * row_stride elements apart; fp32, fp16 or bf16), where a NaN counts as the
  * largest and ties take the lowest index -- the semantics of the reference's
  * greedy sampler, logits.argmax(dim=-1) (mini_engine/sampling.py:14-22; its
- * CUDA variant sampling.cu:52-70).  One launch: column slices per row, the
- * last slice to finish combines them.  `workspace` holds
- * minikv_argmax_workspace_bytes(rows, cols) bytes (16-byte aligned), zero
- * before its first use and left zero by every call (its ticket counters);
- * calls that may overlap on the GPU need separate workspaces.  No host
- * synchronisation: capturable in a CUDA graph. */
+ * CUDA variant sampling.cu:52-70).  Two chained launches: every warp of the
+ * column slices of a row stores its best as a 64-bit key, then one warp per
+ * row takes the largest key and turns it into the index.  `workspace` holds
+ * minikv_argmax_workspace_bytes(rows, cols) bytes (16-byte aligned; scratch,
+ * any contents); calls that may overlap on the GPU need separate workspaces.
+ * No host synchronisation: capturable in a CUDA graph. */
 int64_t minikv_argmax_workspace_bytes(int64_t rows, int64_t cols);
 int minikv_argmax_rows(const void* x, int64_t rows, int64_t cols, int64_t row_stride, int dtype, void* workspace,
                        int64_t workspace_bytes, int64_t* out, void* stream);

@@ -596,8 +596,8 @@ int64_t minikv_argmax_workspace_bytes(int64_t rows, int64_t cols) {
 int minikv_argmax_rows(const void* x, int64_t rows, int64_t cols, int64_t row_stride, int dtype, void* workspace,
                        int64_t workspace_bytes, int64_t* out, void* stream) {
     MINIKV_REQUIRE(valid_dtype(dtype), MINIKV_EINVAL, "FP32/FP16/BF16 required");
-    MINIKV_REQUIRE(rows > 0 && rows <= 65535 && cols > 0 && row_stride >= cols, MINIKV_EINVAL,
-                   "argmax needs 1..65535 rows of at least one column within the row stride");
+    MINIKV_REQUIRE(rows > 0 && rows <= 65535 && cols > 0 && cols < (1ll << 31) && row_stride >= cols, MINIKV_EINVAL,
+                   "argmax needs 1..65535 rows of 1..2^31-1 columns within the row stride");
     MINIKV_REQUIRE(x && out && workspace, MINIKV_EINVAL, "null pointer argument");
     MINIKV_REQUIRE(workspace_bytes >= argmax_workspace_bytes(rows, cols, sm_count()) && aligned16(workspace),
                    MINIKV_EINVAL, "argmax workspace too small or misaligned");

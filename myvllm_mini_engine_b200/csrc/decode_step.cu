@@ -19,6 +19,8 @@
 // product with the weight, each rotary product and their sum) is rounded to
 // T here at the same point; reductions and transcendental functions run in
 // fp32, as torch's opmath does.
+#include <climits>
+
 #include "common.cuh"
 
 namespace minikv {
@@ -216,12 +218,15 @@ __global__ void __launch_bounds__(256) qk_rope_append_kernel(const QkRopeParams 
 // ------------------------------------------------------------ greedy argmax
 // out[r] = index of the largest value of row r: a NaN counts as the largest
 // and ties take the lowest index, the semantics of torch.argmax (the
-// reference's greedy sampler, mini_engine/sampling.py:14-22).  One launch:
-// CTA (s, r) scans columns [s * per, (s + 1) * per) of row r with 16-byte
-// loads and stores its best (value, index); the CTA that takes the row's last
-// ticket (an acquire-release atomic that wraps to zero, so the counters are
-// left zero) combines the slices in column order.
-__device__ __forceinline__ bool argmax_before(float a, int64_t ai, float b, int64_t bi) {
+// reference's greedy sampler, mini_engine/sampling.py:14-22).  Two chained
+// launches.  argmax_rows_kernel: CTA (s, r) scans columns [s * per, (s + 1) *
+// per) of row r with 16-byte loads (four in flight per thread); each warp
+// stores its best as a 64-bit key that orders (value, then lower index): the
+// high word is the value's bits made monotonic (every NaN the largest), the
+// low word the complemented column.  argmax_keys_kernel (one warp per row,
+// after the first launch has ended) takes the largest key of the row's slots
+// and turns it into the index.
+__device__ __forceinline__ bool argmax_before(float a, int ai, float b, int bi) {
     // does (a, ai) win over (b, bi)?
     const bool an = a != a, bn = b != b;
     if (an || bn) return an && (!bn || ai < bi);
@@ -230,8 +235,8 @@ __device__ __forceinline__ bool argmax_before(float a, int64_t ai, float b, int6
 
 struct ArgmaxBest {
     float v;
-    int64_t i;
-    __device__ __forceinline__ void take(float x, int64_t j) {
+    int i;  // column (columns < 2^31); INT_MAX: none yet
+    __device__ __forceinline__ void take(float x, int j) {
         if (argmax_before(x, j, v, i)) {
             v = x;
             i = j;
@@ -239,81 +244,117 @@ struct ArgmaxBest {
     }
 };
 
+// max with NaN propagation (a NaN operand gives NaN)
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int i) {
+    const uint32_t u = __float_as_uint(v);
+    const uint32_t hi = (v != v) ? 0xffffffffu : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+    return ((unsigned long long)hi << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+}
+
 template <typename T, bool kVec>
 __global__ void __launch_bounds__(256) argmax_rows_kernel(const T* __restrict__ x, int64_t cols, int64_t stride,
-                                                          int64_t per, float* __restrict__ part_v,
-                                                          int64_t* __restrict__ part_i,
-                                                          unsigned int* __restrict__ tickets,
-                                                          int64_t* __restrict__ out) {
-    __shared__ float wv[8];
-    __shared__ int64_t wi[8];
-    __shared__ int last;
+                                                          int64_t per, unsigned long long* __restrict__ slots) {
     griddep_wait();
     griddep_launch_dependents();
-    const int splits = gridDim.x, s = blockIdx.x;
+    const int s = blockIdx.x;
     const int64_t r = blockIdx.y;
     const T* row = x + r * stride;
     const int64_t lo = (int64_t)s * per, hi = min(cols, lo + per);
-    ArgmaxBest best{-INFINITY, INT64_MAX};
+    ArgmaxBest best{-INFINITY, INT_MAX};
     if (kVec) {  // the row start and `per` are 16-byte multiples: [lo, hiv) in 16-byte vectors of kV elements
-        constexpr int kV = Elem<T>::kPerVec;
+        constexpr int kV = Elem<T>::kPerVec, kInFlight = 4;  // loads issued before any is consumed
         const int64_t hiv = lo + ((hi - lo) / kV) * kV;
-        for (int64_t c = lo + kV * (int64_t)threadIdx.x; c < hiv; c += kV * (int64_t)blockDim.x) {
-            float f[kV];
-            Elem<T>::load(*reinterpret_cast<const uint4*>(row + c), f);
+        const int64_t step = kV * (int64_t)blockDim.x;
+        for (int64_t c0 = lo + kV * (int64_t)threadIdx.x; c0 < hiv; c0 += kInFlight * step) {
+            uint4 v[kInFlight];
 #pragma unroll
-            for (int e = 0; e < kV; ++e) best.take(f[e], c + e);
+            for (int u = 0; u < kInFlight; ++u)
+                if (c0 + u * step < hiv) v[u] = *reinterpret_cast<const uint4*>(row + c0 + u * step);
+#pragma unroll
+            for (int u = 0; u < kInFlight; ++u) {
+                if (c0 + u * step >= hiv) break;
+                float f[kV];
+                Elem<T>::load(v[u], f);
+                // a thread visits its columns in increasing order, so a vector changes its best only with
+                // a larger value (at its first column holding the vector's max) or with the thread's first
+                // NaN; the vector's NaN-propagating max shows either
+                const int c = (int)(c0 + u * step);
+                float m = f[0];
+#pragma unroll
+                for (int e = 1; e < kV; ++e) m = max_nan(m, f[e]);
+                if (m != m) {
+                    if (best.v == best.v) {
+                        int j = 0;
+#pragma unroll
+                        for (int e = kV - 1; e >= 0; --e) j = (f[e] != f[e]) ? e : j;
+                        best.v = m;
+                        best.i = c + j;
+                    }
+                } else if (m > best.v || best.i == INT_MAX) {
+                    int j = 0;
+#pragma unroll
+                    for (int e = kV - 1; e >= 0; --e) j = (f[e] == m) ? e : j;
+                    best.v = m;
+                    best.i = c + j;
+                }
+            }
         }
-        for (int64_t c = hiv + threadIdx.x; c < hi; c += blockDim.x) best.take(Elem<T>::to_float(row[c]), c);
+        for (int64_t c = hiv + threadIdx.x; c < hi; c += blockDim.x) best.take(Elem<T>::to_float(row[c]), (int)c);
     } else {
-        for (int64_t c = lo + threadIdx.x; c < hi; c += blockDim.x) best.take(Elem<T>::to_float(row[c]), c);
+        for (int64_t c = lo + threadIdx.x; c < hi; c += blockDim.x) best.take(Elem<T>::to_float(row[c]), (int)c);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
-        const int64_t oi = __shfl_xor_sync(0xffffffffu, best.i, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best.i, o);
         best.take(ov, oi);
     }
-    const int warp = threadIdx.x >> 5;
-    if ((threadIdx.x & 31) == 0) {
-        wv[warp] = best.v;
-        wi[warp] = best.i;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best.take(wv[w], wi[w]);
-        part_v[r * splits + s] = best.v;
-        part_i[r * splits + s] = best.i;
-        unsigned int ticket = 0;
-        asm volatile("atom.acq_rel.gpu.global.inc.u32 %0, [%1], %2;"
-                     : "=r"(ticket) : "l"(tickets + r), "r"((unsigned int)(splits - 1)) : "memory");
-        last = ticket == (unsigned int)(splits - 1);
-    }
-    __syncthreads();
-    if (!last || threadIdx.x != 0) return;
-    ArgmaxBest row_best{-INFINITY, INT64_MAX};
-    for (int k = 0; k < splits; ++k) row_best.take(part_v[r * splits + k], part_i[r * splits + k]);
-    out[r] = row_best.i == INT64_MAX ? 0 : row_best.i;
+    // slot (r, s, warp); 0 (below every key) when the warp saw no column
+    if ((threadIdx.x & 31) == 0)
+        slots[(r * gridDim.x + s) * (blockDim.x >> 5) + (threadIdx.x >> 5)] =
+            best.i != INT_MAX ? argmax_key(best.v, best.i) : 0ull;
 }
 
-// Column slices per row: enough CTAs for two per SM, slices of at least 2048
-// columns, a multiple of 8 columns each.
+__global__ void __launch_bounds__(256) argmax_keys_kernel(const unsigned long long* __restrict__ slots,
+                                                          int64_t* __restrict__ out, int64_t rows, int per_row) {
+    griddep_wait();  // the scan has ended and its slots are visible
+    griddep_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < rows;
+         r += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+        unsigned long long key = 0ull;
+        for (int k = lane; k < per_row; k += 32) key = max(key, slots[r * per_row + k]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) key = max(key, __shfl_xor_sync(0xffffffffu, key, o));
+        if (lane == 0) out[r] = (int64_t)(0xffffffffu - (uint32_t)(key & 0xffffffffull));
+    }
+}
+
+// Column slices per row: 8192 columns (four 16-byte loads in flight per thread
+// of 256 for 16-bit logits), narrower (down to 2048) when that leaves fewer than
+// two CTAs per SM; a multiple of 8 columns each.
 static void argmax_plan(int64_t rows, int64_t cols, int sms, int* splits, int64_t* per) {
-    const int64_t want = std::max<int64_t>(1, std::min<int64_t>((2 * (int64_t)sms + rows - 1) / rows,
-                                                                (cols + 2047) / 2048));
+    const int64_t by_width = (cols + 8191) / 8192;
+    const int64_t want = std::max<int64_t>(by_width, std::min<int64_t>((2 * (int64_t)sms + rows - 1) / rows,
+                                                                       (cols + 2047) / 2048));
     int64_t p = (cols + want - 1) / want;
     p = (p + 7) / 8 * 8;
     *per = std::max<int64_t>(p, 8);
     *splits = (int)((cols + *per - 1) / *per);
 }
 
+// one 64-bit key slot per (row, slice, warp of 8)
 static int64_t argmax_workspace_bytes(int64_t rows, int64_t cols, int sms) {
     int splits;
     int64_t per;
     argmax_plan(rows, cols, sms, &splits, &per);
-    const int64_t tickets = (rows * 4 + 255) / 256 * 256;
-    const int64_t values = (rows * splits * 4 + 255) / 256 * 256;
-    return tickets + values + rows * splits * 8;
+    return (rows * splits * 8 * 8 + 255) / 256 * 256;
 }
 
 template <typename T>
@@ -322,18 +363,17 @@ static cudaError_t launch_argmax_typed(const void* x, int64_t rows, int64_t cols
     int splits;
     int64_t per;
     argmax_plan(rows, cols, sms, &splits, &per);
-    unsigned char* w = static_cast<unsigned char*>(ws);
-    unsigned int* tickets = reinterpret_cast<unsigned int*>(w);
-    float* part_v = reinterpret_cast<float*>(w + (rows * 4 + 255) / 256 * 256);
-    int64_t* part_i = reinterpret_cast<int64_t*>(w + (rows * 4 + 255) / 256 * 256 + (rows * splits * 4 + 255) / 256 * 256);
+    unsigned long long* slots = static_cast<unsigned long long*>(ws);
     const T* xt = static_cast<const T*>(x);
     const bool vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (stride * (int64_t)sizeof(T)) % 16 == 0;
     const dim3 grid((unsigned)splits, (unsigned)rows);
-    if (vec)
-        return launch_chained(argmax_rows_kernel<T, true>, grid, dim3(256), 0, s, xt, cols, stride, per, part_v,
-                              part_i, tickets, out);
-    return launch_chained(argmax_rows_kernel<T, false>, grid, dim3(256), 0, s, xt, cols, stride, per, part_v, part_i,
-                          tickets, out);
+    cudaError_t err = vec ? launch_chained(argmax_rows_kernel<T, true>, grid, dim3(256), 0, s, xt, cols, stride, per,
+                                           slots)
+                          : launch_chained(argmax_rows_kernel<T, false>, grid, dim3(256), 0, s, xt, cols, stride, per,
+                                           slots);
+    if (err != cudaSuccess) return err;
+    const unsigned blocks = (unsigned)std::min<int64_t>((rows + 7) / 8, (int64_t)sms * 4);  // 8 rows (warps) per CTA
+    return launch_chained(argmax_keys_kernel, dim3(blocks), dim3(256), 0, s, slots, out, rows, splits * 8);
 }
 
 static cudaError_t launch_argmax(int dtype, const void* x, int64_t rows, int64_t cols, int64_t stride, void* ws,

@@ -157,8 +157,8 @@ def greedy_ids(logits: torch.Tensor) -> torch.Tensor:
 
     The reference samples greedily with ``logits.argmax(dim=-1)`` (``mini_engine/sampling.py:14-22``):
     a NaN counts as the largest value and ties take the lowest index.  ``minikv_argmax_rows``
-    computes the same in one launch.  Its ticket counters live in a zero-filled buffer kept per
-    CUDA stream (left zero by every call; never freed, since a captured graph may use it).
+    computes the same in two chained launches.  Its scratch (one key per warp of a row's column
+    slices) is a buffer kept per CUDA stream (never freed, since a captured graph may use it).
     """
     if logits.ndim != 2 or not logits.is_cuda or logits.stride(1) != 1:
         raise ValueError("logits must be a 2D CUDA tensor with contiguous rows")
