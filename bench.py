@@ -1047,12 +1047,12 @@ def run_qwen3(args, world, rank, local):
                           "decode_share": cfg.num_hidden_layers * launch_ms / ms_per_step},
         "e2e": {"value": args.batch / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-        "gpu_launches": ((5 * cfg.num_hidden_layers + 3) if fused else (5 * cfg.num_hidden_layers + 2)) * args.steps,
+        "gpu_launches": ((5 * cfg.num_hidden_layers + 4) if fused else (5 * cfg.num_hidden_layers + 3)) * args.steps,
         "gpu_launches_note": ("libminikv kernels only: per layer the q|k|v, o, gate|up and down projections "
                               "(tcgen05, element-wise steps fused) and the paged decode, plus the first and the "
-                              "final RMSNorm and the greedy argmax; the LM head is cuBLAS" if fused else
+                              "final RMSNorm and the greedy argmax (two launches); the LM head is cuBLAS" if fused else
                               "libminikv kernels only (RMSNorm x2, qk-norm+RoPE+append, paged decode, SiLU*up per "
-                              "layer, plus the first RMSNorm and the greedy argmax); the 4 projections per layer "
+                              "layer, plus the first RMSNorm and the greedy argmax, two launches); the 4 projections per layer "
                               "and the LM head are cuBLAS"),
         "projections": "fused tcgen05" if fused else "cublas",
         "clocks": clocks.summary(),
