@@ -62,6 +62,7 @@ struct PrefillTcParams {
     int tm;        // query tokens per tile = 128 / group
     int box_rows;  // rows per K/V TMA box (divides block_size and 128, >= 8)
     float scale_log2;
+    float out_scale;  // multiplies the output (an FP8 pool's value scale; 1 otherwise)
 };
 
 // 2^x on the special-function unit (ex2.approx, flush to zero); 2^-inf = 0.
@@ -599,7 +600,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                 tc_fence_after();
             }
             // every lane of the warp loads (warp-wide tcgen05.ld); rows past the chunk store nothing
-            const float inv = (row_valid && l_row > 0.f) ? 1.f / l_row : 0.f;
+            const float inv = (row_valid && l_row > 0.f) ? p.out_scale / l_row : 0.f;
             T* orow = static_cast<T*>(p.out) + ((w.q0 + t) * p.q_heads + w.h * G + g) * D + half * kHalfD;
 #pragma unroll
             for (int cc = 0; cc < kHalfD / 32; ++cc) {
@@ -674,7 +675,7 @@ static int run_prefill_tc(const void* q, const void* key_cache, const void* valu
                           const int64_t* query_starts, const int64_t* block_tables, const int64_t* context_lens,
                           void* out, int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
                           int64_t head_dim, int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype,
-                          cudaStream_t stream) {
+                          cudaStream_t stream, double k_scale = 1.0, float v_scale = 1.f) {
     const bool bf16 = dtype == MINIKV_BF16;
     const int group = (int)(q_heads / kv_heads);
     const int tm = 128 / group;
@@ -699,7 +700,8 @@ static int run_prefill_tc(const void* q, const void* key_cache, const void* valu
     p.table_width = (int)table_width;
     p.tm = tm;
     p.box_rows = box_rows;
-    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim));
+    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim) * k_scale);
+    p.out_scale = v_scale;
     // persistent grid: one CTA per SM, or fewer when the batch has fewer work items
     // (an upper bound: query tiles <= tokens / tm + requests, times the kv heads)
     const int64_t items_bound = ((tokens + tm - 1) / tm + requests) * kv_heads;

@@ -230,9 +230,14 @@ def paged_prefill_attention_fp8(q, key_cache, value_cache, cu_seqlens_q, query_s
 
     Arguments, checks and messages as ``paged_prefill_attention``
     (``mini_engine/kernels/prefill.py:61-131``), plus the pools' scales and
-    format.  ``q`` is fp16 or bf16 ``[tokens, q_heads, head_dim]``.  Each query
-    token runs as one row of the fp8 split-KV decode kernel (the CUDA-core
-    route); Q is rounded to fp16 for the products.
+    format.  ``q`` is fp16 or bf16 ``[tokens, q_heads, head_dim]``.  Shapes
+    the tcgen05 prefill takes (head_dim 64 or 128, GQA group dividing 128,
+    block_size a multiple of 8) run on a dense ``q.dtype`` copy of the pages
+    the tables reference (codes converted exactly), with the key scale folded
+    into the softmax scale and the value scale into the output.  Other shapes,
+    and batches whose copy would pass 8 GiB, run each query token as one row of
+    the fp8 split-KV decode kernel (the CUDA-core route; Q rounded to fp16 for
+    the products).
     """
     if backend != "cuda":
         raise ValueError("paged prefill backend must be cuda (this package has no torch/CPU path)")

@@ -259,14 +259,14 @@ def test_ragged_prefill_over_fp8_pool_matches_oracle(cuda_device, fmt):
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16])
 def test_ragged_prefill_over_fp8_pool_in_several_chunks(cuda_device, dtype):
     """More packed tokens than one launch chunk of the CUDA-core route (4096 query rows): the chunk
-    loop (ticket reset per chunk, q/out offsets, a shorter last chunk) over a small-head model,
-    fp16 and bf16 queries, both formats."""
+    loop (ticket reset per chunk, q/out offsets, a shorter last chunk) over a small-head model
+    (head_dim 96, which the tensor-core route does not take), fp16 and bf16 queries, both formats."""
     from myvllm_mini_engine_b200.engine import PrefillBatch
     from myvllm_mini_engine_b200.kernels import paged_prefill_attention_fp8
     from oracle import prefill as prefill_oracle
 
     gen = np.random.default_rng(61)
-    bs, heads, kv_heads, dim = 16, 2, 1, 64
+    bs, heads, kv_heads, dim = 16, 2, 1, 96
     starts = [0, 48, 3, 200]
     chunks = [2500, 1800, 700, 1333]  # 6333 packed tokens: two chunks of the route
     pages = [(s + n + bs - 1) // bs for s, n in zip(starts, chunks)]
@@ -290,4 +290,56 @@ def test_ragged_prefill_over_fp8_pool_in_several_chunks(cuda_device, dtype):
                                                      bs)
         assert out.dtype == dtype and out.shape == q.shape
         assert_close(out, expected, dtype)
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("dtype,fmt,dim,heads,kv_heads,bs", [
+    (torch.float16, "e4m3", 64, 8, 2, 16),
+    (torch.bfloat16, "e5m2", 128, 16, 16, 32),
+    (torch.bfloat16, "e4m3", 64, 4, 1, 8),
+])
+def test_ragged_prefill_over_fp8_pool_tensor_core_route(cuda_device, dtype, fmt, dim, heads, kv_heads, bs):
+    """The dense-copy tensor-core route: ragged chunks over prefixes, a request with no prefix,
+    a one-token chunk, a shared prefix page, table entries past the context holding garbage page
+    ids (never converted, masked), and an exact repeat (the copy is rebuilt each call)."""
+    from myvllm_mini_engine_b200.engine import PrefillBatch
+    from myvllm_mini_engine_b200.kernels import paged_prefill_attention_fp8
+    from oracle import prefill as prefill_oracle
+
+    gen = np.random.default_rng(dim + heads + bs)
+    starts = [0, 37, 2 * bs, 5]
+    chunks = [150, 61, 1, 200]
+    pages = [(s + n + bs - 1) // bs for s, n in zip(starts, chunks)]
+    blocks = sum(pages) + 4
+    perm = gen.permutation(blocks).tolist()
+    tables, at = [], 0
+    for n in pages:
+        tables.append(perm[at:at + n])
+        at += n
+    tables[2][0] = tables[1][0]  # shared prefix page
+    tokens = [gen.integers(0, 1000, size=n).tolist() for n in chunks]
+    batch = PrefillBatch.from_sequences(tokens, tables, starts, block_size=bs, num_blocks=blocks, device="cuda")
+    bt = batch.block_tables.clone()
+    lens = batch.context_lens.cpu().tolist()
+    for b in range(bt.shape[0]):  # entries past the context: out-of-range and in-range ids alike
+        used = (lens[b] + bs - 1) // bs
+        for j in range(used, bt.shape[1]):
+            bt[b, j] = blocks + 7 if (j % 2) else perm[j % blocks]
+    q = torch.from_numpy(gen.standard_normal((sum(chunks), heads, dim), dtype=np.float32)).to(dtype)
+    cache = torch.from_numpy(gen.standard_normal((2, blocks, bs, kv_heads, dim), dtype=np.float32))
+    kq = torch.from_numpy(fp8_kv.quantize(cache[0], K_SCALE, fmt))
+    vq = torch.from_numpy(fp8_kv.quantize(cache[1], V_SCALE, fmt))
+    meta = (batch.cu_seqlens_q, batch.query_starts, bt, batch.context_lens)
+    expected = prefill_oracle.paged_prefill_fp32(q.float(), fp8_kv.dequantize(kq, K_SCALE, fmt),
+                                                 fp8_kv.dequantize(vq, V_SCALE, fmt), *(t.cpu() for t in meta), bs)
+    first = None
+    for _ in range(2):
+        out = paged_prefill_attention_fp8(q.cuda(), kq.cuda(), vq.cuda(), *meta, bs, K_SCALE, V_SCALE,
+                                          kv_format=fmt, validate=False)
+        assert out.dtype == dtype and out.shape == q.shape
+        assert_close(out, expected, dtype)
+        if first is None:
+            first = out.clone()
+        else:
+            assert torch.equal(out, first)
     assert _lib.device_status() == 0
