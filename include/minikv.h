@@ -218,11 +218,14 @@ int minikv_paged_decode_fp8_append(const void* query, const void* key_cache, con
 /* Ragged causal paged prefill over an FP8 pool: minikv_paged_prefill's
  * contract (arguments, guards, packed [tokens, q_heads, head_dim] query and
  * output) with fp16/bf16 query/output (`dtype`), K/V read as code * scale.
- * Shapes the tensor-core prefill takes run it on a dense copy (in `dtype`)
- * of the table-referenced pages, made in the workspace by a conversion
- * kernel launched first; other shapes, and batches whose copy would pass
- * 8 GiB, run the CUDA-core route (one decode row per query token, fp8
- * consumer).  The workspace has its own size query (no zero fill needed). */
+ * Routes: head_dim 128 on the tensor-core prefill's shapes stages the codes
+ * with TMA and converts them to fp16 inside the kernel (fp16 MMAs; no
+ * workspace); the other tensor-core shapes run it on a dense copy (in
+ * `dtype`) of the table-referenced pages, made in the workspace by a
+ * conversion kernel launched first; other shapes, and batches whose copy
+ * would pass 8 GiB, run the CUDA-core route (one decode row per query token,
+ * fp8 consumer).  The workspace has its own size query (0 bytes: none is
+ * read; no zero fill needed). */
 int64_t minikv_paged_prefill_fp8_workspace_bytes(int64_t tokens, int64_t requests, int64_t q_heads,
                                                  int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
                                                  int64_t block_size, int64_t table_width, int64_t max_query_len,

@@ -482,8 +482,8 @@ int64_t minikv_paged_prefill_fp8_workspace_bytes(int64_t tokens, int64_t request
     if (check_prefill(tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width, dtype))
         return -1;
     if ((dtype != MINIKV_F16 && dtype != MINIKV_BF16) || !fp8_head_dim(head_dim)) return -1;
-    return prefill_fp8_workspace_bytes(tokens, requests, q_heads, kv_heads, head_dim, block_size, table_width, dtype,
-                                       sm_count());
+    return prefill_fp8_workspace_bytes(tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size,
+                                       table_width, dtype, sm_count());
 }
 
 int minikv_paged_prefill_fp8(const void* q, const void* key_cache, const void* value_cache,
@@ -510,10 +510,10 @@ int minikv_paged_prefill_fp8(const void* q, const void* key_cache, const void* v
                    MINIKV_EINVAL, "null pointer argument");
     MINIKV_REQUIRE(aligned16(q) && aligned16(key_cache) && aligned16(value_cache) && aligned16(out), MINIKV_EINVAL,
                    "paged prefill tensors must be 16-byte aligned");
-    const int64_t need = prefill_fp8_workspace_bytes(tokens, requests, q_heads, kv_heads, head_dim, block_size,
-                                                     table_width, dtype, sm_count());
+    const int64_t need = prefill_fp8_workspace_bytes(tokens, requests, q_heads, kv_heads, head_dim, num_blocks,
+                                                     block_size, table_width, dtype, sm_count());
     MINIKV_REQUIRE(need >= 0, MINIKV_EUNSUPPORTED, "paged prefill shape does not fit shared memory");
-    MINIKV_REQUIRE(workspace_bytes >= need && workspace && aligned16(workspace), MINIKV_EINVAL,
+    MINIKV_REQUIRE(workspace_bytes >= need && (need == 0 || (workspace && aligned16(workspace))), MINIKV_EINVAL,
                    "paged prefill workspace too small or misaligned");
     return run_prefill_fp8(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens, out,
                            workspace, tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size,

@@ -81,8 +81,14 @@ static int run_prefill(const void* q, const void* key_cache, const void* value_c
 }
 
 // ------------------------------------------------------------- FP8 pools
-// Tensor-core route over an FP8 pool.  The tcgen05 kernel stages 16-bit pages
-// with TMA, so dequant_table_pages_kernel first writes a dense 16-bit copy of
+// Three routes over an FP8 pool, the first that applies:
+//  1. head_dim 128 and the tcgen05 kernel's shapes: the kernel stages the
+//     pages' codes with TMA and converts them to fp16 in shared memory
+//     (prefill_tc.cu, F8 != 0); no workspace.
+//  2. the other tcgen05 shapes (head_dim 64): the dense copy below, then the
+//     16-bit kernel;
+//  3. the CUDA-core route (further below).
+// Route 2: dequant_table_pages_kernel first writes a dense 16-bit copy of
 // the pages the batch reads: table entry e = b * W + j becomes page e of the
 // copy, with the codes converted exactly (every E4M3 and E5M2 value is an fp16
 // and a bf16 value), and a remapped table holding e, or -1 where the entry is
@@ -202,10 +208,17 @@ static int run_prefill_fp8_tc(const void* q, const void* key_cache, const void* 
 // FP8 pool, CUDA-core route (shapes the tensor-core route does not take): the
 // split-KV decode with the fp8 consumer, one row per query token.  Same token
 // map, chunking and workspace layout as above; the decode plan is the fp8 pool's.
+static bool prefill_fp8_in_kernel(int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
+                                  int64_t head_dim, int64_t num_blocks, int64_t block_size, int dtype) {
+    return head_dim == 128 &&
+           prefill_tc_supported(q_heads, kv_heads, head_dim, block_size, dtype, num_blocks, tokens, requests);
+}
+
 static int64_t prefill_fp8_workspace_bytes(int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
-                                           int64_t head_dim, int64_t block_size, int64_t table_width, int dtype,
-                                           int sms) {
+                                           int64_t head_dim, int64_t num_blocks, int64_t block_size,
+                                           int64_t table_width, int dtype, int sms) {
     if (tokens <= 0) return 0;
+    if (prefill_fp8_in_kernel(tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, dtype)) return 0;
     const int64_t copy = prefill_fp8_copy_bytes(tokens, requests, q_heads, kv_heads, head_dim, block_size,
                                                 table_width, dtype);
     if (copy >= 0) return copy;
@@ -222,6 +235,10 @@ static int run_prefill_fp8(const void* q, const void* key_cache, const void* val
                            int64_t q_heads, int64_t kv_heads, int64_t head_dim, int64_t num_blocks,
                            int64_t block_size, int64_t table_width, float k_scale, float v_scale, bool e5m2,
                            int dtype, cudaStream_t stream) {
+    if (prefill_fp8_in_kernel(tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, dtype))
+        return run_prefill_tc(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens, out,
+                              tokens, requests, q_heads, kv_heads, head_dim, num_blocks, block_size, table_width,
+                              dtype, stream, (double)k_scale, v_scale, e5m2 ? 2 : 1);
     if (prefill_fp8_copy_bytes(tokens, requests, q_heads, kv_heads, head_dim, block_size, table_width, dtype) >= 0)
         return run_prefill_fp8_tc(q, key_cache, value_cache, cu_seqlens_q, query_starts, block_tables, context_lens,
                                   out, workspace, tokens, requests, q_heads, kv_heads, head_dim, num_blocks,

@@ -86,7 +86,7 @@ struct PfLayout {
     static constexpr int OFF_K = Q_BYTES;
     static constexpr int OFF_V = OFF_K + 2 * KV_BYTES;
     static constexpr int OFF_BAR = OFF_V + 2 * KV_BYTES;
-    static constexpr int OFF_RED = OFF_BAR + 256;          // [2][2][128] partial row maxima, [2][128] sums
+    static constexpr int OFF_RED = OFF_BAR + 512;          // [2][2][128] partial row maxima, [2][128] sums
     static constexpr int OFF_PFX = OFF_RED + 3 * 1024;      // [kPfMaxRequests + 1] query-tile prefix
     static constexpr int OFF_ORD = OFF_PFX + 4 * (kPfMaxRequests + 4);  // [kPfMaxSort] sorted query tiles
     static constexpr int SMEM = OFF_ORD + 8 * kPfMaxSort + 1024;        // + alignment slack
@@ -150,12 +150,74 @@ __device__ __forceinline__ int pf_nth_item(int k, int c, int G, int n_items) {
     return i < n_items ? i : -1;
 }
 
-template <typename T, int D>
+// FP8 pools (head_dim 128).  A key tile's codes (128 rows x 128 bytes, the
+// TMA's 128-byte swizzle: chunk c of row r at 16-byte position c ^ (r & 7))
+// land in the second K-block of a 16-bit ring slot; row r of that block is
+// exactly the bytes of code row r.  A lane converts whole rows: it reads all
+// eight chunks of row r, then writes dims 0..63 to row r of the first K-block
+// and dims 64..127 over the codes it has read, so the conversion runs in place.
+// E5M2 codes are the high bytes of their fp16 values; E4M3 codes are placed
+// as fp16 of 2^-8 times their value (exact, subnormals included), and the
+// factor 2^8 goes into the softmax scale (K) and the output scale (V).
+template <int F8>
+__device__ __forceinline__ void pf_convert_codes(unsigned char* slot, int lane) {
+    constexpr int kBlock = 128 * 128;
+#pragma unroll 1
+    for (int r = lane; r < kPfKeys; r += 32) {
+        const int sw = r & 7;
+        const unsigned char* src = slot + kBlock + r * 128;
+        uint4 in[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) in[c] = *reinterpret_cast<const uint4*>(src + ((c ^ sw) << 4));
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+            const uint32_t w[4] = {in[c].x, in[c].y, in[c].z, in[c].w};
+            uint32_t h[8];  // dims 16c .. 16c + 15 as fp16 pairs
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t lo = byte_perm(w[i], 0u, 0x1404u), hi = byte_perm(w[i], 0u, 0x3424u);
+                h[2 * i] = F8 == 1 ? e4m3x2_to_h2_scaled(lo) : lo;
+                h[2 * i + 1] = F8 == 1 ? e4m3x2_to_h2_scaled(hi) : hi;
+            }
+            unsigned char* dst = slot + (c >> 2) * kBlock + r * 128;
+            const int k0 = (2 * c) & 7;
+            *reinterpret_cast<uint4*>(dst + ((k0 ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<uint4*>(dst + (((k0 + 1) ^ sw) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+        }
+    }
+}
+
+// fp16 pair (saturated to the finite range) of a bf16 pair.
+__device__ __forceinline__ uint32_t bf16x2_to_h2_sat(uint32_t w) {
+    uint32_t h;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(__uint_as_float(w & 0xffff0000u)),
+        "f"(__uint_as_float(w << 16)));
+    return h;
+}
+
+// Half `part` (0 or 1) of a bf16 query tile converted in place to fp16, for the
+// fp16 MMAs over FP8 pools (the K and V producer warps take one half each).
+__device__ __forceinline__ void pf_convert_q_bf16(unsigned char* sq, int bytes, int part, int lane) {
+    uint4* q4 = reinterpret_cast<uint4*>(sq) + part * (bytes / 32);
+#pragma unroll 4
+    for (int i = lane; i < bytes / 32; i += 32) {
+        const uint4 v = q4[i];
+        q4[i] = make_uint4(bf16x2_to_h2_sat(v.x), bf16x2_to_h2_sat(v.y), bf16x2_to_h2_sat(v.z), bf16x2_to_h2_sat(v.w));
+    }
+}
+
+template <typename T, int D, int F8 = 0>
 __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
     const __grid_constant__ CUtensorMap tm_v, const PrefillTcParams p) {
     using L = PfLayout<T, D>;
     constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
+    // F8 = 1 (E4M3) or 2 (E5M2): K/V come from an FP8 pool through pf_convert_codes, and
+    // the MMAs run in fp16 (a bf16 query tile is converted once per item)
+    static_assert(F8 == 0 || D == 128, "FP8 pages are staged for head_dim 128 only");
+    using C = typename std::conditional<F8 != 0, __half, T>::type;  // MMA operand type
+    constexpr bool kMmaBf16 = F8 == 0 && kBf16;
+    constexpr bool kConvertQ = F8 != 0 && kBf16;
     extern __shared__ unsigned char smem_raw[];
     unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* sQ = smem;
@@ -185,6 +247,9 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     // still in the previous item's epilogue, reach that tile, and a parity wait two phases behind
     // never returns; S(g + 2) waits for the softmax of tile g, so this barrier stays within one phase.
     uint64_t* bits_full = bar + 29;
+    uint64_t* k8_full = bar + 32;  // [2] FP8 pools: the codes of a K tile landed (k_full: converted)
+    uint64_t* v8_full = bar + 34;  // [2] the same for V
+    uint64_t* q_ready = bar + 36;  // FP8 pools, bf16 query: both halves of Q converted to fp16
     int* qt_pfx = reinterpret_cast<int*>(smem + L::OFF_PFX);         // [requests + 1]
     uint32_t* order = reinterpret_cast<uint32_t*>(smem + L::OFF_ORD);  // [kPfMaxSort] sorted keys, then the keys
 
@@ -235,6 +300,11 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
         mbar_init(mma_drain, 1);
         mbar_init(&bits_full[0], 1);
         mbar_init(&bits_full[1], 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&k8_full[s], 1);
+            mbar_init(&v8_full[s], 1);
+        }
+        mbar_init(q_ready, 2);  // the two producer warps, one half of Q each
         mbar_init_fence();
     }
     if (warp == 1) {
@@ -272,116 +342,247 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
     const int c = blockIdx.x, nC = gridDim.x;
 
     if (warp == 0 || warp == kPfVWarp) {
-        // ------------------------------------------------------------ TMA producers
-        // Warp 0 loads Q and K, warp 10 loads V, each on its own ring of two
-        // slots, so a K slot is refilled as soon as the S MMA has read it,
-        // whatever the P V MMAs are doing (two warps, because a warp that ran
-        // both rings would reconverge after every wait).  Lane l owns box l
-        // (R keys on one page) of a tile; its page id is read one tile ahead.
-        const bool is_v = warp == kPfVWarp;
-        const int box = lane;
-        const unsigned full_mask = 0xffffffffu;
-        const int R = p.box_rows, groups = kPfKeys / R;  // groups <= 16
-        uint64_t* full = is_v ? v_full : k_full;
-        uint64_t* empty = is_v ? v_empty : k_empty;
-        const CUtensorMap* map = is_v ? &tm_v : &tm_k;
-        unsigned char* ring = is_v ? sV : sK;
-        const uint64_t space_limit = space_wait_limit();
-        int gt = 0, active = 0;  // key tiles issued, items whose Q was issued
-        bool stopped = false;    // a space wait gave up: issue nothing more, drain, exit
-        for (int k = 0; !stopped; ++k) {
-            const int it = pf_nth_item(k, c, nC, n_items);
-            if (it < 0) break;
-            const PfItem w = pf_item(p, qt_pfx, order, sorted, it, Hkv);
-            if (w.n_tiles == 0) continue;
-            if (!is_v) {
-                int q_ok = 1;
-                if (lane == 0) {
-                    if (active > 0) q_ok = mbar_wait_space(q_empty, (active - 1) & 1, space_limit) ? 1 : 0;
-                    if (q_ok) {
-                        mbar_arrive_expect_tx(q_full, (uint32_t)L::Q_BYTES);
-#pragma unroll
-                        for (int kb = 0; kb < L::KB; ++kb)
-                            tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, w.h * G, (int)(w.q0 + w.t_lo),
-                                        q_full);
-                    }
-                }
-                if (!__shfl_sync(full_mask, q_ok, 0)) break;
-            }
-            // Page-table entry of this lane's box of tile j (-1: no box).  The entry of
-            // tile j + 2 is loaded while tile j is issued and checked an iteration
-            // later, so the table load never stalls the issue of a tile.
-            auto raw_page = [&](int j) -> int64_t {
-                const int64_t k0 = (int64_t)j * kPfKeys + box * R;
-                if (box >= groups || j >= w.n_tiles || k0 >= w.limit) return -1;
-                return w.table[k0 / p.block_size];
+        if constexpr (F8 != 0) {
+            // -------------------------------------------------------- FP8 producers
+            // As below, with a tile's codes (one box of R rows x 128 bytes per page)
+            // landing on k8_full / v8_full; the warp converts tile g after issuing the
+            // loads of tile g + 1, then releases k_full / v_full.  The K warp converts
+            // the last tile of an item before it waits to replace Q (the item's last S
+            // needs it).  A bf16 Q is converted by both warps (one half each) after the
+            // loads of the item's first key tile; the V warp's wait on Q's landing
+            // cannot run ahead of the K warp's, as the V warp's first tile of item i + 1
+            // waits for P V of item i, which needs the S of item i (and so its Q).
+            const bool is_v = warp == kPfVWarp;
+            const int box = lane;
+            const unsigned full_mask = 0xffffffffu;
+            const int R = p.box_rows, groups = kPfKeys / R;
+            uint64_t* full = is_v ? v_full : k_full;
+            uint64_t* land = is_v ? v8_full : k8_full;
+            uint64_t* empty = is_v ? v_empty : k_empty;
+            const CUtensorMap* map = is_v ? &tm_v : &tm_k;
+            unsigned char* ring = is_v ? sV : sK;
+            const uint64_t space_limit = space_wait_limit();
+            int gt = 0, active = 0, pending = -1;
+            bool stopped = false;
+            auto convert = [&](int g) {
+                const int slot = g & 1;
+                // a landing that timed out (status bit set) is not read; the arrival still happens
+                if (__all_sync(full_mask, mbar_wait(&land[slot], (g >> 1) & 1)))
+                    pf_convert_codes<F8>(ring + slot * L::KV_BYTES, lane);
+                fence_async_smem();
+                tc_fence_before();
+                __syncwarp(full_mask);
+                if (lane == 0) mbar_arrive(&full[slot]);
             };
-            auto checked = [&](int64_t page) -> int64_t {
-                return (page >= 0 && page < p.num_blocks) ? page : -1;
-            };
-            int64_t page = checked(raw_page(0));
-            int64_t next_raw = raw_page(1);
-            for (int j = 0; j < w.n_tiles; ++j, ++gt) {
-                const int slot = gt & 1;
-                const int64_t key0 = (int64_t)j * kPfKeys;
-                const bool valid = page >= 0;
-                uint32_t words[4] = {0u, 0u, 0u, 0u};
+            for (int k = 0; !stopped; ++k) {
+                const int it = pf_nth_item(k, c, nC, n_items);
+                if (it < 0) break;
+                const PfItem w = pf_item(p, qt_pfx, order, sorted, it, Hkv);
+                if (w.n_tiles == 0) continue;
                 if (!is_v) {
-                    // validity bits of the tile's keys: a key is valid when its box is and it is < limit
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        uint32_t bits = 0;
-                        if (valid) {
-                            const int64_t lo = max((int64_t)q * 32, (int64_t)box * R);
-                            const int64_t hi = min(min((int64_t)q * 32 + 32, (int64_t)box * R + R), w.limit - key0);
-                            if (hi > lo) {
-                                const int n = (int)(hi - lo);
-                                bits = (n == 32 ? 0xffffffffu : ((1u << n) - 1u)) << (int)(lo - q * 32);
-                            }
-                        }
-                        words[q] = __reduce_or_sync(full_mask, bits);
+                    if (pending >= 0) {
+                        convert(pending);
+                        pending = -1;
                     }
+                    int q_ok = 1;
+                    if (lane == 0) {
+                        if (active > 0) q_ok = mbar_wait_space(q_empty, (active - 1) & 1, space_limit) ? 1 : 0;
+                        if (q_ok) {
+                            mbar_arrive_expect_tx(q_full, (uint32_t)L::Q_BYTES);
+#pragma unroll
+                            for (int kb = 0; kb < L::KB; ++kb)
+                                tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, w.h * G, (int)(w.q0 + w.t_lo),
+                                            q_full);
+                        }
+                    }
+                    if (!__shfl_sync(full_mask, q_ok, 0)) break;
                 }
-                const uint32_t bytes = (uint32_t)__popc(__ballot_sync(full_mask, valid)) * L::KB * R * 128;
-                if (gt >= 2 && !__all_sync(full_mask, mbar_wait_space(&empty[slot], ((gt >> 1) - 1) & 1, space_limit))) {
-                    stopped = true;  // the MMAs may still read this slot
-                    break;
-                }
-                if (box == 0) {
+                auto raw_page = [&](int j) -> int64_t {
+                    const int64_t k0 = (int64_t)j * kPfKeys + box * R;
+                    if (box >= groups || j >= w.n_tiles || k0 >= w.limit) return -1;
+                    return w.table[k0 / p.block_size];
+                };
+                auto checked = [&](int64_t page) -> int64_t {
+                    return (page >= 0 && page < p.num_blocks) ? page : -1;
+                };
+                int64_t page = checked(raw_page(0));
+                int64_t next_raw = raw_page(1);
+                for (int j = 0; j < w.n_tiles; ++j, ++gt) {
+                    const int slot = gt & 1;
+                    const int64_t key0 = (int64_t)j * kPfKeys;
+                    const bool valid = page >= 0;
+                    uint32_t words[4] = {0u, 0u, 0u, 0u};
                     if (!is_v) {
 #pragma unroll
-                        for (int q = 0; q < 4; ++q) key_ok[4 * (gt & 3) + q] = words[q];
+                        for (int q = 0; q < 4; ++q) {
+                            uint32_t bits = 0;
+                            if (valid) {
+                                const int64_t lo = max((int64_t)q * 32, (int64_t)box * R);
+                                const int64_t hi =
+                                    min(min((int64_t)q * 32 + 32, (int64_t)box * R + R), w.limit - key0);
+                                if (hi > lo) {
+                                    const int n = (int)(hi - lo);
+                                    bits = (n == 32 ? 0xffffffffu : ((1u << n) - 1u)) << (int)(lo - q * 32);
+                                }
+                            }
+                            words[q] = __reduce_or_sync(full_mask, bits);
+                        }
                     }
-                    mbar_arrive_expect_tx(&full[slot], bytes);
-                }
-                __syncwarp(full_mask);
-                if (valid) {
-                    const int z = (int)(page * p.block_size + (key0 + box * R) % p.block_size);
-                    unsigned char* dst = ring + slot * L::KV_BYTES + box * R * 128;
+                    const uint32_t bytes = (uint32_t)__popc(__ballot_sync(full_mask, valid)) * R * 128;
+                    if (gt >= 2 &&
+                        !__all_sync(full_mask, mbar_wait_space(&empty[slot], ((gt >> 1) - 1) & 1, space_limit))) {
+                        stopped = true;
+                        break;
+                    }
+                    if (box == 0) {
+                        if (!is_v) {
 #pragma unroll
-                    for (int kb = 0; kb < L::KB; ++kb)
-                        tma_load_3d(dst + kb * L::BLOCK_BYTES, map, kb * 64, w.h, z, &full[slot]);
+                            for (int q = 0; q < 4; ++q) key_ok[4 * (gt & 3) + q] = words[q];
+                        }
+                        mbar_arrive_expect_tx(&land[slot], bytes);
+                    }
+                    __syncwarp(full_mask);
+                    if (valid) {
+                        const int z = (int)(page * p.block_size + (key0 + box * R) % p.block_size);
+                        tma_load_3d(ring + slot * L::KV_BYTES + L::BLOCK_BYTES + box * R * 128, map, 0, w.h, z,
+                                    &land[slot]);
+                    }
+                    // (the V warp's previous tile first: the previous item's last P V needs it,
+                    // and this item's Q may land much later)
+                    if (pending >= 0) convert(pending);
+                    pending = gt;
+                    if (kConvertQ && j == 0) {
+                        if (__all_sync(full_mask, mbar_wait(q_full, active & 1)))
+                            pf_convert_q_bf16(sQ, L::Q_BYTES, is_v ? 1 : 0, lane);
+                        fence_async_smem();
+                        tc_fence_before();
+                        __syncwarp(full_mask);
+                        if (lane == 0) mbar_arrive(q_ready);
+                    }
+                    page = checked(next_raw);
+                    next_raw = raw_page(j + 2);
                 }
-                page = checked(next_raw);
-                next_raw = raw_page(j + 2);
+                ++active;
             }
-            ++active;
+            if (!stopped && pending >= 0) convert(pending);
+            // Drain: every code tile issued (and Q) has landed before this warp exits.
+            if (lane == 0) {
+                for (int s2 = 0; s2 < 2 && s2 < gt; ++s2) mbar_drain(&land[s2], ((s2 + 2 * ((gt - 1 - s2) / 2)) >> 1) & 1);
+                if (!is_v && active > 0) mbar_drain(q_full, (active - 1) & 1);
+            }
+            __syncwarp();
+        } else {
+            // -------------------------------------------------------- TMA producers
+            // Warp 0 loads Q and K, warp 10 loads V, each on its own ring of two
+            // slots, so a K slot is refilled as soon as the S MMA has read it,
+            // whatever the P V MMAs are doing (two warps, because a warp that ran
+            // both rings would reconverge after every wait).  Lane l owns box l
+            // (R keys on one page) of a tile; its page id is read one tile ahead.
+            const bool is_v = warp == kPfVWarp;
+            const int box = lane;
+            const unsigned full_mask = 0xffffffffu;
+            const int R = p.box_rows, groups = kPfKeys / R;  // groups <= 16
+            uint64_t* full = is_v ? v_full : k_full;
+            uint64_t* empty = is_v ? v_empty : k_empty;
+            const CUtensorMap* map = is_v ? &tm_v : &tm_k;
+            unsigned char* ring = is_v ? sV : sK;
+            const uint64_t space_limit = space_wait_limit();
+            int gt = 0, active = 0;  // key tiles issued, items whose Q was issued
+            bool stopped = false;    // a space wait gave up: issue nothing more, drain, exit
+            for (int k = 0; !stopped; ++k) {
+                const int it = pf_nth_item(k, c, nC, n_items);
+                if (it < 0) break;
+                const PfItem w = pf_item(p, qt_pfx, order, sorted, it, Hkv);
+                if (w.n_tiles == 0) continue;
+                if (!is_v) {
+                    int q_ok = 1;
+                    if (lane == 0) {
+                        if (active > 0) q_ok = mbar_wait_space(q_empty, (active - 1) & 1, space_limit) ? 1 : 0;
+                        if (q_ok) {
+                            mbar_arrive_expect_tx(q_full, (uint32_t)L::Q_BYTES);
+#pragma unroll
+                            for (int kb = 0; kb < L::KB; ++kb)
+                                tma_load_3d(sQ + kb * L::BLOCK_BYTES, &tm_q, kb * 64, w.h * G, (int)(w.q0 + w.t_lo),
+                                            q_full);
+                        }
+                    }
+                    if (!__shfl_sync(full_mask, q_ok, 0)) break;
+                }
+                // Page-table entry of this lane's box of tile j (-1: no box).  The entry of
+                // tile j + 2 is loaded while tile j is issued and checked an iteration
+                // later, so the table load never stalls the issue of a tile.
+                auto raw_page = [&](int j) -> int64_t {
+                    const int64_t k0 = (int64_t)j * kPfKeys + box * R;
+                    if (box >= groups || j >= w.n_tiles || k0 >= w.limit) return -1;
+                    return w.table[k0 / p.block_size];
+                };
+                auto checked = [&](int64_t page) -> int64_t {
+                    return (page >= 0 && page < p.num_blocks) ? page : -1;
+                };
+                int64_t page = checked(raw_page(0));
+                int64_t next_raw = raw_page(1);
+                for (int j = 0; j < w.n_tiles; ++j, ++gt) {
+                    const int slot = gt & 1;
+                    const int64_t key0 = (int64_t)j * kPfKeys;
+                    const bool valid = page >= 0;
+                    uint32_t words[4] = {0u, 0u, 0u, 0u};
+                    if (!is_v) {
+                        // validity bits of the tile's keys: a key is valid when its box is and it is < limit
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            uint32_t bits = 0;
+                            if (valid) {
+                                const int64_t lo = max((int64_t)q * 32, (int64_t)box * R);
+                                const int64_t hi = min(min((int64_t)q * 32 + 32, (int64_t)box * R + R), w.limit - key0);
+                                if (hi > lo) {
+                                    const int n = (int)(hi - lo);
+                                    bits = (n == 32 ? 0xffffffffu : ((1u << n) - 1u)) << (int)(lo - q * 32);
+                                }
+                            }
+                            words[q] = __reduce_or_sync(full_mask, bits);
+                        }
+                    }
+                    const uint32_t bytes = (uint32_t)__popc(__ballot_sync(full_mask, valid)) * L::KB * R * 128;
+                    if (gt >= 2 && !__all_sync(full_mask, mbar_wait_space(&empty[slot], ((gt >> 1) - 1) & 1, space_limit))) {
+                        stopped = true;  // the MMAs may still read this slot
+                        break;
+                    }
+                    if (box == 0) {
+                        if (!is_v) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) key_ok[4 * (gt & 3) + q] = words[q];
+                        }
+                        mbar_arrive_expect_tx(&full[slot], bytes);
+                    }
+                    __syncwarp(full_mask);
+                    if (valid) {
+                        const int z = (int)(page * p.block_size + (key0 + box * R) % p.block_size);
+                        unsigned char* dst = ring + slot * L::KV_BYTES + box * R * 128;
+#pragma unroll
+                        for (int kb = 0; kb < L::KB; ++kb)
+                            tma_load_3d(dst + kb * L::BLOCK_BYTES, map, kb * 64, w.h, z, &full[slot]);
+                    }
+                    page = checked(next_raw);
+                    next_raw = raw_page(j + 2);
+                }
+                ++active;
+            }
+            // Drain: the last phase issued into each slot (and Q's) has landed before this
+            // warp exits, so no TMA copy is in flight when the CTA releases its shared memory.
+            if (lane == 0) {
+                for (int s2 = 0; s2 < 2 && s2 < gt; ++s2) mbar_drain(&full[s2], ((s2 + 2 * ((gt - 1 - s2) / 2)) >> 1) & 1);
+                if (!is_v && active > 0) mbar_drain(q_full, (active - 1) & 1);
+            }
+            __syncwarp();
         }
-        // Drain: the last phase issued into each slot (and Q's) has landed before this
-        // warp exits, so no TMA copy is in flight when the CTA releases its shared memory.
-        if (lane == 0) {
-            for (int s2 = 0; s2 < 2 && s2 < gt; ++s2) mbar_drain(&full[s2], ((s2 + 2 * ((gt - 1 - s2) / 2)) >> 1) & 1);
-            if (!is_v && active > 0) mbar_drain(q_full, (active - 1) & 1);
-        }
-        __syncwarp();
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         // S(j) and P V(j) are issued in whichever order their operands become
         // ready (non-blocking probes), so a late K tile never holds back a
         // P V product whose P is done, and S runs up to two tiles ahead.
         if (lane == 0) {
-            constexpr uint32_t idesc_s = umma_idesc(128, kPfKeys, kBf16, false);
-            constexpr uint32_t idesc_o = umma_idesc(128, D, kBf16, true);
+            constexpr uint32_t idesc_s = umma_idesc(128, kPfKeys, kMmaBf16, false);
+            constexpr uint32_t idesc_o = umma_idesc(128, D, kMmaBf16, true);
             const uint32_t t_o = tmem + 2 * kPfKeys;
             const uint32_t q_addr = smem_addr(sQ);
             int gt = 0, active = 0;
@@ -392,7 +593,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                 const PfItem w = pf_item(p, qt_pfx, order, sorted, it, Hkv);
                 const int n_tiles = w.n_tiles;
                 if (n_tiles == 0) continue;
-                mbar_wait(q_full, active & 1);
+                mbar_wait(kConvertQ ? q_ready : q_full, active & 1);
                 int ns = 0, npv = 0;  // next S and next P V of this item
                 uint64_t idle_since = 0;
                 while (npv < n_tiles) {
@@ -549,7 +750,7 @@ __global__ void __launch_bounds__(kPfThreads, 1) paged_prefill_tc_kernel(
                         pe[u] = (full || ((bits[kx >> 5] >> (kx & 31)) & 1u)) ? x : 0.f;
                         sums[kx & 3] += pe[u];
                     }
-                    packed[e / 2] = __uint_as_float(Elem<T>::pack(pe[0], pe[1]));
+                    packed[e / 2] = __uint_as_float(Elem<C>::pack(pe[0], pe[1]));
                 }
                 tmem_store_32(tmem + lane_base + slot * kPfKeys + half * 32, packed);
                 tmem_store_wait();
@@ -660,11 +861,11 @@ static bool prefill_tc_supported(int64_t q_heads, int64_t kv_heads, int64_t head
     return num_blocks * block_size < (1ll << 31) && tokens < (1ll << 31) && encode_tiled_fn() != nullptr;
 }
 
-template <typename T, int D>
+template <typename T, int D, int F8 = 0>
 static cudaError_t launch_prefill_tc_typed(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
                                            const PrefillTcParams& p, int grid, cudaStream_t stream) {
     using L = PfLayout<T, D>;
-    auto kernel = paged_prefill_tc_kernel<T, D>;
+    auto kernel = paged_prefill_tc_kernel<T, D, F8>;
     static int configured[64] = {0};  // opt-in shared-memory size, set once per device
     cudaError_t err = ensure_smem_limit(kernel, L::SMEM, configured);
     if (err != cudaSuccess) return err;
@@ -675,15 +876,21 @@ static int run_prefill_tc(const void* q, const void* key_cache, const void* valu
                           const int64_t* query_starts, const int64_t* block_tables, const int64_t* context_lens,
                           void* out, int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
                           int64_t head_dim, int64_t num_blocks, int64_t block_size, int64_t table_width, int dtype,
-                          cudaStream_t stream, double k_scale = 1.0, float v_scale = 1.f) {
+                          cudaStream_t stream, double k_scale = 1.0, float v_scale = 1.f, int f8 = 0) {
+    // f8: 0 = 16-bit pool; 1 / 2 = E4M3 / E5M2 pool (head_dim 128), codes converted in the kernel
+    if (f8 != 0 && head_dim != 128) return fail(MINIKV_EINVAL, "FP8 pages are staged for head_dim 128 only");
     const bool bf16 = dtype == MINIKV_BF16;
     const int group = (int)(q_heads / kv_heads);
     const int tm = 128 / group;
     const int box_rows = gcd_int((int)std::min<int64_t>(block_size, 1 << 20), 128);
     CUtensorMap mq, mk, mv;
     if (!encode_map_3d(&mq, q, bf16, head_dim, q_heads, tokens, 64, group, tm) ||
-        !encode_map_3d(&mk, key_cache, bf16, head_dim, kv_heads, num_blocks * block_size, 64, 1, box_rows) ||
-        !encode_map_3d(&mv, value_cache, bf16, head_dim, kv_heads, num_blocks * block_size, 64, 1, box_rows))
+        (f8 == 0 &&
+         (!encode_map_3d(&mk, key_cache, bf16, head_dim, kv_heads, num_blocks * block_size, 64, 1, box_rows) ||
+          !encode_map_3d(&mv, value_cache, bf16, head_dim, kv_heads, num_blocks * block_size, 64, 1, box_rows))) ||
+        (f8 != 0 &&
+         (!encode_map_3d_u8(&mk, key_cache, head_dim, kv_heads, num_blocks * block_size, 128, 1, box_rows) ||
+          !encode_map_3d_u8(&mv, value_cache, head_dim, kv_heads, num_blocks * block_size, 128, 1, box_rows))))
         return fail(MINIKV_ECUDA, "cuTensorMapEncodeTiled failed for the paged prefill operands");
     PrefillTcParams p{};
     p.cu_q = cu_seqlens_q;
@@ -700,15 +907,23 @@ static int run_prefill_tc(const void* q, const void* key_cache, const void* valu
     p.table_width = (int)table_width;
     p.tm = tm;
     p.box_rows = box_rows;
-    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim) * k_scale);
-    p.out_scale = v_scale;
+    const double code_scale = f8 == 1 ? 256.0 : 1.0;  // E4M3 codes are converted to 2^-8 x their value
+    p.scale_log2 = (float)(1.4426950408889634 / std::sqrt((double)head_dim) * k_scale * code_scale);
+    p.out_scale = (float)(v_scale * code_scale);
     // persistent grid: one CTA per SM, or fewer when the batch has fewer work items
     // (an upper bound: query tiles <= tokens / tm + requests, times the kv heads)
     const int64_t items_bound = ((tokens + tm - 1) / tm + requests) * kv_heads;
     if ((tokens + tm - 1) / tm + requests >= (1 << 20)) return fail(MINIKV_EINVAL, "too many paged prefill tiles");
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(items_bound, sm_count()));
     cudaError_t err;
-    if (bf16)
+    if (f8 != 0) {
+        if (bf16)
+            err = f8 == 1 ? launch_prefill_tc_typed<__nv_bfloat16, 128, 1>(mq, mk, mv, p, grid, stream)
+                          : launch_prefill_tc_typed<__nv_bfloat16, 128, 2>(mq, mk, mv, p, grid, stream);
+        else
+            err = f8 == 1 ? launch_prefill_tc_typed<__half, 128, 1>(mq, mk, mv, p, grid, stream)
+                          : launch_prefill_tc_typed<__half, 128, 2>(mq, mk, mv, p, grid, stream);
+    } else if (bf16)
         err = head_dim == 64 ? launch_prefill_tc_typed<__nv_bfloat16, 64>(mq, mk, mv, p, grid, stream)
                              : launch_prefill_tc_typed<__nv_bfloat16, 128>(mq, mk, mv, p, grid, stream);
     else

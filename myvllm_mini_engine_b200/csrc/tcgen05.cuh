@@ -232,6 +232,20 @@ static bool encode_map_3d(CUtensorMap* map, const void* base, bool bf16, uint64_
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The same over one-byte elements (FP8 codes as UINT8); b0 * 1 byte <= 128 for the swizzle.
+static bool encode_map_3d_u8(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0,
+                             uint32_t b1, uint32_t b2) {
+    EncodeTiledFn fn = encode_tiled_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[3] = {d0, d1, d2};
+    const cuuint64_t strides[2] = {d0, d0 * d1};
+    const cuuint32_t box[3] = {b0, b1, b2};
+    const cuuint32_t elem[3] = {1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, elem,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D map over [dim1][dim0] (dim0 innermost, elements of 2 bytes, rows `row_bytes`
 // apart), 128B swizzle; out-of-range rows and columns read as zeros.
 static bool encode_map_2d(CUtensorMap* map, const void* base, bool bf16, uint64_t d0, uint64_t d1,

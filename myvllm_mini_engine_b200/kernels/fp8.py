@@ -230,10 +230,12 @@ def paged_prefill_attention_fp8(q, key_cache, value_cache, cu_seqlens_q, query_s
 
     Arguments, checks and messages as ``paged_prefill_attention``
     (``mini_engine/kernels/prefill.py:61-131``), plus the pools' scales and
-    format.  ``q`` is fp16 or bf16 ``[tokens, q_heads, head_dim]``.  Shapes
-    the tcgen05 prefill takes (head_dim 64 or 128, GQA group dividing 128,
-    block_size a multiple of 8) run on a dense ``q.dtype`` copy of the pages
-    the tables reference (codes converted exactly), with the key scale folded
+    format.  ``q`` is fp16 or bf16 ``[tokens, q_heads, head_dim]``.  On the
+    tcgen05 prefill's shapes (GQA group dividing 128, block_size a multiple of
+    8): at head_dim 128 the kernel stages the codes with TMA and converts them
+    to fp16 in shared memory (a bf16 Q is rounded to fp16 for the products);
+    at head_dim 64 it runs on a dense ``q.dtype`` copy of the pages the tables
+    reference (codes converted exactly).  Either way the key scale is folded
     into the softmax scale and the value scale into the output.  Other shapes,
     and batches whose copy would pass 8 GiB, run each query token as one row of
     the fp8 split-KV decode kernel (the CUDA-core route; Q rounded to fp16 for
@@ -266,12 +268,12 @@ def paged_prefill_attention_fp8(q, key_cache, value_cache, cu_seqlens_q, query_s
                                                         block_size, width, bound, code)
     if need < 0:
         _lib.check(_lib.EINVAL, "paged_prefill_attention_fp8")
-    workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    workspace = torch.empty(need, dtype=torch.uint8, device=q.device) if need > 0 else None  # 0: not read
     with _lib.on_device(q.device):
         status = lib.minikv_paged_prefill_fp8(
             q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), cu_seqlens_q.data_ptr(),
             query_starts.data_ptr(), block_tables.data_ptr(), context_lens.data_ptr(), output.data_ptr(),
-            workspace.data_ptr(), workspace.numel(), tokens, requests, q.shape[1], kv_heads, dim, num_blocks,
+            workspace.data_ptr() if need > 0 else None, need, tokens, requests, q.shape[1], kv_heads, dim, num_blocks,
             block_size, width, bound, k_scale, v_scale, fmt, code, _lib.stream_of(q.device))
     _lib.check(status, "paged_prefill_attention_fp8")
     return output

@@ -294,12 +294,15 @@ def test_ragged_prefill_over_fp8_pool_in_several_chunks(cuda_device, dtype):
 
 
 @pytest.mark.parametrize("dtype,fmt,dim,heads,kv_heads,bs", [
-    (torch.float16, "e4m3", 64, 8, 2, 16),
-    (torch.bfloat16, "e5m2", 128, 16, 16, 32),
-    (torch.bfloat16, "e4m3", 64, 4, 1, 8),
+    (torch.float16, "e4m3", 64, 8, 2, 16),     # dense copy
+    (torch.bfloat16, "e4m3", 64, 4, 1, 8),     # dense copy
+    (torch.bfloat16, "e5m2", 128, 16, 16, 32),  # codes converted in the kernel, bf16 Q converted too
+    (torch.float16, "e4m3", 128, 8, 1, 8),      # in the kernel, fp16 Q, 8-row page boxes
+    (torch.bfloat16, "e4m3", 128, 32, 2, 256),  # in the kernel, 128-row page boxes
 ])
 def test_ragged_prefill_over_fp8_pool_tensor_core_route(cuda_device, dtype, fmt, dim, heads, kv_heads, bs):
-    """The dense-copy tensor-core route: ragged chunks over prefixes, a request with no prefix,
+    """Both tensor-core routes (head_dim 128: codes staged and converted inside the kernel; 64:
+    a dense 16-bit copy first): ragged chunks over prefixes, a request with no prefix,
     a one-token chunk, a shared prefix page, table entries past the context holding garbage page
     ids (never converted, masked), and an exact repeat (the copy is rebuilt each call)."""
     from myvllm_mini_engine_b200.engine import PrefillBatch
@@ -307,7 +310,7 @@ def test_ragged_prefill_over_fp8_pool_tensor_core_route(cuda_device, dtype, fmt,
     from oracle import prefill as prefill_oracle
 
     gen = np.random.default_rng(dim + heads + bs)
-    starts = [0, 37, 2 * bs, 5]
+    starts = [0, 2 * bs + 37, 2 * bs, 5]  # requests 1 and 2 share their first (prefix) page
     chunks = [150, 61, 1, 200]
     pages = [(s + n + bs - 1) // bs for s, n in zip(starts, chunks)]
     blocks = sum(pages) + 4
