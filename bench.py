@@ -76,8 +76,9 @@ def parse_args(argv=None):
                              "up to Qwen3DecodeStep.FUSED_MAX_BATCH (default), or cuBLAS projections around the "
                              "element-wise kernels")
     parser.add_argument("--kv-dtype", choices=("bf16", "fp8", "fp8_e5m2"), default="bf16",
-                        help="decode: the KV pool format; fp8 = E4M3 pool, fp8_e5m2 = E5M2 pool, with per-pool "
-                             "scales (fused quantising KV append + fp8 paged attention), device-timed only")
+                        help="decode / prefill: the KV pool format; fp8 = E4M3 pool, fp8_e5m2 = E5M2 pool, with "
+                             "per-pool scales (decode: fused quantising KV append + fp8 paged attention, "
+                             "device-timed only; prefill: config 4 with a quantising scatter and the fp8 prefill)")
     args = parser.parse_args(argv)
     if args.batch is None:
         args.batch = 32 if args.workload == "decode" else 256
@@ -1143,15 +1144,28 @@ def run_prefill_reference(args, world, rank):
 
 
 def run_prefill(args, world, rank, local):
+    """BASELINE config 4 as one step: copy-on-write, slot scatter, ragged prefill.  With
+    ``--kv-dtype fp8`` / ``fp8_e5m2`` the pool holds E4M3 / E5M2 codes: the CoW moves bytes, the
+    scatter quantises, and the prefill is ``paged_prefill_attention_fp8``."""
     from myvllm_mini_engine_b200 import _lib
     from myvllm_mini_engine_b200.engine import PrefillBatch
-    from myvllm_mini_engine_b200.kernels import copy_blocks, paged_prefill_attention, write_kv_cache_slots
+    from myvllm_mini_engine_b200.kernels import (copy_blocks, paged_prefill_attention, paged_prefill_attention_fp8,
+                                                 write_kv_cache_slots, write_kv_cache_slots_fp8)
 
     device = torch.device("cuda", local)
     c = config4_inputs(device)
     bs, chunk = c["block_size"], 128
     flops = prefill_flops(c["starts"], chunk)
+    fmt = {"fp8": "e4m3", "fp8_e5m2": "e5m2"}.get(args.kv_dtype)  # None: 16-bit pool
+    k_scale = v_scale = 4.5 / 448
     gk, gv = c["key_cache"].to(device), c["value_cache"].to(device)
+    if fmt is not None:
+        rows = gk.shape[0] * bs
+        kq, vq = (torch.empty(gk.shape, dtype=torch.uint8, device=device) for _ in range(2))
+        write_kv_cache_slots_fp8(kq, vq, torch.arange(rows, device=device), gk.view(rows, HKV, D),
+                                 gv.view(rows, HKV, D), k_scale, v_scale, kv_format=fmt, validate=False)
+        gk, gv = kq, vq
+    words = (lambda t: t.view(torch.float16)) if fmt is not None else (lambda t: t)  # CoW moves 16-bit words
     q, key, value = (c[k].to(device) for k in ("q", "key", "value"))
     pairs = torch.tensor([list(c["cow_pair"])], dtype=torch.int64, device=device)
     batch = PrefillBatch.from_sequences(c["tokens"], c["cow_tables"], c["starts"], block_size=bs,
@@ -1159,14 +1173,26 @@ def run_prefill(args, world, rank, local):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     events = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(3)]
 
+    def scatter(k_rows, v_rows):
+        if fmt is None:
+            write_kv_cache_slots(gk, gv, batch.slot_mapping, k_rows, v_rows, validate=False)
+        else:
+            write_kv_cache_slots_fp8(gk, gv, batch.slot_mapping, k_rows, v_rows, k_scale, v_scale, kv_format=fmt,
+                                     validate=False)
+
+    def attend(q_rows):
+        meta = (batch.cu_seqlens_q, batch.query_starts, batch.block_tables, batch.context_lens)
+        if fmt is None:
+            return paged_prefill_attention(q_rows, gk, gv, *meta, bs, validate=False, max_query_len=chunk)
+        return paged_prefill_attention_fp8(q_rows, gk, gv, *meta, bs, k_scale, v_scale, kv_format=fmt,
+                                           validate=False, max_query_len=chunk)
+
     def step(timed=False):
-        copy_blocks(gk.unsqueeze(0), gv.unsqueeze(0), pairs, validate=False)
-        write_kv_cache_slots(gk, gv, batch.slot_mapping, key, value, validate=False)
+        copy_blocks(words(gk).unsqueeze(0), words(gv).unsqueeze(0), pairs, validate=False)
+        scatter(key, value)
         if timed:
             events[1].record()
-        out = paged_prefill_attention(q, gk, gv, batch.cu_seqlens_q, batch.query_starts, batch.block_tables,
-                                      batch.context_lens, bs, validate=False, max_query_len=chunk)
-        return out
+        return attend(q)
 
     side = torch.cuda.Stream(device)
     side.wait_stream(torch.cuda.current_stream(device))
@@ -1210,12 +1236,9 @@ def run_prefill(args, world, rank, local):
     def e2e_step():
         for k, t in host.items():
             dev[k].copy_(t, non_blocking=True)
-        copy_blocks(gk.unsqueeze(0), gv.unsqueeze(0), pairs, validate=False)
-        write_kv_cache_slots(gk, gv, batch.slot_mapping, dev["key"], dev["value"], validate=False)
-        result = paged_prefill_attention(dev["q"], gk, gv, batch.cu_seqlens_q, batch.query_starts,
-                                         batch.block_tables, batch.context_lens, bs, validate=False,
-                                         max_query_len=chunk)
-        out_host.copy_(result, non_blocking=True)
+        copy_blocks(words(gk).unsqueeze(0), words(gv).unsqueeze(0), pairs, validate=False)
+        scatter(dev["key"], dev["value"])
+        out_host.copy_(attend(dev["q"]), non_blocking=True)
 
     for _ in range(3):
         e2e_step()
@@ -1237,14 +1260,22 @@ def run_prefill(args, world, rank, local):
         return None
     line = prefill_line_base(args, world)
     achieved = flops / (prefill_avg * 1e-3) / 1e12
-    kv_read = sum(min(len(t) * bs, s + chunk) for t, s in zip(c["cow_tables"], c["starts"])) * 2 * HKV * D * 2
+    kv_read = sum(min(len(t) * bs, s + chunk) for t, s in zip(c["cow_tables"], c["starts"])) * 2 * HKV * D * \
+        (1 if fmt is not None else 2)
+    if fmt is not None:
+        line["dtype"] = f"{fmt} KV codes, fp16 MMAs (fp32 accumulate)"
+        line["metric"] = PREFILL_METRIC.replace("ragged prefill", f"ragged prefill over an {fmt.upper()} pool")
+        line["config"]["workload"] = line["config"]["workload"].replace(
+            "bf16, block 16", f"bf16 query, {fmt.upper()} KV pool (per-pool scales), block 16")
     line.update({
         "value": world * flops / (step_avg * 1e-3) / 1e12, "ms_per_step": step_avg, "steps": steps,
         "prefill_tokens_s": world * 16 * chunk / (step_avg * 1e-3),
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
-                     "traffic": ncu_traffic("prefill_config4_bf16"),
-                     "kernel": "paged prefill (tcgen05 + TMEM, TMA page boxes) per launch",
+                     "traffic": ncu_traffic("prefill_config4_bf16" if fmt is None else f"prefill_config4_{fmt}"),
+                     "kernel": "paged prefill (tcgen05 + TMEM, TMA page boxes) per launch" if fmt is None else
+                               "paged prefill (tcgen05 + TMEM; FP8 page boxes converted to fp16 in shared memory) "
+                               "per launch",
                      "flops_per_launch": flops, "kv_bytes_per_launch": kv_read,
                      "launch_ms": prefill_avg},
         "e2e": {"value": world * flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
