@@ -75,3 +75,31 @@ def test_prefill_slot_wait_timeout_sets_status_and_exits_cleanly(short_space_wai
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
     assert torch.equal(again, good)
+
+
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_fp8_prefill_wait_timeout_sets_status_and_exits_cleanly(short_space_waits, fmt):
+    # The FP8 prefill's producers convert each tile in place before releasing it; with 100 ns their
+    # slot waits run out, and the tiles already issued must still land before the CTA exits.
+    from myvllm_mini_engine_b200.engine import PrefillBatch
+    from myvllm_mini_engine_b200.kernels import paged_prefill_attention_fp8
+    from oracle import fp8_kv
+
+    c = cases.config4()
+    bs = c["block_size"]
+    batch = PrefillBatch.from_sequences(c["tokens"], c["cow_tables"], c["starts"], block_size=bs,
+                                        num_blocks=c["num_blocks"], device="cuda")
+    kq = torch.from_numpy(fp8_kv.quantize(c["key_cache"], 0.03, fmt)).cuda()
+    vq = torch.from_numpy(fp8_kv.quantize(c["value_cache"], 0.03, fmt)).cuda()
+    args = (c["q"].cuda(), kq, vq, batch.cu_seqlens_q, batch.query_starts, batch.block_tables, batch.context_lens,
+            bs, 0.03, 0.03)
+    good = paged_prefill_attention_fp8(*args, kv_format=fmt, validate=False)
+    assert _lib.device_status() == 0
+    short_space_waits()
+    paged_prefill_attention_fp8(*args, kv_format=fmt, validate=False)
+    assert _lib.device_status() & 1, "the shortened waits must have run out"
+    _lib.set_wait_limit(_lib.DEFAULT_WAIT_LIMIT_NS)
+    again = paged_prefill_attention_fp8(*args, kv_format=fmt, validate=False)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    assert torch.equal(again, good)
