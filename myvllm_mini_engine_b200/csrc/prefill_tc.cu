@@ -33,6 +33,13 @@
 // epilogue are split two ways.  Because P stays in TMEM, the softmax of tile
 // j+1 runs while P_j V_j is on the tensor cores.  No TMA multicast.
 //
+// FP8 pools (template F8 = 1 E4M3, 2 E5M2; head_dim 128): the K and V boxes
+// carry one-byte codes (one 128-byte box per page and kv head instead of two),
+// land in the second K-block of a ring slot and are converted in place to
+// fp16 by the producer warp before it releases the slot; S and P V then run
+// in fp16 (a bf16 query tile is converted to fp16 in shared memory once per
+// item), with the pool's scales folded into the softmax scale and the output.
+//
 // Semantics follow the reference kernel (mini_engine/kernels/csrc/prefill.cu:
 // 104-185): row t of request r attends keys [0, start_r + t]; keys on a page
 // id outside [0, num_blocks) are masked; rows whose position falls outside
