@@ -346,3 +346,17 @@ def test_ragged_prefill_over_fp8_pool_tensor_core_route(cuda_device, dtype, fmt,
         else:
             assert torch.equal(out, first)
     assert _lib.device_status() == 0
+
+
+def test_fp8_prefill_workspace_follows_the_route(cuda_device):
+    """Config 4's shape: head_dim 128 stages the codes inside the tcgen05 kernel (no workspace);
+    head_dim 64 needs the dense 16-bit copy of every table entry's page (two pools + table);
+    head_dim 96 takes the CUDA-core route (token map + decode workspace)."""
+    lib = _lib.load()
+    code = _lib.dtype_code(torch.bfloat16)
+    tokens, requests, hq, hkv, blocks, bs, width = 2048, 16, 16, 8, 455, 16, 71
+    query = lambda dim: lib.minikv_paged_prefill_fp8_workspace_bytes(tokens, requests, hq, hkv, dim, blocks, bs,
+                                                                      width, 128, code)
+    assert query(128) == 0
+    assert query(64) >= 2 * requests * width * bs * hkv * 64 * 2 + requests * width * 8
+    assert query(96) > 0
