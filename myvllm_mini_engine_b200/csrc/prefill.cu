@@ -205,15 +205,18 @@ static int run_prefill_fp8_tc(const void* q, const void* key_cache, const void* 
                           (double)k_scale, v_scale);
 }
 
-// FP8 pool, CUDA-core route (shapes the tensor-core route does not take): the
-// split-KV decode with the fp8 consumer, one row per query token.  Same token
-// map, chunking and workspace layout as above; the decode plan is the fp8 pool's.
+// Route 1 applies: head_dim 128 on the tcgen05 kernel's shapes.
 static bool prefill_fp8_in_kernel(int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
                                   int64_t head_dim, int64_t num_blocks, int64_t block_size, int dtype) {
     return head_dim == 128 &&
            prefill_tc_supported(q_heads, kv_heads, head_dim, block_size, dtype, num_blocks, tokens, requests);
 }
 
+// Workspace of the route a batch takes: none (route 1), the copies (route 2),
+// or route 3's token map and decode workspace.  Route 3 runs the split-KV
+// decode with the fp8 consumer, one row per query token, with the token map,
+// chunking and workspace layout of the 16-bit CUDA-core route above; the
+// decode plan is the fp8 pool's.
 static int64_t prefill_fp8_workspace_bytes(int64_t tokens, int64_t requests, int64_t q_heads, int64_t kv_heads,
                                            int64_t head_dim, int64_t num_blocks, int64_t block_size,
                                            int64_t table_width, int dtype, int sms) {
