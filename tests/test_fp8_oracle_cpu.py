@@ -132,3 +132,21 @@ def test_fp8_pool_dtype_decides_the_format():
     with pytest.raises(ValueError, match="contradicts"):
         paged_attention_fp8(torch.zeros(1, 4, 64, dtype=torch.bfloat16), kc, kc, torch.zeros(1, 1, dtype=torch.int64),
                             torch.ones(1, dtype=torch.int64), 16, 0.1, 0.1, kv_format="e4m3")
+
+
+def test_fp16_placements_of_fp8_codes_are_exact():
+    """The bit placements the kernels use to turn codes into fp16 operands, restated in numpy
+    and checked on every finite code against the oracle's decoder: an E5M2 code is the high
+    byte of the fp16 of its value; an E4M3 code shifted down one bit inside the high byte, with
+    its sign moved back to bit 15, is the fp16 of 2^-8 times its value (subnormals included)."""
+    codes = np.arange(256, dtype=np.uint32)
+    e5m2 = (codes << 8).astype(np.uint16).view(np.float16).astype(np.float64)
+    ref5 = fp8_kv.decode_fp8(codes.astype(np.uint8), "e5m2").astype(np.float64)
+    finite5 = np.isfinite(ref5)
+    assert np.array_equal(e5m2[finite5], ref5[finite5])
+    t = (codes << 8) >> 1
+    e4m3 = ((t + (t & 0x4000)) & 0xFFFF).astype(np.uint16).view(np.float16).astype(np.float64)
+    ref4 = fp8_kv.decode_fp8(codes.astype(np.uint8), "e4m3").astype(np.float64)
+    finite4 = np.isfinite(ref4)
+    assert finite4.sum() == 254  # 0x7f and 0xff are NaN
+    assert np.array_equal(e4m3[finite4] * 256.0, ref4[finite4])
